@@ -1,0 +1,45 @@
+/*
+ * kv-compact-accel-cuda.h — the compaction library's accelerator seam on CUDA.
+ *
+ * Same entry points, argument meaning and return convention (0 = done,
+ * -1 = no usable device) as the reference's HIP seam
+ * (fabiantax/kv-compact include/kv-compact-accel.h:22-55), renamed
+ * kv_compact_hip_* -> kv_compact_cuda_*. All pointers are HOST pointers;
+ * each call stages its operands to the current CUDA device (sm_100a) and
+ * copies the result back. The scoring entry points produce the reference's
+ * CPU-path values bit for bit (sequential fp32 dot products, then the scale).
+ *
+ * A build of the reference that defines the HIP seam can link against
+ * libkvc.so by mapping the names.
+ */
+#pragma once
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* 1 when a device that runs the library's sm_100a kernels is present
+ * (reference kv-compact-accel.h:22). */
+int kv_compact_cuda_available(void);
+
+/* C[m x n] = scale * A[m x k] B[n x k]^T (reference kv-compact-accel.h:24-26). */
+int kv_compact_cuda_mat_mul_ABt_scaled(const float * A, const float * B, float * C,
+                                       int m, int n, int k, float scale);
+
+/* scores_out[h][qi*T + ki] = scale * Q_ref[qi, h, :] . K_all[ki, h, :]
+ * for every head (reference kv-compact-accel.h:38-40). */
+int kv_compact_cuda_score_all_heads(const float * Q_ref, const float * K_all, float ** scores_out,
+                                    int n_q, int T, int n_head_kv, int d_k, float scale);
+
+/* Y_out[h] = W_per_head[h] (n_q x T) . V_h (T x d_v), V_h the head-h columns
+ * of V_all [T x n_head_kv*d_v] (reference kv-compact-accel.h:50-52). */
+int kv_compact_cuda_refit_target_all_heads(const float * const * W_per_head, const float * V_all,
+                                           float ** Y_out, int n_q, int T, int n_head_kv, int d_v);
+
+/* Release the device buffers the seam keeps between calls
+ * (reference kv-compact-accel.h:55). */
+void kv_compact_cuda_pool_free(void);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,222 @@
+// batched.cu — whole-model, device-resident compaction (include/kvc-batched.h).
+//
+// All filtered layers are decoded to fp32 once, planned, and handed to the
+// engine as one job list, so every pipeline stage is a single launch over
+// all (layer, chunk) units of the model.
+#include <algorithm>
+#include <vector>
+
+#include "../../include/kvc-batched.h"
+#include "engine.h"
+
+namespace {
+enum { SLOT_BATCH_KV = 3, SLOT_BATCH_IO = 5 };
+
+bool layer_on(const kvc_model_desc * m, const kv_compact_params & p, int l) {
+    if (!p.layer_filter) return true;
+    return p.layer_filter(l, m->n_layers, p.layer_filter_data) != 0;
+}
+
+int check(const kvc_model_desc * m, const kvc_layer_desc * L) {
+    if (!m || !L) return KVC_ERR_NULL;
+    if (m->T <= 0 || m->n_head_kv <= 0 || m->d_k <= 0 || m->d_v <= 0 || m->n_layers <= 0) return KVC_ERR_DIMS;
+    if (kvc_row_elements(m->k_type, m->k_row_bytes) != m->n_head_kv * m->d_k ||
+        kvc_row_elements(m->v_type, m->v_row_bytes) != m->n_head_kv * m->d_v)
+        return KVC_ERR_ROWSIZE;
+    return KVC_OK;
+}
+
+kv_compact_params params_or_default(const kv_compact_params * p) {
+    return p ? *p : kv_compact_params_default();
+}
+}  // namespace
+
+extern "C" {
+
+KVC_EXPORT uint64_t kvc_launch_count(void) {
+    int rc;
+    kvc_ctx * ctx = kvc_get_ctx(&rc);
+    return ctx ? ctx->launches : 0;
+}
+
+KVC_EXPORT int kvc_profile(int enable, double * stage_ms, uint64_t * stage_launches, int n) {
+    int rc;
+    kvc_ctx * ctx = kvc_get_ctx(&rc);
+    if (!ctx) return rc;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    kvc_resolve_timers(ctx);
+    for (int i = 0; i < n && i < KVC_N_STAGES; i++) {
+        if (stage_ms) stage_ms[i] = ctx->stage_ms[i];
+        if (stage_launches) stage_launches[i] = ctx->stage_launches[i];
+    }
+    for (int i = 0; i < KVC_N_STAGES; i++) { ctx->stage_ms[i] = 0.0; ctx->stage_launches[i] = 0; }
+    ctx->profiling = enable;
+    return KVC_N_STAGES;
+}
+
+KVC_EXPORT int kvc_plan_layers(const kvc_model_desc * m, const kvc_layer_desc * L, const kv_compact_params * params,
+                    int * t_out) {
+    int rc = check(m, L);
+    if (rc) return rc;
+    if (!t_out) return KVC_ERR_NULL;
+    kv_compact_params p = params_or_default(params);
+    for (int l = 0; l < m->n_layers; l++) {
+        t_out[l] = 0;
+        if (!layer_on(m, p, l)) continue;
+        const bool qn = p.use_cheap_qref || !L[l].Q_ref;
+        if (!L[l].K || !L[l].V) return KVC_ERR_NULL;
+        kvc_plan pl;
+        if ((rc = kvc_make_plan(m->T, L[l].n_q, qn, m->n_head_kv, m->d_k, m->d_v, p, &pl))) return rc;
+        t_out[l] = pl.t_total;
+    }
+    return KVC_OK;
+}
+
+KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_desc * L, const kv_compact_params * params,
+                           kvc_layer_result * R, int want_stats) {
+    int rc = check(m, L);
+    if (rc) return rc;
+    if (!R) return KVC_ERR_NULL;
+    kv_compact_params p = params_or_default(params);
+    kvc_ctx * ctx = kvc_get_ctx(&rc);
+    if (!ctx) return rc;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaStream_t st = ctx->stream;
+    const int H = m->n_head_kv, dk = m->d_k, dv = m->d_v, T = m->T;
+    const int ek = H * dk, ev = H * dv;
+
+    std::vector<int> on;
+    for (int l = 0; l < m->n_layers; l++) {
+        R[l].t = 0;
+        if (layer_on(m, p, l)) on.push_back(l);
+    }
+    const int n = (int)on.size();
+    if (n == 0) return KVC_OK;
+    std::vector<kvc_plan> plans(n);
+    for (int i = 0; i < n; i++) {
+        const int l = on[i];
+        if (!L[l].K || !L[l].V) return KVC_ERR_NULL;
+        const bool qn = p.use_cheap_qref || !L[l].Q_ref;
+        if ((rc = kvc_make_plan(T, L[l].n_q, qn, H, dk, dv, p, &plans[i]))) return rc;
+    }
+    // fp32 caches of every filtered layer, plus generated cheap queries and R-KV weights
+    const size_t nk = ((size_t)T * ek + 31) & ~31ULL, nv = ((size_t)T * ev + 31) & ~31ULL;
+    void * a;
+    if ((rc = kvc_arena(ctx, SLOT_BATCH_KV, (size_t)n * (nk + nv) * 4, &a))) return rc;
+    float * F = (float *)a;
+    const bool rkv = p.reasoning && p.reasoning->classifier;
+    size_t io = 0;
+    for (int i = 0; i < n; i++) if (plans[i].top_cheap) io += (((size_t)plans[i].nq_top * ek) + 31) & ~31ULL;
+    if (rkv) io += (size_t)T + 32;
+    void * b = nullptr;
+    if ((rc = kvc_arena(ctx, SLOT_BATCH_IO, io * 4 + 256, &b))) return rc;
+    float * io_p = (float *)b;
+    float * dW = nullptr;
+    if (rkv) {
+        std::vector<float> w(T);
+        const kv_compact_reasoning & r = *p.reasoning;
+        for (int j = 0; j < T; j++) {
+            int ty = r.classifier(j + r.token_offset, r.classifier_data);
+            w[j] = ty == KV_TOKEN_THINKING ? r.thinking_weight : (ty == KV_TOKEN_TRANSITION ? r.transition_weight : 1.0f);
+        }
+        dW = io_p;
+        io_p += ((size_t)T + 31) & ~31ULL;
+        KVC_CUDA(cudaMemcpyAsync(dW, w.data(), (size_t)T * 4, cudaMemcpyHostToDevice, st));
+    }
+    std::vector<kvc_layer_job> jobs(n);
+    for (int i = 0; i < n; i++) {
+        const int l = on[i];
+        float * dK = F + (size_t)i * (nk + nv);
+        float * dV = dK + nk;
+        {
+            kvc_stage_timer tm(ctx, KVC_ST_DECODE, 2);
+            if ((rc = kvc_launch_decode((const uint8_t *)L[l].K, m->k_row_bytes, m->k_type, dK, T, ek, st))) return rc;
+            if ((rc = kvc_launch_decode((const uint8_t *)L[l].V, m->v_row_bytes, m->v_type, dV, T, ev, st))) return rc;
+        }
+        kvc_layer_job & J = jobs[i];
+        J.K = dK;
+        J.V = dV;
+        if (plans[i].top_cheap) {
+            float * q = io_p;
+            io_p += (((size_t)plans[i].nq_top * ek) + 31) & ~31ULL;
+            if ((rc = kvc_launch_cheap_q(dK, T, ek, plans[i].nq_top, q, st))) return rc;
+            ctx->launches += 1;
+            J.Q = q;
+        } else {
+            J.Q = L[l].Q_ref;
+        }
+        J.rkv_w = dW;
+        J.plan = &plans[i];
+        if (!R[l].selected_indices || !R[l].beta || !R[l].C_v) return KVC_ERR_NULL;
+        J.out.sel = R[l].selected_indices;
+        J.out.beta = R[l].beta;
+        J.out.cv = R[l].C_v;
+        J.out.t_total = plans[i].t_total;
+    }
+    kvc_phase_ms ph;
+    if ((rc = kvc_engine_run(ctx, p, H, dk, dv, jobs.data(), n, want_stats ? &ph : nullptr))) return rc;
+    for (int i = 0; i < n; i++) {
+        const int l = on[i];
+        const int t = plans[i].t_total;
+        R[l].t = t;
+        if (R[l].K_out) {
+            kvc_stage_timer tm(ctx, KVC_ST_REQUANT, 1);
+            if ((rc = kvc_launch_encode_gather(jobs[i].K, (size_t)ek, R[l].selected_indices, t, ek, m->k_type,
+                                               R[l].K_out, m->k_row_bytes, st)))
+                return rc;
+        }
+        if (R[l].V_out) {
+            kvc_stage_timer tm(ctx, KVC_ST_REQUANT, 1);
+            if ((rc = kvc_launch_encode_heads(R[l].C_v, H, t, dv, m->v_type, R[l].V_out, m->v_row_bytes, st)))
+                return rc;
+        }
+        memset(&R[l].stats, 0, sizeof(R[l].stats));
+        if (want_stats) {
+            if ((rc = kvc_engine_metrics(ctx, jobs[i], H, dk, dv, &R[l].stats))) return rc;
+            R[l].stats.scoring_ms = ph.scoring_ms / n;
+            R[l].stats.nnls_ms = ph.refit_ms / n;
+        }
+    }
+    KVC_CUDA(cudaStreamSynchronize(st));
+    kvc_resolve_timers(ctx);
+    return KVC_OK;
+}
+
+KVC_EXPORT int kvc_quantize_rows_dev(const float * src, size_t src_stride, int type, int rows, int n, uint8_t * dst,
+                                     size_t dst_row_bytes) {
+    if (!src || !dst) return KVC_ERR_NULL;
+    if (rows < 0 || n <= 0) return KVC_ERR_DIMS;
+    if (kvc_row_bytes(type, n) > dst_row_bytes) return KVC_ERR_ROWSIZE;
+    int rc;
+    kvc_ctx * ctx = kvc_get_ctx(&rc);
+    if (!ctx) return rc;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    {
+        kvc_stage_timer tm(ctx, KVC_ST_REQUANT, 1);
+        if ((rc = kvc_launch_encode_gather(src, src_stride, nullptr, rows, n, type, dst, dst_row_bytes, ctx->stream)))
+            return rc;
+    }
+    KVC_CUDA(cudaStreamSynchronize(ctx->stream));
+    kvc_resolve_timers(ctx);
+    return KVC_OK;
+}
+
+KVC_EXPORT int kvc_dequantize_rows_dev(const uint8_t * src, size_t src_row_bytes, int type, int rows, int n,
+                                       float * dst) {
+    if (!src || !dst) return KVC_ERR_NULL;
+    if (rows < 0 || n <= 0) return KVC_ERR_DIMS;
+    if (kvc_row_elements(type, src_row_bytes) < n) return KVC_ERR_ROWSIZE;
+    int rc;
+    kvc_ctx * ctx = kvc_get_ctx(&rc);
+    if (!ctx) return rc;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    {
+        kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1);
+        if ((rc = kvc_launch_decode(src, src_row_bytes, type, dst, rows, n, ctx->stream))) return rc;
+    }
+    KVC_CUDA(cudaStreamSynchronize(ctx->stream));
+    kvc_resolve_timers(ctx);
+    return KVC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,337 @@
+// codec.cu — F32/F16/Q8_0/Q4_0/Q4_1 row codecs, bit-exact with the reference.
+//
+// The reference codecs (include/kv-compact-state.h:326-629) define:
+//   * F16 decode: exact IEEE half -> float (subnormals normalised, NaN payload kept)
+//   * F16 encode: mantissa TRUNCATION (no rounding), exponent < -10 -> +-0,
+//     overflow and NaN -> +-inf
+//   * Q8_0 (34 B / 32 values): d = f16trunc(amax/127), q = (int8)roundf(clamp(x*127/amax))
+//   * Q4_0 (18 B): d = f16trunc(amax/7), q = clamp(roundf(x*7/amax + 8)), nibbles lo|hi<<4
+//   * Q4_1 (20 B): d = f16trunc((max-min)/15), m = f16trunc(min),
+//     q = clamp(roundf((x-min)*15/(max-min)))
+// The block functions below are __host__ __device__ so the host entry points
+// (kv_quantize_row / kv_dequantize_row) and the device kernels share one
+// definition. Every multiply/add is an explicit round-to-nearest operation
+// (kvc_mul/kvc_add), never contracted, because the reference (x86-64 without
+// FMA) rounds after each operation.
+#include "kvc_internal.h"
+
+#include <math.h>
+
+#define QK 32
+
+KVC_HD float kvc_h2f(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1Fu;
+    uint32_t m = h & 0x3FFu;
+    uint32_t bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else {
+            int ee = 1;
+            while (!(m & 0x400u)) { m <<= 1; ee--; }
+            m &= 0x3FFu;
+            bits = sign | ((uint32_t)(ee + 112) << 23) | (m << 13);
+        }
+    } else if (e == 31) {
+        bits = sign | 0x7F800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 112u) << 23) | (m << 13);
+    }
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(bits);
+#else
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+#endif
+}
+
+KVC_HD uint16_t kvc_f2h_trunc(float v) {
+#ifdef __CUDA_ARCH__
+    uint32_t f = __float_as_uint(v);
+#else
+    uint32_t f;
+    memcpy(&f, &v, 4);
+#endif
+    uint32_t sign = (f >> 16) & 0x8000u;
+    int e = (int)((f >> 23) & 0xFFu) - 112;
+    uint32_t m = (f >> 13) & 0x3FFu;
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        return (uint16_t)(sign | ((m | 0x400u) >> (1 - e)));
+    }
+    if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+    return (uint16_t)(sign | ((uint32_t)e << 10) | m);
+}
+
+// max(lo, min(hi, v)) in std::min/std::max operand order (NaN -> hi).
+KVC_HD float kvc_clamp(float v, float lo, float hi) {
+    float m = (v < hi) ? v : hi;
+    return (lo < m) ? m : lo;
+}
+
+KVC_HD float kvc_roundf(float x) { return roundf(x); }
+
+int kvc_block_bytes(int type) {
+    switch (type) {
+    case 0: return 4;
+    case 1: return 2;
+    case 8: return 34;
+    case 2: return 18;
+    case 3: return 20;
+    default: return 4;
+    }
+}
+
+static bool is_block(int type) { return type == 8 || type == 2 || type == 3; }
+
+int kvc_row_elements(int type, size_t row_bytes) {
+    if (type == 0) return (int)(row_bytes / 4);
+    if (type == 1) return (int)(row_bytes / 2);
+    if (is_block(type)) return (int)(row_bytes / (size_t)kvc_block_bytes(type)) * QK;
+    return (int)(row_bytes / 4);
+}
+
+size_t kvc_row_bytes(int type, int n) {
+    if (type == 0) return (size_t)n * 4;
+    if (type == 1) return (size_t)n * 2;
+    if (is_block(type)) return (size_t)(n / QK) * (size_t)kvc_block_bytes(type);
+    return (size_t)n * 4;
+}
+
+// ---- one 32-value block ---------------------------------------------------
+KVC_HD uint16_t ld16(const uint8_t * p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+KVC_HD void st16(uint8_t * p, uint16_t v) { p[0] = (uint8_t)(v & 0xFF); p[1] = (uint8_t)(v >> 8); }
+
+KVC_HD void decode_block(const uint8_t * b, int type, float * o) {
+    float d = kvc_h2f(ld16(b));
+    if (type == 8) {
+        for (int i = 0; i < QK; i++) o[i] = kvc_mul(d, (float)(int8_t)b[2 + i]);
+    } else if (type == 2) {
+        for (int i = 0; i < QK / 2; i++) {
+            uint8_t q = b[2 + i];
+            o[2 * i] = kvc_mul(d, kvc_sub((float)(q & 0xF), 8.0f));
+            o[2 * i + 1] = kvc_mul(d, kvc_sub((float)(q >> 4), 8.0f));
+        }
+    } else {
+        float m = kvc_h2f(ld16(b + 2));
+        for (int i = 0; i < QK / 2; i++) {
+            uint8_t q = b[4 + i];
+            o[2 * i] = kvc_add(kvc_mul(d, (float)(q & 0xF)), m);
+            o[2 * i + 1] = kvc_add(kvc_mul(d, (float)(q >> 4)), m);
+        }
+    }
+}
+
+KVC_HD void encode_block(const float * x, int type, uint8_t * o) {
+    if (type == 8 || type == 2) {
+        float amax = 0.0f;
+        for (int i = 0; i < QK; i++) { float a = fabsf(x[i]); if (a > amax) amax = a; }
+        float lim = (type == 8) ? 127.0f : 7.0f;
+        float d = kvc_div(amax, lim);
+        st16(o, kvc_f2h_trunc(d));
+        float id = (d != 0.0f) ? kvc_div(lim, amax) : 0.0f;
+        if (type == 8) {
+            for (int i = 0; i < QK; i++)
+                o[2 + i] = (uint8_t)(int8_t)kvc_roundf(kvc_clamp(kvc_mul(x[i], id), -128.0f, 127.0f));
+        } else {
+            for (int i = 0; i < QK / 2; i++) {
+                float v0 = kvc_add(kvc_mul(x[2 * i], id), 8.0f);
+                float v1 = kvc_add(kvc_mul(x[2 * i + 1], id), 8.0f);
+                uint8_t q0 = (uint8_t)kvc_clamp(kvc_roundf(v0), 0.0f, 15.0f);
+                uint8_t q1 = (uint8_t)kvc_clamp(kvc_roundf(v1), 0.0f, 15.0f);
+                o[2 + i] = (uint8_t)(q0 | (q1 << 4));
+            }
+        }
+    } else {
+        float lo = x[0], hi = x[0];
+        for (int i = 1; i < QK; i++) { if (x[i] < lo) lo = x[i]; if (x[i] > hi) hi = x[i]; }
+        float rng = kvc_sub(hi, lo);
+        float d = kvc_div(rng, 15.0f);
+        st16(o, kvc_f2h_trunc(d));
+        st16(o + 2, kvc_f2h_trunc(lo));
+        float id = (d != 0.0f) ? kvc_div(15.0f, rng) : 0.0f;
+        for (int i = 0; i < QK / 2; i++) {
+            float v0 = kvc_mul(kvc_sub(x[2 * i], lo), id);
+            float v1 = kvc_mul(kvc_sub(x[2 * i + 1], lo), id);
+            uint8_t q0 = (uint8_t)kvc_clamp(kvc_roundf(v0), 0.0f, 15.0f);
+            uint8_t q1 = (uint8_t)kvc_clamp(kvc_roundf(v1), 0.0f, 15.0f);
+            o[4 + i] = (uint8_t)(q0 | (q1 << 4));
+        }
+    }
+}
+
+// ---- host rows -------------------------------------------------------------
+void kvc_host_decode_row(const uint8_t * src, int type, float * dst, size_t n) {
+    if (type == 0) { memcpy(dst, src, n * 4); return; }
+    if (type == 1) {
+        for (size_t i = 0; i < n; i++) dst[i] = kvc_h2f(ld16(src + 2 * i));
+        return;
+    }
+    if (!is_block(type)) { memset(dst, 0, n * 4); return; }
+    size_t nb = n / QK, bb = (size_t)kvc_block_bytes(type);
+    for (size_t b = 0; b < nb; b++) decode_block(src + b * bb, type, dst + b * QK);
+}
+
+size_t kvc_host_encode_row(const float * src, int type, uint8_t * dst, int n) {
+    if (type == 0) { memcpy(dst, src, (size_t)n * 4); return (size_t)n * 4; }
+    if (type == 1) {
+        for (int i = 0; i < n; i++) st16(dst + 2 * i, kvc_f2h_trunc(src[i]));
+        return (size_t)n * 2;
+    }
+    if (!is_block(type)) return 0;
+    int nb = n / QK, bb = kvc_block_bytes(type);
+    for (int b = 0; b < nb; b++) encode_block(src + b * QK, type, dst + (size_t)b * bb);
+    return (size_t)nb * (size_t)bb;
+}
+
+// ---- device kernels --------------------------------------------------------
+// Decode `rows` rows of n values. One thread per 32-value block (or per
+// element for F16/F32); consecutive threads touch consecutive bytes, and each
+// thread writes its 32 floats as 8 float4 stores.
+__global__ void k_decode_blocks(const uint8_t * __restrict__ src, size_t rb, int type,
+                                float * __restrict__ dst, int rows, int n) {
+    int nb = n / QK;
+    long long total = (long long)rows * nb;
+    int bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        long long r = i / nb;
+        int b = (int)(i - r * nb);
+        const uint8_t * p = src + r * rb + (size_t)b * bb;
+        uint8_t raw[34];
+        for (int k = 0; k < bb; k++) raw[k] = __ldg(p + k);
+        float o[QK];
+        decode_block(raw, type, o);
+        float * q = dst + r * (long long)n + (long long)b * QK;
+        if ((((uintptr_t)q) & 15) == 0) {
+            for (int k = 0; k < QK; k += 4)
+                *reinterpret_cast<float4 *>(q + k) = make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
+        } else {
+            for (int k = 0; k < QK; k++) q[k] = o[k];
+        }
+    }
+}
+
+__global__ void k_decode_elems(const uint8_t * __restrict__ src, size_t rb, int type,
+                               float * __restrict__ dst, int rows, int n) {
+    long long total = (long long)rows * n;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        long long r = i / n;
+        int e = (int)(i - r * n);
+        const uint8_t * p = src + r * rb;
+        if (type == 1) {
+            dst[i] = kvc_h2f(ld16(p + 2 * e));
+        } else if (type == 0) {
+            float v;
+            memcpy(&v, p + 4 * e, 4);
+            dst[i] = v;
+        } else {
+            dst[i] = 0.0f;
+        }
+    }
+}
+
+static int grid_for(long long work, int threads) {
+    long long g = (work + threads - 1) / threads;
+    if (g > 148LL * 64) g = 148LL * 64;
+    if (g < 1) g = 1;
+    return (int)g;
+}
+
+int kvc_launch_decode(const uint8_t * src, size_t rb, int type, float * dst, int rows, int n,
+                      cudaStream_t st) {
+    if (rows <= 0 || n <= 0) return KVC_OK;
+    if (is_block(type)) {
+        long long work = (long long)rows * (n / QK);
+        k_decode_blocks<<<grid_for(work, 256), 256, 0, st>>>(src, rb, type, dst, rows, n);
+    } else {
+        long long work = (long long)rows * n;
+        k_decode_elems<<<grid_for(work, 256), 256, 0, st>>>(src, rb, type, dst, rows, n);
+    }
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+__device__ __forceinline__ bool dev_is_block(int type) { return type == 8 || type == 2 || type == 3; }
+
+// K_out rows: row j = src[rows_idx[j]] (fp32, stride src_stride) re-encoded.
+__global__ void k_encode_gather(const float * __restrict__ src, size_t stride,
+                                const int * __restrict__ idx, int rows, int n, int type,
+                                uint8_t * __restrict__ dst, size_t drb) {
+    bool blk = dev_is_block(type);
+    int per_row = blk ? n / QK : n;
+    long long total = (long long)rows * per_row;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        long long r = i / per_row;
+        int b = (int)(i - r * per_row);
+        const float * row = src + (idx ? (long long)idx[r] : r) * (long long)stride;
+        uint8_t * o = dst + r * drb;
+        if (blk) {
+            float x[QK];
+            for (int k = 0; k < QK; k++) x[k] = row[b * QK + k];
+            uint8_t tmp[34];
+            encode_block(x, type, tmp);
+            int bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
+            for (int k = 0; k < bb; k++) o[(size_t)b * bb + k] = tmp[k];
+        } else if (type == 1) {
+            st16(o + 2 * b, kvc_f2h_trunc(row[b]));
+        } else {
+            float v = row[b];
+            memcpy(o + 4 * b, &v, 4);
+        }
+    }
+}
+
+// V_out rows: row j, element e = h*dv + k comes from cv[h][j][k].
+__global__ void k_encode_heads(const float * __restrict__ cv, int H, int t, int dv, int type,
+                               uint8_t * __restrict__ dst, size_t drb) {
+    int n = H * dv;
+    bool blk = dev_is_block(type);
+    int per_row = blk ? n / QK : n;
+    long long total = (long long)t * per_row;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        long long j = i / per_row;
+        int b = (int)(i - j * per_row);
+        uint8_t * o = dst + j * drb;
+        if (blk) {
+            float x[QK];
+            for (int k = 0; k < QK; k++) {
+                int e = b * QK + k;
+                int h = e / dv, c = e - h * dv;
+                x[k] = cv[((long long)h * t + j) * dv + c];
+            }
+            uint8_t tmp[34];
+            encode_block(x, type, tmp);
+            int bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
+            for (int k = 0; k < bb; k++) o[(size_t)b * bb + k] = tmp[k];
+        } else {
+            int h = b / dv, c = b - h * dv;
+            float v = cv[((long long)h * t + j) * dv + c];
+            if (type == 1) st16(o + 2 * b, kvc_f2h_trunc(v));
+            else memcpy(o + 4 * b, &v, 4);
+        }
+    }
+}
+
+int kvc_launch_encode_gather(const float * src, size_t stride, const int * idx, int rows, int n,
+                             int type, uint8_t * dst, size_t drb, cudaStream_t st) {
+    if (rows <= 0) return KVC_OK;
+    long long work = (long long)rows * (is_block(type) ? n / QK : n);
+    k_encode_gather<<<grid_for(work, 128), 128, 0, st>>>(src, stride, idx, rows, n, type, dst, drb);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+int kvc_launch_encode_heads(const float * cv, int H, int t, int dv, int type, uint8_t * dst,
+                            size_t drb, cudaStream_t st) {
+    if (t <= 0) return KVC_OK;
+    long long work = (long long)t * (is_block(type) ? (H * dv) / QK : H * dv);
+    k_encode_heads<<<grid_for(work, 128), 128, 0, st>>>(cv, H, t, dv, type, dst, drb);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}

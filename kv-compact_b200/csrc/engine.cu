@@ -1,0 +1,484 @@
+// engine.cu — planning, per-device context and the stage pipeline.
+//
+// Pipeline over a flat list of units (one per (layer, chunk), all heads):
+//   scoring phase:  k_score -> k_softmax_importance -> k_aggregate -> k_select
+//   refit phase:    k_pv (Y) -> beta (NNLS, optional) -> k_score gather (S[:,sel])
+//                   -> k_softmax_x (X) -> k_gram + k_chol_solve (C_v)
+//                   -> refinement rounds (optional)
+// Every stage is one launch over all units of the batch, so a whole model
+// (all filtered layers) is a handful of launches that fill the 148 SMs.
+#include "engine.h"
+
+#include <math.h>
+#include <stdlib.h>
+
+#include <algorithm>
+
+// ---------------------------------------------------------------------------
+// planning (host)
+// ---------------------------------------------------------------------------
+static int cheap_nq(int T) {                 // src/kv-compact-api.cpp:384-387
+    int n = T / 2;
+    if (n > 64) n = 64;
+    if (n < 4) n = 4;
+    if (n > T) n = T;
+    return n;
+}
+
+static int size_t_for(int T, const kv_compact_params & p) {   // :396-409
+    int t;
+    if (p.target_count > 0) {
+        t = p.target_count < T ? p.target_count : T;
+    } else {
+        t = (int)((float)T * p.target_ratio);
+        if (t < 1) t = 1;
+        if (t > T) t = T;
+    }
+    if (p.n_shared_prefix > t) t = p.n_shared_prefix < T ? p.n_shared_prefix : T;
+    return t;
+}
+
+static int clamp_prefix(int prefix, int t) {
+    if (prefix <= 0) return 0;
+    return prefix < t ? prefix : t;
+}
+
+int kvc_make_plan(int T, int n_q, bool q_null, int H, int dk, int dv, const kv_compact_params & p,
+                  kvc_plan * out) {
+    if (T <= 0 || H <= 0 || dk <= 0 || dv <= 0) return KVC_ERR_DIMS;
+    kvc_plan pl;
+    pl.T = T;
+    if (p.use_cheap_qref || q_null) {
+        pl.top_cheap = true;
+        pl.nq_top = cheap_nq(T);
+    } else {
+        if (n_q <= 0) return KVC_ERR_DIMS;
+        pl.nq_top = n_q;
+    }
+    const int t_top = size_t_for(T, p);
+
+    int cs = p.chunk_size;                   // :417-437
+    if (cs == 0) {
+        float re = (p.target_count > 0) ? (float)p.target_count / (float)T : p.target_ratio;
+        if (re <= 0.0f) re = 0.5f;
+        if (re > 1.0f) re = 1.0f;
+        int et = (int)((float)T * re);
+        if (et > 256) {
+            cs = (int)(256.0f / re);
+            if (cs < 64) cs = 64;
+            if (cs >= T) cs = T;
+        } else {
+            cs = T;
+        }
+    } else if (cs < 0) {
+        cs = T;
+    }
+    pl.chunk = cs;
+
+    if (cs >= T) {
+        kvc_plan_unit u;
+        u.start = 0;
+        u.C = T;
+        u.t = t_top;
+        u.prefix = clamp_prefix(p.n_shared_prefix, t_top);
+        u.nq = pl.nq_top;
+        u.qmode = 0;
+        pl.units.push_back(u);
+        pl.t_total = t_top;
+    } else {
+        int nc = (T + cs - 1) / cs;
+        pl.t_total = 0;
+        for (int c = 0; c < nc; c++) {
+            kvc_plan_unit u;
+            u.start = c * cs;
+            int end = u.start + cs;
+            if (end > T) end = T;
+            u.C = end - u.start;
+            kv_compact_params cp = p;
+            cp.chunk_size = -1;
+            if (c > 0) cp.n_shared_prefix = 0;
+            if (cp.n_shared_prefix > u.C) cp.n_shared_prefix = u.C;
+            if (p.use_cheap_qref) {
+                u.qmode = 1;
+                u.nq = cheap_nq(u.C);
+            } else {
+                u.qmode = 0;
+                u.nq = pl.nq_top;
+            }
+            u.t = size_t_for(u.C, cp);
+            u.prefix = clamp_prefix(cp.n_shared_prefix, u.t);
+            pl.units.push_back(u);
+            pl.t_total += u.t;
+        }
+    }
+    *out = std::move(pl);
+    return KVC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// context and arenas
+// ---------------------------------------------------------------------------
+static std::mutex g_ctx_mu;
+static kvc_ctx * g_ctx[64];
+
+kvc_ctx * kvc_get_ctx(int * rc) {
+    int dev = -1, n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        if (rc) *rc = KVC_ERR_NODEV;
+        return nullptr;
+    }
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        if (rc) *rc = KVC_ERR_NODEV;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_ctx_mu);
+    if (!g_ctx[dev]) {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major < 10) {
+            fprintf(stderr, "[kvc] device %d (sm_%d%d) cannot run sm_100a kernels\n", dev, prop.major, prop.minor);
+            if (rc) *rc = KVC_ERR_NODEV;
+            return nullptr;
+        }
+        kvc_ctx * c = new kvc_ctx();
+        c->device = dev;
+        if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+            delete c;
+            if (rc) *rc = KVC_ERR_CUDA;
+            return nullptr;
+        }
+        for (auto & e : c->ev) cudaEventCreate(&e);
+        g_ctx[dev] = c;
+    }
+    if (rc) *rc = KVC_OK;
+    return g_ctx[dev];
+}
+
+int kvc_arena(kvc_ctx * ctx, int slot, size_t bytes, void ** out) {
+    if (bytes == 0) bytes = 256;
+    if (ctx->arena_cap[slot] < bytes) {
+        if (ctx->arena[slot]) {
+            KVC_CUDA(cudaStreamSynchronize(ctx->stream));
+            cudaFree(ctx->arena[slot]);
+            ctx->arena[slot] = nullptr;
+            ctx->arena_cap[slot] = 0;
+        }
+        size_t cap = bytes + bytes / 8;
+        KVC_CUDA(cudaMalloc(&ctx->arena[slot], cap));
+        ctx->arena_cap[slot] = cap;
+    }
+    *out = ctx->arena[slot];
+    return KVC_OK;
+}
+
+static cudaEvent_t next_event(kvc_ctx * ctx, int * idx) {
+    if (ctx->ev_used == ctx->ev_pool.size()) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        ctx->ev_pool.push_back(e);
+    }
+    *idx = (int)ctx->ev_used;
+    return ctx->ev_pool[ctx->ev_used++];
+}
+
+kvc_stage_timer::kvc_stage_timer(kvc_ctx * c, int s, int n_launch) : ctx(c), stage(s) {
+    ctx->launches += (uint64_t)n_launch;
+    ctx->stage_launches[s] += (uint64_t)n_launch;
+    if (!ctx->profiling) return;
+    cudaEventRecord(next_event(ctx, &first), ctx->stream);
+}
+
+kvc_stage_timer::~kvc_stage_timer() {
+    if (first < 0) return;
+    int second;
+    cudaEventRecord(next_event(ctx, &second), ctx->stream);
+    ctx->pending.push_back({stage, first});
+}
+
+void kvc_resolve_timers(kvc_ctx * ctx) {
+    if (ctx->pending.empty()) { ctx->ev_used = 0; return; }
+    cudaEventSynchronize(ctx->ev_pool[ctx->ev_used - 1]);
+    for (auto & pr : ctx->pending) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, ctx->ev_pool[pr.second], ctx->ev_pool[pr.second + 1]);
+        ctx->stage_ms[pr.first] += ms;
+    }
+    ctx->pending.clear();
+    ctx->ev_used = 0;
+}
+
+// ---------------------------------------------------------------------------
+// small utility kernels
+// ---------------------------------------------------------------------------
+__global__ void k_gather_rows(const float * __restrict__ src, int ss, const int * __restrict__ idx, int rows,
+                              int n, float * __restrict__ dst, int ds) {
+    long long total = (long long)rows * n;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        long long r = i / n;
+        int c = (int)(i - r * n);
+        dst[r * ds + c] = src[(long long)idx[r] * ss + c];
+    }
+}
+
+int kvc_launch_gather_rows(const float * src, int ss, const int * idx, int rows, int n, float * dst, int ds,
+                           cudaStream_t st) {
+    if (rows <= 0 || n <= 0) return KVC_OK;
+    long long work = (long long)rows * n;
+    int g = (int)std::min<long long>((work + 255) / 256, 148LL * 32);
+    k_gather_rows<<<g, 256, 0, st>>>(src, ss, idx, rows, n, dst, ds);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+// Cheap reference queries: rows of K at floor(((i+1)/(n+1))^2 (T-1))
+// (src/kv-compact-api.cpp:132-152).
+__global__ void k_cheap_q(const float * __restrict__ K, int T, int ek, int nq, float * __restrict__ Q) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)nq * ek;
+         i += (long long)gridDim.x * blockDim.x) {
+        int qi = (int)(i / ek), c = (int)(i % ek);
+        float fr = __fdiv_rn((float)(qi + 1), (float)(nq + 1));
+        fr = __fmul_rn(fr, fr);
+        int pos = (int)__fmul_rn(fr, (float)(T - 1));
+        if (pos >= T) pos = T - 1;
+        if (pos < 0) pos = 0;
+        Q[i] = K[(long long)pos * ek + c];
+    }
+}
+
+int kvc_launch_cheap_q(const float * K, int T, int ek, int nq, float * Q, cudaStream_t st) {
+    long long work = (long long)nq * ek;
+    int g = (int)std::min<long long>((work + 255) / 256, 148LL * 8);
+    k_cheap_q<<<g, 256, 0, st>>>(K, T, ek, nq, Q);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// pipeline
+// ---------------------------------------------------------------------------
+static inline long long al32(long long x) { return (x + 31) & ~31LL; }
+
+struct unit_sizes {
+    long long fs, is, gs;
+};
+
+static unit_sizes sizes_of(const kvc_plan_unit & u, int H, int dv) {
+    unit_sizes s;
+    const int n = std::min(u.nq, u.t);
+    s.fs = al32((long long)H * u.nq * u.C) + al32((long long)(2 * H + 1) * u.C) + al32((long long)2 * H * u.nq) +
+           al32((long long)H * u.nq * dv) + al32((long long)H * u.nq * u.t);
+    s.is = al32(u.t) + al32(4LL * u.C);
+    s.gs = al32((long long)H * n * n);
+    return s;
+}
+
+int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, int dv,
+                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase) {
+    if (n_jobs <= 0) return KVC_OK;
+    cudaStream_t st = ctx->stream;
+    if (p.use_sensitivity && H > 64) return KVC_ERR_SHAPE;
+    if (dk > KVC_MAX_D || dv > KVC_MAX_D) return KVC_ERR_SHAPE;
+    if (!p.skip_beta || p.refine_rounds > 0 || p.use_omp) {
+        // beta / refinement / OMP stages are dispatched below
+    }
+
+    kvc_params_dev P;
+    P.H = H; P.dk = dk; P.dv = dv;
+    P.score_method = p.score_method;
+    P.skip_beta = p.skip_beta;
+    P.use_sensitivity = p.use_sensitivity;
+    P.use_diversity = p.use_diversity;
+    P.diversity_strength = p.diversity_strength;
+    P.nnls_method = p.nnls_method;
+    P.nnls_max_iter = p.nnls_max_iter;
+    P.nnls_pgd_iters = p.nnls_pgd_iters;
+    P.ridge = p.ridge;
+    P.isd = 1.0f / sqrtf((float)dk);
+
+    // ---- layer outputs table
+    if (ctx->outs_cap < (size_t)n_jobs) {
+        if (ctx->d_outs) cudaFree(ctx->d_outs);
+        ctx->outs_cap = (size_t)n_jobs * 2;
+        KVC_CUDA(cudaMalloc(&ctx->d_outs, ctx->outs_cap * sizeof(kvc_layer_out)));
+    }
+    std::vector<kvc_layer_out> outs(n_jobs);
+    for (int l = 0; l < n_jobs; l++) outs[l] = jobs[l].out;
+    KVC_CUDA(cudaMemcpyAsync(ctx->d_outs, outs.data(), n_jobs * sizeof(kvc_layer_out), cudaMemcpyHostToDevice, st));
+    for (int l = 0; l < n_jobs; l++)
+        if (outs[l].t_total > 0)
+            KVC_CUDA(cudaMemsetAsync(outs[l].beta, 0, (size_t)H * outs[l].t_total * sizeof(float), st));
+
+    // ---- flat unit list, split into batches that fit the scratch budget
+    struct ref { int l, i; };
+    std::vector<ref> all;
+    for (int l = 0; l < n_jobs; l++)
+        for (int i = 0; i < (int)jobs[l].plan->units.size(); i++) all.push_back({l, i});
+
+    size_t free_b = 0, total_b = 0;
+    cudaMemGetInfo(&free_b, &total_b);
+    long long budget = (long long)std::min<size_t>((size_t)(free_b * 0.6), (size_t)48 << 30);
+    // bytes already held by our arenas can be reused
+    budget += (long long)(ctx->arena_cap[0] + ctx->arena_cap[1] + ctx->arena_cap[2]);
+
+    if (phase) KVC_CUDA(cudaEventRecord(ctx->ev[0], st));
+    double score_ms = 0, refit_ms = 0;
+
+    size_t pos = 0;
+    while (pos < all.size()) {
+        // gather a batch
+        std::vector<kvc_unit> U;
+        long long fs = 0, is = 0, gs = 0;
+        int max_nq = 1, max_C = 1, max_t = 1, max_n = 1;
+        size_t lsq_smem = 0;
+        // R-KV weights live at the front of the float arena, per layer
+        std::vector<long long> w_base(n_jobs, -1);
+        for (int l = 0; l < n_jobs; l++)
+            if (jobs[l].rkv_w) { w_base[l] = fs; fs += al32(jobs[l].plan->T); }
+        size_t first = pos;
+        while (pos < all.size()) {
+            const kvc_plan_unit & pu = jobs[all[pos].l].plan->units[all[pos].i];
+            unit_sizes s = sizes_of(pu, H, dv);
+            long long bytes = (fs + s.fs) * 4 + (is + s.is) * 4 + (gs + s.gs) * 8;
+            if (pos > first && bytes > budget) break;
+            const kvc_layer_job & J = jobs[all[pos].l];
+            const int ek = H * dk, ev = H * dv;
+            kvc_unit u;
+            memset(&u, 0, sizeof(u));
+            u.K = J.K + (long long)pu.start * ek;
+            u.V = J.V + (long long)pu.start * ev;
+            u.Q = J.Q;
+            u.C = pu.C; u.t = pu.t; u.prefix = pu.prefix; u.nq = pu.nq; u.qmode = pu.qmode;
+            u.layer = all[pos].l;
+            int off = 0;
+            for (int k = 0; k < all[pos].i; k++) off += J.plan->units[k].t;
+            u.out_off = off;
+            u.token_base = pu.start;
+            u.active = 1;
+            u.s_off = fs; fs += al32((long long)H * pu.nq * pu.C);
+            u.imp_off = fs; fs += al32((long long)(2 * H + 1) * pu.C);
+            u.row_off = fs; fs += al32((long long)2 * H * pu.nq);
+            u.y_off = fs; fs += al32((long long)H * pu.nq * dv);
+            u.x_off = fs; fs += al32((long long)H * pu.nq * pu.t);
+            u.w_off = w_base[u.layer] >= 0 ? w_base[u.layer] + pu.start : -1;
+            u.sel_off = is; is += al32(pu.t);
+            u.c_off = is; is += al32(4LL * pu.C);
+            const int n = std::min(pu.nq, pu.t);
+            if (n > 3072) return KVC_ERR_SHAPE;
+            u.g_off = gs; gs += al32((long long)H * n * n);
+            max_nq = std::max(max_nq, pu.nq);
+            max_C = std::max(max_C, pu.C);
+            max_t = std::max(max_t, pu.t);
+            max_n = std::max(max_n, n);
+            lsq_smem = std::max(lsq_smem, kvc_lsq_smem_bytes(n));
+            U.push_back(u);
+            pos++;
+        }
+        void * a0; void * a1; void * a2;
+        int rc;
+        if ((rc = kvc_arena(ctx, 0, (size_t)fs * 4, &a0))) return rc;
+        if ((rc = kvc_arena(ctx, 1, (size_t)is * 4, &a1))) return rc;
+        if ((rc = kvc_arena(ctx, 2, (size_t)gs * 8, &a2))) return rc;
+        float * F = (float *)a0;
+        int * I = (int *)a1;
+        double * G = (double *)a2;
+        for (int l = 0; l < n_jobs; l++)
+            if (w_base[l] >= 0)
+                KVC_CUDA(cudaMemcpyAsync(F + w_base[l], jobs[l].rkv_w, (size_t)jobs[l].plan->T * 4,
+                                         cudaMemcpyDeviceToDevice, st));
+        if (ctx->units_cap < U.size()) {
+            if (ctx->d_units) { KVC_CUDA(cudaStreamSynchronize(st)); cudaFree(ctx->d_units); }
+            ctx->units_cap = U.size() * 2;
+            KVC_CUDA(cudaMalloc(&ctx->d_units, ctx->units_cap * sizeof(kvc_unit)));
+        }
+        KVC_CUDA(cudaMemcpyAsync(ctx->d_units, U.data(), U.size() * sizeof(kvc_unit), cudaMemcpyHostToDevice, st));
+        const int nu = (int)U.size();
+        const kvc_unit * du = ctx->d_units;
+
+        if (phase) KVC_CUDA(cudaEventRecord(ctx->ev[1], st));
+        {
+            kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1);
+            if ((rc = kvc_launch_score(du, nu, max_nq, max_C, P, F, I, 0, st))) return rc;
+        }
+        {
+            kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1);
+            if ((rc = kvc_launch_softmax_importance(du, nu, P, F, st))) return rc;
+        }
+        {
+            kvc_stage_timer tm(ctx, KVC_ST_SELECT, 2);
+            if ((rc = kvc_launch_aggregate(du, nu, P, F, st))) return rc;
+            if ((rc = kvc_launch_select(du, nu, max_C, P, F, I, ctx->d_outs, st))) return rc;
+        }
+        if (phase) KVC_CUDA(cudaEventRecord(ctx->ev[2], st));
+        {
+            kvc_stage_timer tm(ctx, KVC_ST_PV, 1);
+            if ((rc = kvc_launch_pv(du, nu, max_nq, P, F, st))) return rc;
+        }
+        for (int r = 0; r <= p.refine_rounds; r++) {
+            if (r > 0) {
+                kvc_stage_timer tm(ctx, KVC_ST_REFINE, 1);
+                if ((rc = kvc_launch_refine(du, nu, P, F, I, ctx->d_outs, st))) return rc;
+            }
+            if (!p.skip_beta) {
+                kvc_stage_timer tm(ctx, KVC_ST_BETA, 1);
+                if ((rc = kvc_launch_beta(du, nu, max_nq, max_t, P, F, I, G, ctx->d_outs, st))) return rc;
+            }
+            {
+                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 2);
+                if ((rc = kvc_launch_score(du, nu, max_nq, max_t, P, F, I, 1, st))) return rc;
+                if ((rc = kvc_launch_softmax_x(du, nu, max_nq, P, F, ctx->d_outs, st))) return rc;
+            }
+            {
+                kvc_stage_timer tm(ctx, KVC_ST_LSQ, 2);
+                if ((rc = kvc_launch_lsq(du, nu, max_n, lsq_smem, P, F, G, ctx->d_outs, st))) return rc;
+            }
+        }
+        if (phase) {
+            KVC_CUDA(cudaEventRecord(ctx->ev[3], st));
+            KVC_CUDA(cudaEventSynchronize(ctx->ev[3]));
+            float a = 0, b = 0;
+            cudaEventElapsedTime(&a, ctx->ev[1], ctx->ev[2]);
+            cudaEventElapsedTime(&b, ctx->ev[2], ctx->ev[3]);
+            score_ms += a;
+            refit_ms += b;
+        }
+    }
+    if (phase) {
+        phase->scoring_ms = score_ms;
+        phase->refit_ms = refit_ms;
+    }
+    return KVC_OK;
+}
+
+int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, int dv, kv_compact_stats * st) {
+    const kvc_plan & pl = *job.plan;
+    const int pairs = kvc_metric_pairs(H, pl.nq_top);
+    const int t = job.out.t_total;
+    const long long per = std::max(pl.T, t);
+    void * a4;
+    int rc;
+    if ((rc = kvc_arena(ctx, 4, (size_t)(pairs * per + pairs * 3 + 32) * 4, &a4))) return rc;
+    float * scratch = (float *)a4;
+    float * res = scratch + pairs * per;
+    float isd = 1.0f / sqrtf((float)dk);
+    {
+        kvc_stage_timer tm(ctx, KVC_ST_METRICS, 1);
+        if ((rc = kvc_launch_metrics(job.K, job.V, job.Q, pl.T, pl.nq_top, H, dk, dv, job.out.sel, job.out.beta,
+                                     job.out.cv, t, isd, scratch, res, ctx->stream)))
+            return rc;
+    }
+    std::vector<float> h(pairs * 3);
+    KVC_CUDA(cudaMemcpyAsync(h.data(), res, pairs * 3 * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    KVC_CUDA(cudaStreamSynchronize(ctx->stream));
+    float sc = 0.0f, sm = 0.0f;
+    int agree = 0;
+    for (int i = 0; i < pairs; i++) {
+        sc += h[i * 3 + 0];
+        sm += h[i * 3 + 1];
+        agree += h[i * 3 + 2] > 0.5f ? 1 : 0;
+    }
+    st->avg_cosine_sim = sc / (float)pairs;
+    st->avg_mse = sm / (float)pairs;
+    st->avg_agreement = (float)agree / (float)pairs;
+    return KVC_OK;
+}

@@ -1,0 +1,135 @@
+// engine.h — host-side planning and the device pipeline over (layer, chunk) units.
+#pragma once
+
+#include <mutex>
+#include <vector>
+
+#include "../../include/kv-compact-api.h"
+#include "kvc_internal.h"
+
+#define KVC_N_STAGES 11
+
+// One chunk of one layer as the reference's kv_compact would process it.
+struct kvc_plan_unit {
+    int start;    // first token
+    int C;        // tokens
+    int t;        // kept keys
+    int prefix;   // forced leading keys (<= t)
+    int nq;       // reference queries used by this chunk
+    int qmode;    // 0: top-level queries, 1: cheap queries from this chunk's keys
+};
+
+struct kvc_plan {
+    int T = 0;
+    int nq_top = 0;        // n_q_used of the top-level call
+    bool top_cheap = false;// top-level queries are sampled from the full K
+    int chunk = 0;         // effective chunk size (T when unchunked)
+    int t_total = 0;
+    std::vector<kvc_plan_unit> units;
+};
+
+// Mirrors src/kv-compact-api.cpp:369-437 and the per-chunk sub-call sizing
+// (:466-498 + :382-409). Returns 0 or a negative reference error code.
+int kvc_make_plan(int T, int n_q, bool q_null, int H, int dk, int dv, const kv_compact_params & p,
+                  kvc_plan * out);
+
+// Device-side job for one layer: fp32 caches resident on the device.
+struct kvc_layer_job {
+    const float * K = nullptr;      // [T x H*dk]
+    const float * V = nullptr;      // [T x H*dv]
+    const float * Q = nullptr;      // [nq_top x H*dk] top-level queries
+    const float * rkv_w = nullptr;  // [T] device R-KV weights or null
+    const kvc_plan * plan = nullptr;
+    kvc_layer_out out{};            // device outputs (sel, beta, cv, t_total)
+};
+
+struct kvc_phase_ms {
+    double scoring_ms = 0.0;
+    double refit_ms = 0.0;
+};
+
+// Per-device state: stream, events and grow-only scratch arenas.
+struct kvc_ctx {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev[4] = {};
+    std::mutex mu;
+    void * arena[8] = {};
+    size_t arena_cap[8] = {};
+    kvc_unit * d_units = nullptr;
+    size_t units_cap = 0;
+    kvc_layer_out * d_outs = nullptr;
+    size_t outs_cap = 0;
+    uint64_t launches = 0;          // kernel launches issued (for the bench)
+    // optional per-stage device timing (kvc_profile_*): events around each stage
+    int profiling = 0;
+    double stage_ms[KVC_N_STAGES] = {};
+    uint64_t stage_launches[KVC_N_STAGES] = {};
+    std::vector<cudaEvent_t> ev_pool;            // reused timing events
+    std::vector<std::pair<int, int>> pending;    // (stage, first event index) awaiting resolution
+    size_t ev_used = 0;
+};
+
+// Accumulate the elapsed times of the stages recorded since the last call
+// (waits for the last recorded event).
+void kvc_resolve_timers(kvc_ctx * ctx);
+
+// Stage ids for per-stage timing.
+enum {
+    KVC_ST_DECODE = 0, KVC_ST_SCORE, KVC_ST_SOFTMAX, KVC_ST_SELECT, KVC_ST_PV, KVC_ST_BETA,
+    KVC_ST_XBUILD, KVC_ST_LSQ, KVC_ST_REFINE, KVC_ST_METRICS, KVC_ST_REQUANT,
+};
+
+// Brackets one stage with events on ctx->stream when profiling is on.
+struct kvc_stage_timer {
+    kvc_ctx * ctx;
+    int stage;
+    int first = -1;
+    kvc_stage_timer(kvc_ctx * c, int s, int n_launch);
+    ~kvc_stage_timer();
+};
+
+// Context of the current CUDA device (created on first use). nullptr if no device.
+kvc_ctx * kvc_get_ctx(int * rc);
+
+// Grow arena slot `slot` to at least `bytes` (device memory).
+int kvc_arena(kvc_ctx * ctx, int slot, size_t bytes, void ** out);
+
+// Run the compaction pipeline over all units of `jobs` on ctx->stream.
+// Outputs land in each job's `out` buffers. Stream-ordered; no host sync
+// unless `phase` is non-null (then the phases are timed with events).
+int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, int dv,
+                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase);
+
+// Quality metrics of one layer (device), summed on the host in reference order.
+int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, int dv,
+                       kv_compact_stats * st);
+
+// Launchers (kernels in score.cu, select.cu, lsq.cu, nnls.cu, metrics.cu).
+int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_cols,
+                     const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st);
+int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const kvc_params_dev & P,
+                                  float * fs, cudaStream_t st);
+int kvc_launch_pv(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
+                  float * fs, cudaStream_t st);
+int kvc_launch_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
+                         float * fs, const kvc_layer_out * d_outs, cudaStream_t st);
+int kvc_launch_aggregate(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,
+                         cudaStream_t st);
+int kvc_launch_select(const kvc_unit * d_units, int n_units, int max_C, const kvc_params_dev & P, float * fs,
+                      int * is, const kvc_layer_out * d_outs, cudaStream_t st);
+size_t kvc_lsq_smem_bytes(int n);
+int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, size_t smem_bytes,
+                   const kvc_params_dev & P, const float * fs, double * gs,
+                   const kvc_layer_out * d_outs, cudaStream_t st);
+int kvc_metric_pairs(int H, int nq);
+int kvc_launch_metrics(const float * K, const float * V, const float * Q, int T, int nq, int H, int dk, int dv,
+                       const int * sel, const float * beta, const float * cv, int t, float isd,
+                       float * scratch, float * res, cudaStream_t st);
+int kvc_launch_gather_rows(const float * src, int src_stride, const int * idx, int rows, int n,
+                           float * dst, int dst_stride, cudaStream_t st);
+int kvc_launch_cheap_q(const float * K, int T, int ek, int nq, float * Q, cudaStream_t st);
+int kvc_launch_beta(const kvc_unit * d_units, int n_units, int max_nq, int max_t, const kvc_params_dev & P,
+                    float * fs, int * is, double * gs, const kvc_layer_out * d_outs, cudaStream_t st);
+int kvc_launch_refine(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,
+                      int * is, const kvc_layer_out * d_outs, cudaStream_t st);

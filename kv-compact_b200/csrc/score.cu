@@ -1,0 +1,327 @@
+// score.cu — reference scoring, row softmax + key importance, refit target Y.
+//
+// Stage 1, k_score: S[q][j] = (sum_d Q[q][d] * K[key(j)][d]) * (1/sqrt(d_k))
+//   The reference computes each dot product as a sequential fp32 sum over d
+//   with a separate multiply per term, then scales (include/kv-compact-math.h:
+//   44-54, src/kv-compact-api.cpp:618-628). Key selection ranks keys by values
+//   derived from S, and a different summation order moves S by ~1e-6 relative,
+//   which is enough to reorder keys whose importances differ by less than
+//   that. So every S element here is accumulated in exactly the reference's
+//   order with explicitly rounded multiply and add: S is bit-identical to the
+//   reference's. The kernel is a 64x64-tile SIMT GEMM whose inner loop runs
+//   over d in order for 16 independent accumulators per thread.
+//   The same kernel builds S[:, sel] for the value refit (gather mode).
+//
+// Stage 2, k_softmax_importance: row softmax with max shift and
+//   1/(sum + 1e-12) (math.h:201-248), A overwrites S in place, row max/sum
+//   are kept for the beta fit, and per-key importance aggregates A over the
+//   queries in query order (max, RMS or mean), plus the per-key max used by
+//   sensitivity weighting (math.h:579-594).
+//
+// Stage 3, k_pv: Y_h = A_h V_h (math.h:70-80 via src/kv-compact-api.cpp:754-783),
+//   a 64x64-tile SIMT GEMM with fp32 FMA (Y only feeds the least-squares
+//   right-hand side, which is tolerance-checked).
+#include "kvc_internal.h"
+
+#include <math.h>
+
+namespace {
+
+constexpr int SB = 64, SK = 32, ST = 256;
+
+// Position of cheap reference query qi of n within a chunk of C tokens
+// (src/kv-compact-api.cpp:140-146): floor(((qi+1)/(n+1))^2 * (C-1)).
+__device__ __forceinline__ int cheap_pos(int qi, int n, int C) {
+    float fr = __fdiv_rn((float)(qi + 1), (float)(n + 1));
+    fr = __fmul_rn(fr, fr);
+    int pos = (int)__fmul_rn(fr, (float)(C - 1));
+    if (pos >= C) pos = C - 1;
+    if (pos < 0) pos = 0;
+    return pos;
+}
+
+__device__ __forceinline__ const float * qrow_ptr(const kvc_unit & u, int q, int h, int ek, int dk) {
+    if (u.qmode == 0) return u.Q + (long long)q * ek + (long long)h * dk;
+    return u.K + (long long)cheap_pos(q, u.nq, u.C) * ek + (long long)h * dk;
+}
+
+// Load a [rows x SK] slab starting at column d0 from row pointers into
+// smem transposed ([SK][SB+4]); zero outside bounds.
+__device__ __forceinline__ void load_slab(float (*dst)[SB + 4], const float * const * rowp, int nrows,
+                                          int d0, int dk, bool vec_ok) {
+    int tid = threadIdx.x;
+    int r = tid >> 2;            // 0..63
+    int c = (tid & 3) * 8;       // 0,8,16,24
+    const float * p = (r < nrows) ? rowp[r] : nullptr;
+    float v[8];
+    if (p && vec_ok && d0 + c + 8 <= dk) {
+        float4 a = *reinterpret_cast<const float4 *>(p + d0 + c);
+        float4 b = *reinterpret_cast<const float4 *>(p + d0 + c + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = (p && d0 + c + i < dk) ? p[d0 + c + i] : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) dst[c + i][r] = v[i];
+}
+
+}  // namespace
+
+// mode 0: all C keys of the chunk -> S block (ld C)
+// mode 1: the t selected keys     -> X block (ld t), X later softmaxed in place
+__global__ void __launch_bounds__(ST) k_score(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                              float * __restrict__ fs, const int * __restrict__ is,
+                                              int mode) {
+    const kvc_unit u = units[blockIdx.z];
+    if (!u.active) return;
+    const int h = blockIdx.y;
+    const int ncols = mode == 0 ? u.C : u.t;
+    const int tq = (u.nq + SB - 1) / SB, tk = (ncols + SB - 1) / SB;
+    if ((int)blockIdx.x >= tq * tk) return;
+    const int q0 = (blockIdx.x / tk) * SB, j0 = (blockIdx.x % tk) * SB;
+    const int ek = P.H * P.dk, dk = P.dk;
+    const int * sel = is + u.sel_off;
+
+    __shared__ float Qs[SK][SB + 4];
+    __shared__ float Ks[SK][SB + 4];
+    __shared__ const float * qp[SB];
+    __shared__ const float * kp[SB];
+    int tid = threadIdx.x;
+    if (tid < SB) {
+        int q = q0 + tid;
+        qp[tid] = q < u.nq ? qrow_ptr(u, q, h, ek, dk) : nullptr;
+    } else if (tid < 2 * SB) {
+        int j = j0 + tid - SB;
+        if (j < ncols) {
+            int key = mode == 0 ? j : sel[j];
+            kp[tid - SB] = u.K + (long long)key * ek + (long long)h * dk;
+        } else {
+            kp[tid - SB] = nullptr;
+        }
+    }
+    __syncthreads();
+    const bool vec_ok = ((ek & 3) == 0) && ((dk & 3) == 0) &&
+                        ((((uintptr_t)u.K) & 15) == 0) && (u.qmode == 1 || (((uintptr_t)u.Q) & 15) == 0);
+    const int ty = tid >> 4, tx = tid & 15;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+
+    for (int d0 = 0; d0 < dk; d0 += SK) {
+        load_slab(Qs, qp, SB, d0, dk, vec_ok);
+        load_slab(Ks, kp, SB, d0, dk, vec_ok);
+        __syncthreads();
+        const int kend = min(SK, dk - d0);
+        for (int kk = 0; kk < kend; kk++) {
+            float4 a = *reinterpret_cast<const float4 *>(&Qs[kk][ty * 4]);
+            float4 b = *reinterpret_cast<const float4 *>(&Ks[kk][tx * 4]);
+            float av[4] = {a.x, a.y, a.z, a.w};
+            float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+        }
+        __syncthreads();
+    }
+    const int ld = ncols;
+    float * out = fs + (mode == 0 ? u.s_off + (long long)h * u.nq * u.C : u.x_off + (long long)h * u.nq * u.t);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int q = q0 + ty * 4 + i;
+        if (q >= u.nq) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int c = j0 + tx * 4 + j;
+            if (c < ncols) out[(long long)q * ld + c] = __fmul_rn(acc[i][j], P.isd);
+        }
+    }
+}
+
+// One CTA per (unit, head). Phase 1: one warp per row — max, exp, sum,
+// normalise in place. Phase 2: one thread per key — aggregate over queries.
+__global__ void __launch_bounds__(256) k_softmax_importance(const kvc_unit * __restrict__ units,
+                                                           kvc_params_dev P, float * __restrict__ fs) {
+    const kvc_unit u = units[blockIdx.y];
+    const int h = blockIdx.x;
+    const int C = u.C, nq = u.nq;
+    float * S = fs + u.s_off + (long long)h * nq * C;
+    float * rmax = fs + u.row_off + (long long)h * 2 * nq;
+    float * rsum = rmax + nq;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int q = warp; q < nq; q += nw) {
+        float * row = S + (long long)q * C;
+        float m = row[0];
+        for (int j = lane; j < C; j += 32) { float v = row[j]; if (v > m) m = v; }
+        for (int o = 16; o; o >>= 1) { float v = __shfl_xor_sync(0xffffffffu, m, o); if (v > m) m = v; }
+        float s = 0.0f;
+        for (int j = lane; j < C; j += 32) {
+            float e = expf(__fsub_rn(row[j], m));
+            row[j] = e;
+            s = __fadd_rn(s, e);
+        }
+        for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        float inv = __fdiv_rn(1.0f, __fadd_rn(s, 1e-12f));
+        for (int j = lane; j < C; j += 32) row[j] = __fmul_rn(row[j], inv);
+        if (lane == 0) { rmax[q] = m; rsum[q] = s; }
+    }
+    __syncthreads();
+    float * imp = fs + u.imp_off + (long long)h * C;
+    float * cmax = fs + u.imp_off + (long long)(P.H + h) * C;
+    const float inv_m = __fdiv_rn(1.0f, (float)nq);
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+        float acc = 0.0f, mx = 0.0f;
+        for (int q = 0; q < nq; q++) {
+            float w = S[(long long)q * C + j];
+            if (P.score_method == 0) { if (w > acc) acc = w; }
+            else if (P.score_method == 1) acc = __fadd_rn(acc, __fmul_rn(w, w));
+            else acc = __fadd_rn(acc, w);
+            if (w > mx) mx = w;
+        }
+        if (P.score_method == 1) acc = sqrtf(__fmul_rn(acc, inv_m));
+        else if (P.score_method == 2) acc = __fmul_rn(acc, inv_m);
+        imp[j] = acc;
+        cmax[j] = mx;
+    }
+}
+
+// Y_h [nq x dv] = A_h [nq x C] . V_h [C x dv]; 64x64 output tile per CTA.
+__global__ void __launch_bounds__(ST) k_pv(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                           float * __restrict__ fs) {
+    const kvc_unit u = units[blockIdx.z];
+    const int h = blockIdx.y;
+    const int dv = P.dv, ev = P.H * P.dv, nq = u.nq, C = u.C;
+    const int tq = (nq + SB - 1) / SB, tn = (dv + SB - 1) / SB;
+    if ((int)blockIdx.x >= tq * tn) return;
+    const int q0 = (blockIdx.x / tn) * SB, n0 = (blockIdx.x % tn) * SB;
+    const float * A = fs + u.s_off + (long long)h * nq * C;
+    const float * V = u.V + (long long)h * dv;
+    float * Y = fs + u.y_off + (long long)h * nq * dv;
+
+    __shared__ float As[SK][SB + 4];   // [k][row]
+    __shared__ float Vs[SK][SB + 4];   // [k][col]
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < C; k0 += SK) {
+        // A tile: 64 rows x 32 k; thread -> row tid/4, 8 consecutive k
+        {
+            int r = tid >> 2, c = (tid & 3) * 8;
+            int q = q0 + r;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                int k = k0 + c + i;
+                As[c + i][r] = (q < nq && k < C) ? A[(long long)q * C + k] : 0.0f;
+            }
+        }
+        // V tile: 32 k x 64 cols; thread -> k tid/8, 8 consecutive cols
+        {
+            int r = tid >> 3, c = (tid & 7) * 8;
+            int k = k0 + r;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                int n = n0 + c + i;
+                Vs[r][c + i] = (k < C && n < dv) ? V[(long long)k * ev + n] : 0.0f;
+            }
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < SK; kk++) {
+            float4 a = *reinterpret_cast<const float4 *>(&As[kk][ty * 4]);
+            float4 b = *reinterpret_cast<const float4 *>(&Vs[kk][tx * 4]);
+            float av[4] = {a.x, a.y, a.z, a.w};
+            float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int q = q0 + ty * 4 + i;
+        if (q >= nq) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int n = n0 + tx * 4 + j;
+            if (n < dv) Y[(long long)q * dv + n] = acc[i][j];
+        }
+    }
+}
+
+// Row softmax of X = S[:, sel] + beta in place (math.h:83-100 via
+// src/kv-compact-api.cpp:834-840); one warp per row.
+__global__ void __launch_bounds__(256) k_softmax_x(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                   float * __restrict__ fs, const float * __restrict__ beta_all,
+                                                   const kvc_layer_out * __restrict__ outs) {
+    const kvc_unit u = units[blockIdx.z];
+    if (!u.active) return;
+    const int h = blockIdx.y;
+    const int t = u.t, nq = u.nq;
+    const kvc_layer_out lo = outs[u.layer];
+    const float * beta = lo.beta + (long long)h * lo.t_total + u.out_off;
+    float * X = fs + u.x_off + (long long)h * nq * t;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int q = blockIdx.x * nw + warp; q < nq; q += gridDim.x * nw) {
+        float * row = X + (long long)q * t;
+        float m = -INFINITY;
+        bool first = true;
+        for (int j = lane; j < t; j += 32) {
+            float v = __fadd_rn(row[j], beta[j]);
+            row[j] = v;
+            if (first || v > m) { m = v; first = false; }
+        }
+        for (int o = 16; o; o >>= 1) { float v = __shfl_xor_sync(0xffffffffu, m, o); if (v > m) m = v; }
+        float s = 0.0f;
+        for (int j = lane; j < t; j += 32) {
+            float e = expf(__fsub_rn(row[j], m));
+            row[j] = e;
+            s = __fadd_rn(s, e);
+        }
+        for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        float inv = __fdiv_rn(1.0f, __fadd_rn(s, 1e-12f));
+        for (int j = lane; j < t; j += 32) row[j] = __fmul_rn(row[j], inv);
+    }
+    (void)beta_all;
+}
+
+int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_cols,
+                     const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    int tiles = ((max_nq + SB - 1) / SB) * ((max_cols + SB - 1) / SB);
+    dim3 grid(tiles, P.H, n_units);
+    k_score<<<grid, ST, 0, st>>>(d_units, P, fs, is, mode);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const kvc_params_dev & P,
+                                  float * fs, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    k_softmax_importance<<<dim3(P.H, n_units), 256, 0, st>>>(d_units, P, fs);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+int kvc_launch_pv(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
+                  float * fs, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    int tiles = ((max_nq + SB - 1) / SB) * ((P.dv + SB - 1) / SB);
+    k_pv<<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+int kvc_launch_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
+                         float * fs, const kvc_layer_out * d_outs, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    int rows_per_cta = 8;
+    int gx = (max_nq + rows_per_cta - 1) / rows_per_cta;
+    k_softmax_x<<<dim3(gx, P.H, n_units), 256, 0, st>>>(d_units, P, fs, nullptr, d_outs);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}

@@ -772,8 +772,13 @@ kv_compact_params oracle_params_default(void) {               /* api.cpp:333-358
 static float * g_trace_imp = NULL;
 static int g_trace_cap = 0;
 static int g_trace_len = 0;
+static int g_trace_base = 0;   /* chunk start of the body being traced */
 
-void oracle_trace_importance(float * buf, int cap) { g_trace_imp = buf; g_trace_cap = cap; g_trace_len = 0; }
+/* Record the global importance of every key of the next call into buf
+ * (position j of the layer -> buf[j]); pass NULL to stop tracing. */
+void oracle_trace_importance(float * buf, int cap) {
+    g_trace_imp = buf; g_trace_cap = cap; g_trace_len = 0; g_trace_base = 0;
+}
 int oracle_trace_len(void) { return g_trace_len; }
 
 /* beta for one head: w from NNLS on exp-scores, beta = log(max(1e-12, w))
@@ -873,9 +878,8 @@ static int orc_compact_body(const float * K, const float * V, const float * Q, i
         }
     }
     if (g_trace_imp) {
-        int n = T < g_trace_cap ? T : g_trace_cap;
-        memcpy(g_trace_imp, gimp, (size_t)n * 4);
-        g_trace_len = n;
+        for (int j = 0; j < T && g_trace_base + j < g_trace_cap; j++) g_trace_imp[g_trace_base + j] = gimp[j];
+        if (g_trace_base + T > g_trace_len) g_trace_len = g_trace_base + T;
     }
 
     /* selection (api.cpp:687-744) */
@@ -1060,9 +1064,11 @@ int oracle_kv_compact(const float * K, const float * V, const float * Q, int T, 
         if (cp.n_shared_prefix > cT) cp.n_shared_prefix = cT;
         kv_compact_reasoning rz;
         if (cp.reasoning) { rz = *cp.reasoning; rz.token_offset += st; cp.reasoning = &rz; }
+        g_trace_base = st;
         rc = oracle_kv_compact(K + (size_t)st * ek, V + (size_t)st * ev, Qu, cT, nq, H, dk, dv,
                                &cp, &cr[c]);
     }
+    g_trace_base = 0;
     if (rc != 0) {
         for (int c = 0; c < nc; c++) oracle_result_free(&cr[c]);
         free(cr); free(cheap);

@@ -1,0 +1,130 @@
+"""GPU parity of libkvc.so (called through the drop-in C ABI) against the
+reference's outputs (golden fixtures made by running the reference) and the
+CPU oracle. Tolerances are stated in tests/parity.py."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import parity
+from caserun import run_case
+from conftest import golden_cases, golden_path, load_case
+from kvc_b200 import abi
+
+pytestmark = pytest.mark.gpu
+
+# features the device pipeline implements
+UNSUPPORTED = {"use_omp"}
+
+
+def supported(case):
+    p = case["meta"]["params"] or {}
+    return not any(p.get(k) for k in UNSUPPORTED)
+
+
+def oracle_importance(oracle, case):
+    """Per-position global importance as the reference computes it."""
+    T = case["meta"]["data"]["T"]
+    buf = np.zeros(T, np.float32)
+    lib = oracle["_lib"]
+    lib.oracle_trace_importance(buf.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), T)
+    rc, _ = run_case(oracle, case)
+    lib.oracle_trace_importance(None, 0)
+    assert rc == 0
+    return buf
+
+
+GOLDEN = [c for c in golden_cases() if c not in ("codecs",)]
+
+
+@pytest.mark.parametrize("name", GOLDEN)
+def test_golden_parity(kvc, oracle, name):
+    case = load_case(golden_path(name))
+    if not supported(case):
+        pytest.skip("option not on the device path yet")
+    meta = case["meta"]
+    p = meta["params"] or {}
+    rc, out = run_case(kvc, case)
+    assert rc == 0, rc
+    assert out["t"] == int(case["t"])
+    if meta["kind"] == "multi_round":
+        # indices map through two rounds; require the set to agree exactly
+        np.testing.assert_array_equal(out["indices"], case["indices"])
+    elif p.get("use_diversity"):
+        np.testing.assert_array_equal(out["indices"], case["indices"])
+    else:
+        imp = oracle_importance(oracle, case)
+        units = parity.plan_units(meta["data"]["T"], p)
+        mism, ties, worst = parity.classify_indices(out["indices"], case["indices"], imp, units)
+        assert mism == ties, f"{mism} index mismatches, {ties} near-ties, worst gap {worst:.3e}"
+        if mism:
+            print(f"\n{name}: {ties} near-tie swaps (<{parity.NEAR_TIE_REL} relative importance gap)")
+    assert np.all(np.isfinite(out["C_v"]))
+    same = np.array_equal(out["indices"], case["indices"])
+    if p.get("skip_beta", 1):
+        assert np.all(out["beta"] == 0)
+    # C_v against the exact fp64 ridge solution of the same selection
+    if meta["kind"] == "compact" and same:
+        d = meta["data"]["d"]
+        H = meta["data"]["H"]
+        Q = case["Q"] if case["Q"].size else None
+        ex = parity.exact_cv(case["K"], case["V"], Q, H, d, case["indices"], case["beta"],
+                             parity.plan_units(meta["data"]["T"], p), p, Q is None)
+        e_ours = parity.rel_l2(out["C_v"], ex)
+        e_ref = parity.rel_l2(case["C_v"], ex)
+        print(f"\n{name}: C_v rel-L2 ours-vs-fp64 {e_ours:.2e}, reference-vs-fp64 {e_ref:.2e}, "
+              f"ours-vs-reference {parity.rel_l2(out['C_v'], case['C_v']):.2e}")
+        assert e_ours <= max(parity.CV_REL_TOL, e_ref), (e_ours, e_ref)
+    # quality stats: cosine of compacted attention vs the reference's
+    cos_ours, cos_ref = out["stats_arr"][0], case["stats"][0]
+    assert cos_ours >= parity.COS_RATIO * cos_ref - 1e-6, (cos_ours, cos_ref)
+    if "K_out" in case and same:
+        np.testing.assert_array_equal(out["K_out"], case["K_out"])
+        # device V requant == host codec (pinned to the reference) on our C_v
+        dk = meta["data"]["d"]
+        H = meta["data"]["H"]
+        rows = np.concatenate([out["C_v"][h] for h in range(H)], axis=1).reshape(out["t"], H * dk)
+        rows = np.ascontiguousarray(np.stack([np.concatenate([out["C_v"][h][j] for h in range(H)]) for j in range(out["t"])]))
+        np.testing.assert_array_equal(out["V_out"], abi.quantize_rows(kvc, rows, meta["data"]["v_type"]))
+
+
+def test_seam_scores_bitexact(kvc, oracle):
+    """kv_compact_cuda_score_all_heads reproduces the CPU path's scores bit
+    for bit (sequential dot, then the scale)."""
+    rng = np.random.default_rng(5)
+    nq, T, H, d = 37, 301, 3, 48
+    Q = rng.standard_normal((nq, H * d)).astype(np.float32)
+    K = rng.standard_normal((T, H * d)).astype(np.float32)
+    outs = [np.zeros(nq * T, np.float32) for _ in range(H)]
+    FP = ctypes.POINTER(ctypes.c_float)
+    arr = (FP * H)(*[o.ctypes.data_as(FP) for o in outs])
+    scale = np.float32(1.0) / np.sqrt(np.float32(d))
+    rc = kvc["_lib"].kv_compact_cuda_score_all_heads(abi.fptr(Q), abi.fptr(K), arr, nq, T, H, d, float(scale))
+    assert rc == 0
+    for h in range(H):
+        q, k = Q[:, h * d:(h + 1) * d], K[:, h * d:(h + 1) * d]
+        ref = np.zeros((nq, T), np.float32)
+        acc = np.zeros((nq, T), np.float32)
+        for dd in range(d):
+            acc = (acc + (q[:, dd:dd + 1] * k[:, dd][None, :]).astype(np.float32)).astype(np.float32)
+        ref = (acc * np.float32(scale)).astype(np.float32)
+        np.testing.assert_array_equal(outs[h].reshape(nq, T), ref)
+
+
+def test_seam_refit_target(kvc):
+    rng = np.random.default_rng(6)
+    nq, T, H, d = 20, 333, 2, 40
+    W = [rng.random((nq, T)).astype(np.float32) for _ in range(H)]
+    V = rng.standard_normal((T, H * d)).astype(np.float32)
+    Y = [np.zeros((nq, d), np.float32) for _ in range(H)]
+    FP = ctypes.POINTER(ctypes.c_float)
+    wa = (FP * H)(*[w.ctypes.data_as(FP) for w in W])
+    ya = (FP * H)(*[y.ctypes.data_as(FP) for y in Y])
+    assert kvc["_lib"].kv_compact_cuda_refit_target_all_heads(wa, abi.fptr(V), ya, nq, T, H, d) == 0
+    for h in range(H):
+        ref = W[h].astype(np.float64) @ V[:, h * d:(h + 1) * d].astype(np.float64)
+        np.testing.assert_allclose(Y[h], ref, rtol=1e-5, atol=1e-5)
+
+
+def test_device_available(kvc):
+    assert kvc["_lib"].kv_compact_cuda_available() == 1
