@@ -454,12 +454,12 @@ int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, 
     const kvc_plan & pl = *job.plan;
     const int pairs = kvc_metric_pairs(H, pl.nq_top);
     const int t = job.out.t_total;
-    const long long per = std::max(pl.T, t);
+    const size_t nf = kvc_metric_scratch_floats(H, pl.nq_top, pl.T, t, dv);
     void * a4;
     int rc;
-    if ((rc = kvc_arena(ctx, 4, (size_t)(pairs * per + pairs * 3 + 32) * 4, &a4))) return rc;
+    if ((rc = kvc_arena(ctx, 4, nf * 4, &a4))) return rc;
     float * scratch = (float *)a4;
-    float * res = scratch + pairs * per;
+    float * res = scratch + nf - 64 - (size_t)pairs * 3;
     float isd = 1.0f / sqrtf((float)dk);
     {
         kvc_stage_timer tm(ctx, KVC_ST_METRICS, 1);

@@ -123,6 +123,7 @@ int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, size_t smem
                    const kvc_params_dev & P, const float * fs, double * gs,
                    const kvc_layer_out * d_outs, cudaStream_t st);
 int kvc_metric_pairs(int H, int nq);
+size_t kvc_metric_scratch_floats(int H, int nq, int T, int t, int dv);
 int kvc_launch_metrics(const float * K, const float * V, const float * Q, int T, int nq, int H, int dk, int dv,
                        const int * sel, const float * beta, const float * cv, int t, float isd,
                        float * scratch, float * res, cudaStream_t st);

@@ -23,6 +23,8 @@
 
 namespace {
 constexpr int GT = 32;
+constexpr int FN = 128;   // max unknowns of the fast path (k_lsq_small)
+constexpr int FC = 8;     // right-hand-side columns per warp in k_lsq_small (16 warps)
 }
 
 __global__ void __launch_bounds__(256) k_gram(const kvc_unit * __restrict__ units, kvc_params_dev P,
@@ -96,6 +98,7 @@ __global__ void __launch_bounds__(256) k_chol_solve(const kvc_unit * __restrict_
     const int nq = u.nq, t = u.t, dv = P.dv;
     const bool dual = nq < t;
     const int n = dual ? nq : t;
+    if (n <= FN && dv <= FN) return;           // handled by k_lsq_small
     const int PW = lsq_panel(n);
     const float * X = fs + u.x_off + (long long)h * nq * t;
     const float * Y = fs + u.y_off + (long long)h * nq * dv;
@@ -196,6 +199,197 @@ __global__ void __launch_bounds__(256) k_chol_solve(const kvc_unit * __restrict_
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// Fast path: n = min(n_q, t) <= 128 and d_v <= 128, one CTA of 16 warps per
+// (unit, head). G (fp64) lives in shared memory and is factorised with a
+// 32-column blocked Cholesky (3 block-wide barriers per block column). The
+// right-hand sides stay in registers: warp w owns columns [8w, 8w+8), lane l
+// owns rows l, l+32, l+64, l+96, and both triangular solves run
+// warp-synchronously (no block barriers). Z then replaces G in shared memory
+// for the dual product C_v = X^T Z.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(512, 1) k_lsq_small(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                      const float * __restrict__ fs, const double * __restrict__ gs,
+                                                      const kvc_layer_out * __restrict__ outs) {
+    const kvc_unit u = units[blockIdx.x];
+    if (!u.active) return;
+    const int nq = u.nq, t = u.t, dv = P.dv;
+    const bool dual = nq < t;
+    const int n = dual ? nq : t;
+    if (n > FN || dv > FN) return;            // handled by k_chol_solve
+    const int h = blockIdx.y;
+    const float * X = fs + u.x_off + (long long)h * nq * t;
+    const float * Y = fs + u.y_off + (long long)h * nq * dv;
+    const kvc_layer_out lo = outs[u.layer];
+    float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
+    const double * Gg = gs + u.g_off + (long long)h * n * n;
+
+    extern __shared__ double G[];              // [n][n], later Z [n][dv]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int e = tid; e < n * n; e += blockDim.x) G[e] = Gg[e];
+    __syncthreads();
+
+    // ---- blocked Cholesky, lower triangle, row-major G[i*n + j]
+    for (int kb = 0; kb < n; kb += 32) {
+        const int nb = min(32, n - kb);
+        if (warp == 0) {
+            for (int k = kb; k < kb + nb; k++) {
+                double d = G[k * n + k];
+                double l = (d > 0.0 && isfinite(d)) ? sqrt(d) : 0.0;
+                __syncwarp();
+                if (lane == 0) G[k * n + k] = l;
+                const int i = kb + lane;
+                if (i > k && i < kb + nb) G[i * n + k] = (l > 0.0) ? G[i * n + k] / l : 0.0;
+                __syncwarp();
+                if (i > k && i < kb + nb) {
+                    const double lik = G[i * n + k];
+                    for (int j = k + 1; j <= i; j++) G[i * n + j] -= lik * G[j * n + k];
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+        // panel below the diagonal block: L_ik = (A_ik - sum_{m<k} L_im L_km) / L_kk
+        for (int i = kb + nb + tid; i < n; i += blockDim.x) {
+            for (int k = kb; k < kb + nb; k++) {
+                double v = G[i * n + k];
+                for (int m = kb; m < k; m++) v -= G[i * n + m] * G[k * n + m];
+                const double l = G[k * n + k];
+                G[i * n + k] = (l > 0.0) ? v / l : 0.0;
+            }
+        }
+        __syncthreads();
+        // trailing update of the lower triangle
+        const int r0 = kb + nb, m = n - r0;
+        for (int e = tid; e < m * m; e += blockDim.x) {
+            const int i = r0 + e / m, j = r0 + e % m;
+            if (j > i) continue;
+            double v = G[i * n + j];
+            for (int q = kb; q < kb + nb; q++) v -= G[i * n + q] * G[j * n + q];
+            G[i * n + j] = v;
+        }
+        __syncthreads();
+    }
+
+    // ---- right-hand sides in registers
+    const int c0 = warp * FC;
+    double b[4][FC];
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int r = lane + 32 * s;
+#pragma unroll
+        for (int c = 0; c < FC; c++) {
+            double v = 0.0;
+            if (r < n && c0 + c < dv) {
+                if (dual) {
+                    v = (double)Y[(long long)r * dv + c0 + c];
+                } else {
+                    for (int q = 0; q < nq; q++)
+                        v = fma((double)X[(long long)q * t + r], (double)Y[(long long)q * dv + c0 + c], v);
+                }
+            }
+            b[s][c] = v;
+        }
+    }
+    // ---- forward: L w = b. Row k = 32*S + kk lives in slot S of lane kk;
+    // S is a compile-time loop index so b never needs dynamic indexing.
+#pragma unroll
+    for (int S = 0; S < 4; S++) {
+        for (int kk = 0; kk < 32; kk++) {
+            const int k = 32 * S + kk;
+            if (k >= n) break;
+            const double lkk = G[k * n + k];
+            double z[FC];
+#pragma unroll
+            for (int c = 0; c < FC; c++) {
+                const double v = (lkk > 0.0) ? b[S][c] / lkk : 0.0;
+                z[c] = __shfl_sync(0xffffffffu, v, kk);
+            }
+            if (lane == kk) {
+#pragma unroll
+                for (int c = 0; c < FC; c++) b[S][c] = z[c];
+            }
+#pragma unroll
+            for (int s2 = S; s2 < 4; s2++) {
+                const int r = lane + 32 * s2;
+                if (r > k && r < n) {
+                    const double l = G[r * n + k];
+#pragma unroll
+                    for (int c = 0; c < FC; c++) b[s2][c] -= l * z[c];
+                }
+            }
+        }
+    }
+    // ---- backward: L^T x = w
+#pragma unroll
+    for (int S = 3; S >= 0; S--) {
+        for (int kk = 31; kk >= 0; kk--) {
+            const int k = 32 * S + kk;
+            if (k >= n) continue;
+            const double lkk = G[k * n + k];
+            double z[FC];
+#pragma unroll
+            for (int c = 0; c < FC; c++) {
+                const double v = (lkk > 0.0) ? b[S][c] / lkk : 0.0;
+                z[c] = __shfl_sync(0xffffffffu, v, kk);
+            }
+            if (lane == kk) {
+#pragma unroll
+                for (int c = 0; c < FC; c++) b[S][c] = z[c];
+            }
+#pragma unroll
+            for (int s2 = 0; s2 <= S; s2++) {
+                const int r = lane + 32 * s2;
+                if (r < k) {
+                    const double l = G[k * n + r];
+#pragma unroll
+                    for (int c = 0; c < FC; c++) b[s2][c] -= l * z[c];
+                }
+            }
+        }
+    }
+    if (!dual) {
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const int r = lane + 32 * s;
+            if (r >= n) continue;
+#pragma unroll
+            for (int c = 0; c < FC; c++)
+                if (c0 + c < dv) cv[(long long)r * dv + c0 + c] = (float)b[s][c];
+        }
+        return;
+    }
+    __syncthreads();                            // every warp is done with L
+    double * Z = G;                             // [n][dv]
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        const int r = lane + 32 * s;
+        if (r >= n) continue;
+#pragma unroll
+        for (int c = 0; c < FC; c++)
+            if (c0 + c < dv) Z[r * dv + c0 + c] = b[s][c];
+    }
+    __syncthreads();
+    // ---- C_v[j][cb:cb+16] = sum_a X[a][j] Z[a][cb:cb+16]
+    const int nblk = (dv + 15) / 16;
+    for (int e = tid; e < t * nblk; e += blockDim.x) {
+        const int j = e % t, cb = (e / t) * 16;
+        double acc[16];
+#pragma unroll
+        for (int c = 0; c < 16; c++) acc[c] = 0.0;
+        for (int a = 0; a < nq; a++) {
+            const double x = (double)X[(long long)a * t + j];
+            const double * zr = Z + a * dv + cb;
+#pragma unroll
+            for (int c = 0; c < 16; c++) acc[c] = fma(x, zr[c < dv - cb ? c : 0], acc[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < 16; c++)
+            if (cb + c < dv) cv[(long long)j * dv + cb + c] = (float)acc[c];
+    }
+}
+
 size_t kvc_lsq_smem_bytes(int n) {
     size_t pw = (size_t)lsq_panel(n);
     size_t b = (size_t)n * pw * sizeof(double);
@@ -210,8 +404,14 @@ int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, size_t smem
     int tn = (max_n + GT - 1) / GT;
     k_gram<<<dim3(tn * tn, P.H, n_units), 256, 0, st>>>(d_units, P, fs, gs);
     KVC_CUDA(cudaGetLastError());
-    KVC_CUDA(cudaFuncSetAttribute(k_chol_solve, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
-    k_chol_solve<<<dim3(n_units, P.H), 256, smem_bytes, st>>>(d_units, P, fs, gs, d_outs);
+    const size_t fast_smem = (size_t)FN * FN * sizeof(double);
+    KVC_CUDA(cudaFuncSetAttribute(k_lsq_small, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fast_smem));
+    k_lsq_small<<<dim3(n_units, P.H), 512, fast_smem, st>>>(d_units, P, fs, gs, d_outs);
     KVC_CUDA(cudaGetLastError());
+    if (max_n > FN || P.dv > FN) {
+        KVC_CUDA(cudaFuncSetAttribute(k_chol_solve, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
+        k_chol_solve<<<dim3(n_units, P.H), 256, smem_bytes, st>>>(d_units, P, fs, gs, d_outs);
+        KVC_CUDA(cudaGetLastError());
+    }
     return KVC_OK;
 }

@@ -52,10 +52,8 @@ def kvc():
     """libkvc.so bound through the drop-in ABI."""
     if not os.path.exists(LIB_PATH):
         pytest.fail("kv-compact_b200/lib/libkvc.so missing: run `make -C kv-compact_b200`")
-    lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_LOCAL)
-    fns = abi.bind(lib)
-    fns["_lib"] = lib
-    return fns
+    from kvc_b200 import lib as kvclib
+    return kvclib.load()
 
 
 def load_case(path):

@@ -1,0 +1,199 @@
+"""GPU tests at configuration shapes: the whole-model batched API against the
+drop-in C ABI, cfg1/cfg2-shaped layers against the reference CPU library
+(oracle/_ref when built, else the C oracle), the device codecs, and
+size-independent properties at the full cfg4 size."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import parity
+from conftest import REPO, has_gpu
+from kvc_b200 import ORACLE_PATH, REF_PATH, abi, workloads
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def cpu_ref():
+    """The reference library if built here, else the oracle restatement."""
+    if os.path.exists(REF_PATH):
+        return abi.bind(ctypes.CDLL(REF_PATH, mode=ctypes.RTLD_LOCAL)), "reference"
+    return abi.bind(ctypes.CDLL(ORACLE_PATH, mode=ctypes.RTLD_LOCAL), prefix="oracle_"), "oracle"
+
+
+def trace_importance(oracle, fn):
+    """Run fn() on the oracle with importance tracing; returns the trace."""
+    def go(T):
+        buf = np.zeros(T, np.float32)
+        lib = oracle["_lib"]
+        lib.oracle_trace_importance(buf.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), T)
+        fn()
+        lib.oracle_trace_importance(None, 0)
+        return buf
+    return go
+
+
+def check_indices(ours, ref, imp, units):
+    mism, ties, worst = parity.classify_indices(ours, ref, imp, units)
+    assert mism == ties, f"{mism} index mismatches, {ties} near-ties, worst gap {worst:.3e}"
+    return mism
+
+
+def test_cfg1_shape_cheap_q(kvc, oracle, cpu_ref):
+    """cfg1: 1 layer, 1 head, d=128, T=4096, low-rank keys with outlier
+    channels, K-as-Q (cheap queries, Q pointer NULL), 50%, no chunking."""
+    ref, _ = cpu_ref
+    T, H, d = 4096, 1, 128
+    K, V, _ = workloads.small_case(0, T, 4, H, d, "lowrank")
+    pk = dict(target_ratio=0.5, chunk_size=-1, use_cheap_qref=1)
+    rc, ours = abi.run_compact(kvc, K, V, None, 0, H, d, d, abi.make_params(kvc, **pk))
+    assert rc == 0
+    rc, theirs = abi.run_compact(ref, K, V, None, 0, H, d, d, abi.make_params(ref, **pk))
+    assert rc == 0
+    assert ours["t"] == theirs["t"] == 2048
+    imp = trace_importance(oracle, lambda: abi.run_compact(oracle, K, V, None, 0, H, d, d,
+                                                             abi.make_params(oracle, **pk)))(T)
+    check_indices(ours["indices"], theirs["indices"], imp, parity.plan_units(T, pk))
+    assert ours["stats"]["avg_cosine_sim"] >= parity.COS_RATIO * theirs["stats"]["avg_cosine_sim"] - 1e-6
+    if np.array_equal(ours["indices"], theirs["indices"]):
+        ex = parity.exact_cv(K, V, None, H, d, theirs["indices"], theirs["beta"], parity.plan_units(T, pk), pk, True)
+        e_ours, e_ref = parity.rel_l2(ours["C_v"], ex), parity.rel_l2(theirs["C_v"], ex)
+        print(f"\ncfg1: C_v rel-L2 ours {e_ours:.2e} reference {e_ref:.2e} (vs fp64)")
+        assert e_ours <= max(parity.CV_REL_TOL, e_ref)
+
+
+def test_cfg2_layer_f16(kvc, oracle, cpu_ref):
+    """One cfg2 layer: 8 KV heads, d=128, T=16384, fp16 K/V (F16 path of
+    kv_compact_quantized), SnapKV n_q=128, 20% (auto chunks of 1280)."""
+    ref, _ = cpu_ref
+    T, H, d, nq = 16384, 8, 128, 128
+    K, V, Q = workloads.small_case(7, T, nq, H, d, "rope")
+    Kq, Vq = abi.quantize_rows(kvc, K, abi.KV_TYPE_F16), abi.quantize_rows(kvc, V, abi.KV_TYPE_F16)
+    pk = dict(target_ratio=0.2)
+    args = (Kq, Vq, Q, 1, 1, Kq.shape[1], Vq.shape[1], T, nq, H, d, d)
+    rc, ours = abi.run_quantized(kvc, *args, abi.make_params(kvc, **pk))
+    assert rc == 0
+    rc, theirs = abi.run_quantized(ref, *args, abi.make_params(ref, **pk))
+    assert rc == 0
+    assert ours["t"] == theirs["t"] == 3276
+    Kf = abi.dequantize_rows(kvc, Kq, 1, H * d)
+    Vf = abi.dequantize_rows(kvc, Vq, 1, H * d)
+    imp = trace_importance(oracle, lambda: abi.run_compact(oracle, Kf, Vf, Q, nq, H, d, d,
+                                                             abi.make_params(oracle, **pk)))(T)
+    n_ties = check_indices(ours["indices"], theirs["indices"], imp, parity.plan_units(T, pk))
+    print(f"\ncfg2 layer: {n_ties} near-tie swaps of {ours['t']}")
+    assert ours["stats"]["avg_cosine_sim"] >= parity.COS_RATIO * theirs["stats"]["avg_cosine_sim"] - 1e-6
+    same = ours["indices"] == theirs["indices"]
+    np.testing.assert_array_equal(ours["K_out"][same], theirs["K_out"][same])
+    if np.all(same):
+        ex = parity.exact_cv(Kf, Vf, Q, H, d, theirs["indices"], theirs["beta"], parity.plan_units(T, pk), pk, False)
+        e_ours, e_ref = parity.rel_l2(ours["C_v"], ex), parity.rel_l2(theirs["C_v"], ex)
+        print(f"cfg2 layer: C_v rel-L2 ours {e_ours:.2e} reference {e_ref:.2e} (vs fp64), "
+              f"ours vs reference {parity.rel_l2(ours['C_v'], theirs['C_v']):.2e}")
+        assert e_ours <= max(parity.CV_REL_TOL, e_ref)
+
+
+def _model(fns, T, H, d, n_layers, typ, seed):
+    import torch
+    from kvc_b200 import lib
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    Kq, Vq, Q = [], [], []
+    for _ in range(n_layers):
+        K = workloads.torch_rope_keys(T, H, d, g, "cuda")
+        V = torch.randn((T, H * d), generator=g, device="cuda")
+        Kq.append(lib.quantize_dev(fns, K, typ))
+        Vq.append(lib.quantize_dev(fns, V, typ))
+        Q.append(workloads.torch_snapkv_queries(H, d, g, "cuda").contiguous())
+    return Kq, Vq, Q
+
+
+@pytest.mark.parametrize("typ", [abi.KV_TYPE_Q8_0, abi.KV_TYPE_Q4_0])
+def test_batched_equals_dropin(kvc, typ):
+    """kvc_compact_layers_dev over 3 layers == kv_compact_quantized per layer,
+    bit for bit."""
+    import torch
+    from kvc_b200 import lib
+    T, H, d = 3000, 2, 64
+    Kq, Vq, Q = _model(kvc, T, H, d, 3, typ, 11)
+    params = abi.make_params(kvc, target_ratio=0.2)
+    model = lib.BatchedModel(kvc, Kq, Vq, Q, T, H, d, d, typ, typ, params)
+    model.run(want_stats=True)
+    torch.cuda.synchronize()
+    for l in range(3):
+        t = model.t[l]
+        rc, one = abi.run_quantized(kvc, Kq[l].cpu().numpy(), Vq[l].cpu().numpy(), Q[l].cpu().numpy(), typ, typ,
+                                    Kq[l].shape[1], Vq[l].shape[1], T, Q[l].shape[0], H, d, d, params)
+        assert rc == 0 and one["t"] == t
+        np.testing.assert_array_equal(model.sel[l][:t].cpu().numpy(), one["indices"])
+        np.testing.assert_array_equal(model.cv[l][:H * t * d].cpu().numpy().reshape(H, t, d), one["C_v"])
+        np.testing.assert_array_equal(model.kout[l].cpu().numpy().reshape(t, -1), one["K_out"])
+        np.testing.assert_array_equal(model.vout[l].cpu().numpy().reshape(t, -1), one["V_out"])
+        st = model.stats(l)
+        assert abs(st["avg_cosine_sim"] - one["stats"]["avg_cosine_sim"]) < 1e-6
+
+
+def test_layer_filter_periodic(kvc):
+    """params.layer_filter (periodic, interval 4) selects layers 3, 7 of 8."""
+    from kvc_b200 import lib
+    T, H, d = 2000, 2, 32
+    Kq, Vq, Q = _model(kvc, T, H, d, 8, abi.KV_TYPE_Q8_0, 12)
+
+    @abi.LAYER_FILTER_FN
+    def periodic(l, n, data):
+        return 1 if (l + 1) % 4 == 0 else 0
+
+    params = abi.make_params(kvc, target_ratio=0.25)
+    params.layer_filter = periodic
+    model = lib.BatchedModel(kvc, Kq, Vq, Q, T, H, d, d, 8, 8, params)
+    model.run()
+    assert [l for l in range(8) if model.t[l] > 0] == [3, 7]
+    assert [model.results[l].t for l in range(8)] == model.t
+
+
+@pytest.mark.parametrize("typ", [0, 1, 2, 3, 8])
+def test_device_codecs_match_host(kvc, typ):
+    import torch
+    from kvc_b200 import lib
+    rng = np.random.default_rng(typ)
+    X = (rng.standard_normal((257, 512)) * rng.choice([1e-6, 1e-2, 1.0, 3e4], size=(257, 1))).astype(np.float32)
+    X[3] = 0.0
+    X[4, ::3] = -0.0
+    B_dev = lib.quantize_dev(kvc, torch.from_numpy(X).cuda(), typ).cpu().numpy()
+    np.testing.assert_array_equal(B_dev, abi.quantize_rows(kvc, X, typ))
+    D_dev = lib.dequantize_dev(kvc, torch.from_numpy(B_dev).cuda(), typ, 512).cpu().numpy()
+    np.testing.assert_array_equal(D_dev, abi.dequantize_rows(kvc, B_dev, typ, 512))
+
+
+def test_full_size_cfg4_properties(kvc):
+    """Two cfg4 layers at full size (T=100,000, 8 heads, d=128, Q8_0): kept
+    counts as planned, indices ascending and unique, each chunk keeps its
+    share inside its bounds, outputs finite, K_out == encode(decode(K)[sel])."""
+    import torch
+    from kvc_b200 import lib
+    T, H, d = 100_000, 8, 128
+    Kq, Vq, Q = _model(kvc, T, H, d, 2, abi.KV_TYPE_Q8_0, 13)
+    params = abi.make_params(kvc, target_ratio=0.2)
+    model = lib.BatchedModel(kvc, Kq, Vq, Q, T, H, d, d, 8, 8, params)
+    model.run()
+    units = parity.plan_units(T, dict(target_ratio=0.2))
+    assert len(units) == 79 and sum(u[2] for u in units) == 20000
+    for l in range(2):
+        t = model.t[l]
+        assert t == 20000
+        sel = model.sel[l][:t].cpu().numpy()
+        assert np.all(np.diff(sel) > 0) and sel[0] >= 0 and sel[-1] < T
+        off = 0
+        for (st, C, tc, _, _) in units:
+            chunk = sel[off:off + tc]
+            assert chunk.min() >= st and chunk.max() < st + C
+            off += tc
+        assert torch.isfinite(model.cv[l][:H * t * d]).all()
+        Kd = lib.dequantize_dev(kvc, Kq[l], 8, H * d)
+        rows = Kd[torch.from_numpy(sel).long().cuda()].contiguous()
+        np.testing.assert_array_equal(model.kout[l].cpu().numpy().reshape(t, -1),
+                                      lib.quantize_dev(kvc, rows, 8).cpu().numpy())
+        st = model.stats(l)
+        assert 0.9 < st["avg_cosine_sim"] <= 1.0001
