@@ -266,6 +266,7 @@ struct unit_sizes {
 static unit_sizes sizes_of(const kvc_plan_unit & u, int H, int dv) {
     unit_sizes s;
     const int n = std::min(u.nq, u.t);
+    (void)n;
     s.fs = al32((long long)H * u.nq * u.C) + al32((long long)(2 * H + 1) * u.C) + al32((long long)2 * H * u.nq) +
            al32((long long)H * u.nq * dv) + al32((long long)H * u.nq * u.t);
     s.is = al32(u.t) + al32(4LL * u.C);
@@ -279,8 +280,9 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     cudaStream_t st = ctx->stream;
     if (p.use_sensitivity && H > 64) return KVC_ERR_SHAPE;
     if (dk > KVC_MAX_D || dv > KVC_MAX_D) return KVC_ERR_SHAPE;
-    if (!p.skip_beta || p.refine_rounds > 0 || p.use_omp) {
-        // beta / refinement / OMP stages are dispatched below
+    if (p.use_omp) {
+        fprintf(stderr, "[kvc] OMP key selection is not available on the device path\n");
+        return KVC_ERR_SHAPE;
     }
 
     kvc_params_dev P;
@@ -365,7 +367,9 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             u.c_off = is; is += al32(4LL * pu.C);
             const int n = std::min(pu.nq, pu.t);
             if (n > 3072) return KVC_ERR_SHAPE;
-            u.g_off = gs; gs += al32((long long)H * n * n);
+            long long gper = (long long)n * n;
+            if (!p.skip_beta) gper = std::max<long long>(gper, (long long)kvc_nnls_doubles_per_head(pu.t, pu.nq));
+            u.g_off = gs; gs += al32((long long)H * gper);
             max_nq = std::max(max_nq, pu.nq);
             max_C = std::max(max_C, pu.C);
             max_t = std::max(max_t, pu.t);
@@ -419,13 +423,16 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
                 kvc_stage_timer tm(ctx, KVC_ST_REFINE, 1);
                 if ((rc = kvc_launch_refine(du, nu, P, F, I, ctx->d_outs, st))) return rc;
             }
+            {
+                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1);     // raw S[:, sel]
+                if ((rc = kvc_launch_score(du, nu, max_nq, max_t, P, F, I, 1, st))) return rc;
+            }
             if (!p.skip_beta) {
-                kvc_stage_timer tm(ctx, KVC_ST_BETA, 1);
+                kvc_stage_timer tm(ctx, KVC_ST_BETA, 2);
                 if ((rc = kvc_launch_beta(du, nu, max_nq, max_t, P, F, I, G, ctx->d_outs, st))) return rc;
             }
             {
-                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 2);
-                if ((rc = kvc_launch_score(du, nu, max_nq, max_t, P, F, I, 1, st))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1);     // X = softmax(S[:, sel] + beta)
                 if ((rc = kvc_launch_softmax_x(du, nu, max_nq, P, F, ctx->d_outs, st))) return rc;
             }
             {

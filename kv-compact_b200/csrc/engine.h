@@ -132,5 +132,6 @@ int kvc_launch_gather_rows(const float * src, int src_stride, const int * idx, i
 int kvc_launch_cheap_q(const float * K, int T, int ek, int nq, float * Q, cudaStream_t st);
 int kvc_launch_beta(const kvc_unit * d_units, int n_units, int max_nq, int max_t, const kvc_params_dev & P,
                     float * fs, int * is, double * gs, const kvc_layer_out * d_outs, cudaStream_t st);
+size_t kvc_nnls_doubles_per_head(int t, int nq);
 int kvc_launch_refine(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,
                       int * is, const kvc_layer_out * d_outs, cudaStream_t st);
