@@ -40,6 +40,21 @@ int kv_compact_cuda_refit_target_all_heads(const float * const * W_per_head, con
  * (reference kv-compact-accel.h:55). */
 void kv_compact_cuda_pool_free(void);
 
+/* kv_compact_cuda_score_all_heads for callers that cannot let the library
+ * allocate device memory (an engine that has reserved all of HBM for its own
+ * allocator, or a path that must not pay cudaMalloc's latency and implicit
+ * synchronisation). No counterpart in the reference. Same arguments and the
+ * same bit-identical scores; staging lives in a 16 MiB array compiled into
+ * the library (held by every GPU that loads it), so it needs
+ * n_q*H*d_k + T*H*d_k + H*n_q*T floats (each part rounded up to 64) <=
+ * 4,194,304 and returns -13 with a message beyond that; -1 on bad arguments
+ * or no sm_100 device. The first call on a device looks up the array's
+ * address (make it before any stream capture). Calls share the array: calls
+ * from this process are serialised, calls overlapping on the GPU race. */
+int kv_compact_cuda_score_all_heads_noalloc(const float * Q_ref, const float * K_all,
+                                            float ** scores_out, int n_q, int T,
+                                            int n_head_kv, int d_k, float scale);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,6 +18,7 @@ DROPIN_SYMBOLS = [
 SEAM_SYMBOLS = [
     "kv_compact_cuda_available", "kv_compact_cuda_mat_mul_ABt_scaled", "kv_compact_cuda_score_all_heads",
     "kv_compact_cuda_refit_target_all_heads", "kv_compact_cuda_pool_free",
+    "kv_compact_cuda_score_all_heads_noalloc",
 ]
 BATCHED_SYMBOLS = ["kvc_plan_layers", "kvc_compact_layers_dev", "kvc_launch_count", "kvc_profile",
                    "kvc_quantize_rows_dev", "kvc_dequantize_rows_dev"]
@@ -61,6 +62,9 @@ def load(path=None):
     lib.kv_compact_cuda_score_all_heads.argtypes = [FP, FP, POINTER(FP), c_int, c_int, c_int, c_int, c_float]
     lib.kv_compact_cuda_refit_target_all_heads.restype = c_int
     lib.kv_compact_cuda_refit_target_all_heads.argtypes = [POINTER(FP), FP, POINTER(FP), c_int, c_int, c_int, c_int]
+    lib.kv_compact_cuda_score_all_heads_noalloc.restype = c_int
+    lib.kv_compact_cuda_score_all_heads_noalloc.argtypes = [FP, FP, POINTER(FP), c_int, c_int, c_int, c_int,
+                                                            c_float]
     lib.kv_compact_cuda_pool_free.restype = None
     lib.kv_compact_cuda_pool_free.argtypes = []
     lib.kvc_plan_layers.restype = c_int
