@@ -51,7 +51,8 @@ METRIC = "compaction input tokens/s, all layers×KV-heads, 100k ctx 5x; % of roo
 
 
 def filtered_layers(cfg):
-    return [l for l in range(cfg["n_layers"]) if cfg["interval"] <= 1 or (l + 1) % cfg["interval"] == 0]
+    ls = [l for l in range(cfg["n_layers"]) if cfg["interval"] <= 1 or (l + 1) % cfg["interval"] == 0]
+    return ls[:cfg["max_layers"]] if cfg.get("max_layers") else ls
 
 
 def workload_desc(name, cfg):
@@ -342,8 +343,12 @@ def main():
     ap.add_argument("--config", default="cfg4_q8", choices=sorted(CONFIGS))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="compact only the first N filtered layers (small cases for profiling)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.layers > 0:
+        cfg["max_layers"] = args.layers
     if args.impl == "reference":
         run_reference(args, cfg, args.config)
     else:

@@ -10,7 +10,10 @@
  * reference's callers do with kv_compact_should_compact_layer().
  *
  * All pointers in kvc_layer_desc / kvc_layer_result are DEVICE pointers of
- * the current CUDA device. Calls return after the work has completed.
+ * the current CUDA device. The library's work runs on a blocking stream, so
+ * it starts after all work the caller queued on the legacy default stream;
+ * inputs written on other non-blocking streams must be synchronised by the
+ * caller first. Calls return after the work has completed.
  *
  * Limits: d_k, d_v <= 256; min(n_q, t) <= 3072 per chunk; H <= 64 with
  * use_sensitivity. Violations return -13.

@@ -3,7 +3,7 @@
 // Pipeline over a flat list of units (one per (layer, chunk), all heads):
 //   scoring phase:  k_score -> k_softmax_importance -> k_aggregate -> k_select
 //   refit phase:    k_pv (Y) -> beta (NNLS, optional) -> k_score gather (S[:,sel])
-//                   -> k_softmax_x (X) -> k_gram + k_chol_solve (C_v)
+//                   -> k_softmax_x (X) -> k_dgemm + k_lsq_factor (C_v)
 //                   -> refinement rounds (optional)
 // Every stage is one launch over all units of the batch, so a whole model
 // (all filtered layers) is a handful of launches that fill the 148 SMs.
@@ -142,7 +142,10 @@ kvc_ctx * kvc_get_ctx(int * rc) {
         }
         kvc_ctx * c = new kvc_ctx();
         c->device = dev;
-        if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        // A blocking stream: its work is ordered after everything the caller
+        // queued on the legacy default stream (e.g. PyTorch producing the
+        // device caches the batched API reads) and vice versa.
+        if (cudaStreamCreate(&c->stream) != cudaSuccess) {
             delete c;
             if (rc) *rc = KVC_ERR_CUDA;
             return nullptr;
@@ -270,7 +273,7 @@ static unit_sizes sizes_of(const kvc_plan_unit & u, int H, int dv) {
     s.fs = al32((long long)H * u.nq * u.C) + al32((long long)(2 * H + 1) * u.C) + al32((long long)2 * H * u.nq) +
            al32((long long)H * u.nq * dv) + al32((long long)H * u.nq * u.t);
     s.is = al32(u.t) + al32(4LL * u.C);
-    s.gs = al32((long long)H * n * n);
+    s.gs = al32((long long)H * n * n) + al32((long long)H * n * dv);
     return s;
 }
 
@@ -322,6 +325,12 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     long long budget = (long long)std::min<size_t>((size_t)(free_b * 0.6), (size_t)48 << 30);
     // bytes already held by our arenas can be reused
     budget += (long long)(ctx->arena_cap[0] + ctx->arena_cap[1] + ctx->arena_cap[2]);
+    // KVC_SCRATCH_BUDGET_MB caps the scratch of one batch (testing the
+    // multi-batch path, or leaving room for other users of the device)
+    if (const char * env = getenv("KVC_SCRATCH_BUDGET_MB")) {
+        long long mb = atoll(env);
+        if (mb > 0) budget = std::min(budget, mb << 20);
+    }
 
     if (phase) KVC_CUDA(cudaEventRecord(ctx->ev[0], st));
     double score_ms = 0, refit_ms = 0;
@@ -370,6 +379,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             long long gper = (long long)n * n;
             if (!p.skip_beta) gper = std::max<long long>(gper, (long long)kvc_nnls_doubles_per_head(pu.t, pu.nq));
             u.g_off = gs; gs += al32((long long)H * gper);
+            u.z_off = gs; gs += al32((long long)H * n * dv);
             max_nq = std::max(max_nq, pu.nq);
             max_C = std::max(max_C, pu.C);
             max_t = std::max(max_t, pu.t);
@@ -436,8 +446,8 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
                 if ((rc = kvc_launch_softmax_x(du, nu, max_nq, P, F, ctx->d_outs, st))) return rc;
             }
             {
-                kvc_stage_timer tm(ctx, KVC_ST_LSQ, 2);
-                if ((rc = kvc_launch_lsq(du, nu, max_n, lsq_smem, P, F, G, ctx->d_outs, st))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_LSQ, (max_n > 128 || dv > 128) ? 5 : 4);
+                if ((rc = kvc_launch_lsq(du, nu, max_n, max_t, lsq_smem, P, F, G, ctx->d_outs, st))) return rc;
             }
         }
         if (phase) {
@@ -477,6 +487,9 @@ int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, 
     std::vector<float> h(pairs * 3);
     KVC_CUDA(cudaMemcpyAsync(h.data(), res, pairs * 3 * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
     KVC_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (getenv("KVC_DEBUG_METRICS"))
+        fprintf(stderr, "[kvc] metrics T=%d t=%d nq=%d pairs=%d first (cos,mse,agree)=(%g,%g,%g) scratch=%p\n",
+                pl.T, t, pl.nq_top, pairs, h[0], h[1], h[2], (void *)scratch);
     float sc = 0.0f, sm = 0.0f;
     int agree = 0;
     for (int i = 0; i < pairs; i++) {

@@ -119,7 +119,7 @@ int kvc_launch_aggregate(const kvc_unit * d_units, int n_units, const kvc_params
 int kvc_launch_select(const kvc_unit * d_units, int n_units, int max_C, const kvc_params_dev & P, float * fs,
                       int * is, const kvc_layer_out * d_outs, cudaStream_t st);
 size_t kvc_lsq_smem_bytes(int n);
-int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, size_t smem_bytes,
+int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, int max_t, size_t smem_bytes,
                    const kvc_params_dev & P, const float * fs, double * gs,
                    const kvc_layer_out * d_outs, cudaStream_t st);
 int kvc_metric_pairs(int H, int nq);

@@ -68,7 +68,8 @@ struct kvc_unit {
     long long row_off;    // floats: H blocks of nq (row max / row sum)
     long long y_off;      // floats: H blocks of nq*dv
     long long x_off;      // floats: H blocks of nq*t
-    long long g_off;      // doubles: H blocks of n*n
+    long long g_off;      // doubles: H blocks of n*n (NNLS: its own per-head stride)
+    long long z_off;      // doubles: H blocks of n*d_v (dual Z, or primal X^T Y)
     long long sel_off;    // ints: t selected chunk-local positions
     long long w_off;      // floats: C R-KV weights (or -1: none)
     long long c_off;      // ints/floats: C per-candidate scratch (selection)

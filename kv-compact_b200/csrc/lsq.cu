@@ -14,76 +14,132 @@
 // triangular solves. A non-positive pivot marks its unknown singular and
 // zeroes it, the counterpart of the reference skipping pivots below 1e-12.
 //
-// k_gram:       32x32 fp64 tiles of G, grid over all tiles of all (unit, head)
-// k_chol_solve: one CTA per (unit, head); G in shared memory when n <= 128,
-//               right-hand sides in panels of PW columns.
+// The dense products run as one batched fp64 GEMM launch each (k_dgemm,
+// 64x64 tiles, 4x4 per thread, over every (unit, head)):
+//   GRAM  G = X X^T (dual) or X^T X (primal), + ridge on the diagonal
+//   RHS   R = X^T Y                          (primal only)
+//   OUT   C_v = X^T Z                        (dual only)
+// and the latency-bound part runs one CTA per (unit, head):
+//   k_lsq_factor  Cholesky of G in shared memory (n <= 128) + both triangular
+//                 solves for all d_v right-hand sides in registers; writes Z
+//                 (dual) or C_v (primal).
+//   k_chol_solve  the same for n > 128 or d_v > 128, G in global memory.
 #include "kvc_internal.h"
 
 #include <math.h>
 
 namespace {
 constexpr int GT = 32;
-constexpr int FN = 128;   // max unknowns of the fast path (k_lsq_small)
-constexpr int FC = 8;     // right-hand-side columns per warp in k_lsq_small (16 warps)
+constexpr int FN = 128;   // max unknowns of the shared-memory path (k_lsq_factor)
+constexpr int FC = 8;     // right-hand-side columns per warp in k_lsq_factor (16 warps)
 }
 
-__global__ void __launch_bounds__(256) k_gram(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                              const float * __restrict__ fs, double * __restrict__ gs) {
+enum { DG_GRAM = 0, DG_RHS = 1, DG_OUT = 2 };
+constexpr int DT = 64, DK = 16;
+
+// One 64x64 tile of C = A B per CTA for the (unit, head, mode) problem.
+__global__ void __launch_bounds__(256) k_dgemm(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                               const float * __restrict__ fs, double * __restrict__ gs,
+                                               const kvc_layer_out * __restrict__ outs, int mode) {
     const kvc_unit u = units[blockIdx.z];
     if (!u.active) return;
     const int h = blockIdx.y;
-    const int nq = u.nq, t = u.t;
+    const int nq = u.nq, t = u.t, dv = P.dv;
     const bool dual = nq < t;
-    const int n = dual ? nq : t, inner = dual ? t : nq;
-    const int tn = (n + GT - 1) / GT;
-    if ((int)blockIdx.x >= tn * tn) return;
-    const int a0 = (blockIdx.x / tn) * GT, b0 = (blockIdx.x % tn) * GT;
-    if (b0 > a0) return;                     // lower tiles only; mirrored on store
+    const int n = dual ? nq : t;
+    if ((mode == DG_RHS && dual) || (mode == DG_OUT && !dual)) return;
+    if (mode != DG_GRAM && (n > FN || dv > FN)) return;     // k_chol_solve does its own
+    int M, N, K;
+    if (mode == DG_GRAM) { M = n; N = n; K = dual ? t : nq; }
+    else { M = t; N = dv; K = nq; }
+    const int tn = (N + DT - 1) / DT, tm = (M + DT - 1) / DT;
+    if ((int)blockIdx.x >= tm * tn) return;
+    const int m0 = (blockIdx.x / tn) * DT, n0 = (blockIdx.x % tn) * DT;
+    if (mode == DG_GRAM && n0 > m0) return;          // lower tiles; mirrored on store
     const float * X = fs + u.x_off + (long long)h * nq * t;
-    double * G = gs + u.g_off + (long long)h * n * n;
-    __shared__ double As[GT][GT + 1];
-    __shared__ double Bs[GT][GT + 1];
+    const float * Y = fs + u.y_off + (long long)h * nq * dv;
+    const double * Z = gs + u.z_off + (long long)h * n * dv;
+
+    __shared__ __align__(16) double As[DK][DT + 2];
+    __shared__ __align__(16) double Bs[DK][DT + 2];
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    double acc[2][2] = {{0, 0}, {0, 0}};
-    for (int k0 = 0; k0 < inner; k0 += GT) {
-        for (int e = tid; e < GT * GT; e += 256) {
-            int r = e / GT, c = e % GT;       // r: operand index, c: inner offset
-            int a = a0 + r, b = b0 + r, k = k0 + c;
-            float xa = 0.0f, xb = 0.0f;
-            if (k < inner) {
-                if (dual) {
-                    if (a < n) xa = X[(long long)a * t + k];
-                    if (b < n) xb = X[(long long)b * t + k];
-                } else {
-                    if (a < n) xa = X[(long long)k * t + a];
-                    if (b < n) xb = X[(long long)k * t + b];
-                }
+    const bool rows = (mode == DG_GRAM && dual);     // operands are rows of X (k contiguous)
+    double acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+    for (int k0 = 0; k0 < K; k0 += DK) {
+        for (int e = tid; e < DT * DK; e += 256) {
+            int mm, kk;
+            if (rows) { mm = e / DK; kk = e % DK; } else { kk = e / DT; mm = e % DT; }
+            const int m = m0 + mm, k = k0 + kk;
+            double v = 0.0;
+            if (m < M && k < K) v = rows ? (double)X[(long long)m * t + k] : (double)X[(long long)k * t + m];
+            As[kk][mm] = v;
+        }
+        for (int e = tid; e < DT * DK; e += 256) {
+            int nn, kk;
+            if (rows) { nn = e / DK; kk = e % DK; } else { kk = e / DT; nn = e % DT; }
+            const int c = n0 + nn, k = k0 + kk;
+            double v = 0.0;
+            if (c < N && k < K) {
+                if (mode == DG_GRAM) v = dual ? (double)X[(long long)c * t + k] : (double)X[(long long)k * t + c];
+                else if (mode == DG_RHS) v = (double)Y[(long long)k * dv + c];
+                else v = Z[(long long)k * dv + c];
             }
-            As[c][r] = (double)xa;
-            Bs[c][r] = (double)xb;
+            Bs[kk][nn] = v;
         }
         __syncthreads();
-#pragma unroll 4
-        for (int kk = 0; kk < GT; kk++) {
-            double x0 = As[kk][ty * 2], x1 = As[kk][ty * 2 + 1];
-            double y0 = Bs[kk][tx * 2], y1 = Bs[kk][tx * 2 + 1];
-            acc[0][0] = fma(x0, y0, acc[0][0]);
-            acc[0][1] = fma(x0, y1, acc[0][1]);
-            acc[1][0] = fma(x1, y0, acc[1][0]);
-            acc[1][1] = fma(x1, y1, acc[1][1]);
+#pragma unroll
+        for (int kk = 0; kk < DK; kk++) {
+            const double2 a01 = *reinterpret_cast<const double2 *>(&As[kk][ty * 4]);
+            const double2 a23 = *reinterpret_cast<const double2 *>(&As[kk][ty * 4 + 2]);
+            const double2 b01 = *reinterpret_cast<const double2 *>(&Bs[kk][tx * 4]);
+            const double2 b23 = *reinterpret_cast<const double2 *>(&Bs[kk][tx * 4 + 2]);
+            const double av[4] = {a01.x, a01.y, a23.x, a23.y};
+            const double bv[4] = {b01.x, b01.y, b23.x, b23.y};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
         }
         __syncthreads();
     }
-    const double ridge = (double)P.ridge;
-    for (int i = 0; i < 2; i++)
-        for (int j = 0; j < 2; j++) {
-            int a = a0 + ty * 2 + i, b = b0 + tx * 2 + j;
-            if (a < n && b < n && b <= a) {
-                double v = acc[i][j] + (a == b ? ridge : 0.0);
-                G[(long long)a * n + b] = v;
-                G[(long long)b * n + a] = v;
+    if (mode == DG_GRAM) {
+        double * G = gs + u.g_off + (long long)h * n * n;
+        const double ridge = (double)P.ridge;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int a = m0 + ty * 4 + i, b = n0 + tx * 4 + j;
+                if (a < n && b < n && b <= a) {
+                    const double v = acc[i][j] + (a == b ? ridge : 0.0);
+                    G[(long long)a * n + b] = v;
+                    G[(long long)b * n + a] = v;
+                }
             }
-        }
+    } else if (mode == DG_RHS) {
+        double * R = gs + u.z_off + (long long)h * n * dv;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int a = m0 + ty * 4 + i, c = n0 + tx * 4 + j;
+                if (a < M && c < N) R[(long long)a * dv + c] = acc[i][j];
+            }
+    } else {
+        const kvc_layer_out lo = outs[u.layer];
+        float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int a = m0 + ty * 4 + i, c = n0 + tx * 4 + j;
+                if (a < M && c < N) cv[(long long)a * dv + c] = (float)acc[i][j];
+            }
+    }
 }
 
 // Panel width for n unknowns: keeps the n x PW fp64 panel within 96 KB.
@@ -98,7 +154,7 @@ __global__ void __launch_bounds__(256) k_chol_solve(const kvc_unit * __restrict_
     const int nq = u.nq, t = u.t, dv = P.dv;
     const bool dual = nq < t;
     const int n = dual ? nq : t;
-    if (n <= FN && dv <= FN) return;           // handled by k_lsq_small
+    if (n <= FN && dv <= FN) return;           // handled by k_lsq_factor
     const int PW = lsq_panel(n);
     const float * X = fs + u.x_off + (long long)h * nq * t;
     const float * Y = fs + u.y_off + (long long)h * nq * dv;
@@ -201,17 +257,19 @@ __global__ void __launch_bounds__(256) k_chol_solve(const kvc_unit * __restrict_
 
 
 // ---------------------------------------------------------------------------
-// Fast path: n = min(n_q, t) <= 128 and d_v <= 128, one CTA of 16 warps per
-// (unit, head). G (fp64) lives in shared memory and is factorised with a
-// 32-column blocked Cholesky (3 block-wide barriers per block column). The
-// right-hand sides stay in registers: warp w owns columns [8w, 8w+8), lane l
-// owns rows l, l+32, l+64, l+96, and both triangular solves run
-// warp-synchronously (no block barriers). Z then replaces G in shared memory
-// for the dual product C_v = X^T Z.
+// Factor + solve, n = min(n_q, t) <= 128 and d_v <= 128, one CTA of 16 warps
+// per (unit, head). G (fp64, from k_dgemm) is copied to shared memory with an
+// odd row stride so column walks hit distinct banks, and factorised with a
+// right-looking Cholesky whose steps are spread over all 16 warps. The
+// right-hand sides (Y for the dual, X^T Y from
+// k_dgemm for the primal) stay in registers: warp w owns columns [8w, 8w+8),
+// lane l rows l, l+32, l+64, l+96, and both triangular solves run
+// warp-synchronously with reciprocal pivots. The result Z (dual, consumed by
+// the OUT GEMM) or C_v (primal) is written to global memory.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512, 1) k_lsq_small(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                                      const float * __restrict__ fs, const double * __restrict__ gs,
-                                                      const kvc_layer_out * __restrict__ outs) {
+__global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                       const float * __restrict__ fs, double * __restrict__ gs,
+                                                       const kvc_layer_out * __restrict__ outs) {
     const kvc_unit u = units[blockIdx.x];
     if (!u.active) return;
     const int nq = u.nq, t = u.t, dv = P.dv;
@@ -219,60 +277,39 @@ __global__ void __launch_bounds__(512, 1) k_lsq_small(const kvc_unit * __restric
     const int n = dual ? nq : t;
     if (n > FN || dv > FN) return;            // handled by k_chol_solve
     const int h = blockIdx.y;
-    const float * X = fs + u.x_off + (long long)h * nq * t;
     const float * Y = fs + u.y_off + (long long)h * nq * dv;
-    const kvc_layer_out lo = outs[u.layer];
-    float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
     const double * Gg = gs + u.g_off + (long long)h * n * n;
+    double * Zg = gs + u.z_off + (long long)h * n * dv;        // primal: holds X^T Y on entry
 
-    extern __shared__ double G[];              // [n][n], later Z [n][dv]
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int e = tid; e < n * n; e += blockDim.x) G[e] = Gg[e];
+    extern __shared__ double G[];
+    const int ld = n + 1;
+    double * rinv = G + n * ld;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+    for (int e = tid; e < n * n; e += nthr) G[(e / n) * ld + (e % n)] = Gg[e];
     __syncthreads();
 
-    // ---- blocked Cholesky, lower triangle, row-major G[i*n + j]
-    for (int kb = 0; kb < n; kb += 32) {
-        const int nb = min(32, n - kb);
-        if (warp == 0) {
-            for (int k = kb; k < kb + nb; k++) {
-                double d = G[k * n + k];
-                double l = (d > 0.0 && isfinite(d)) ? sqrt(d) : 0.0;
-                __syncwarp();
-                if (lane == 0) G[k * n + k] = l;
-                const int i = kb + lane;
-                if (i > k && i < kb + nb) G[i * n + k] = (l > 0.0) ? G[i * n + k] / l : 0.0;
-                __syncwarp();
-                if (i > k && i < kb + nb) {
-                    const double lik = G[i * n + k];
-                    for (int j = k + 1; j <= i; j++) G[i * n + j] -= lik * G[j * n + k];
-                }
-                __syncwarp();
-            }
+    // Right-looking Cholesky, every step parallel over the whole CTA. Each
+    // thread derives the pivot reciprocal itself (no extra barrier); the
+    // scaled column goes to colk first so the rank-1 update never reads a
+    // column entry another thread is rewriting. Two barriers per column.
+    double * colk = rinv + FN;                     // [n]
+    for (int k = 0; k < n; k++) {
+        const double d = G[k * ld + k];
+        const double l = (d > 0.0 && isfinite(d)) ? sqrt(d) : 0.0;
+        const double il = (l > 0.0) ? 1.0 / l : 0.0;
+        for (int i = k + 1 + tid; i < n; i += nthr) colk[i] = G[i * ld + k] * il;
+        if (tid == 0) rinv[k] = il;
+        __syncthreads();                           // every thread has read the pivot
+        if (tid == 0) G[k * ld + k] = l;
+        const int m = n - k - 1;                   // trailing size
+        for (int e = tid; e < m * m; e += nthr) {
+            const int i = k + 1 + e / m, j = k + 1 + e % m;
+            if (j <= i) G[i * ld + j] -= colk[i] * colk[j];
         }
-        __syncthreads();
-        // panel below the diagonal block: L_ik = (A_ik - sum_{m<k} L_im L_km) / L_kk
-        for (int i = kb + nb + tid; i < n; i += blockDim.x) {
-            for (int k = kb; k < kb + nb; k++) {
-                double v = G[i * n + k];
-                for (int m = kb; m < k; m++) v -= G[i * n + m] * G[k * n + m];
-                const double l = G[k * n + k];
-                G[i * n + k] = (l > 0.0) ? v / l : 0.0;
-            }
-        }
-        __syncthreads();
-        // trailing update of the lower triangle
-        const int r0 = kb + nb, m = n - r0;
-        for (int e = tid; e < m * m; e += blockDim.x) {
-            const int i = r0 + e / m, j = r0 + e % m;
-            if (j > i) continue;
-            double v = G[i * n + j];
-            for (int q = kb; q < kb + nb; q++) v -= G[i * n + q] * G[j * n + q];
-            G[i * n + j] = v;
-        }
+        for (int i = k + 1 + tid; i < n; i += nthr) G[i * ld + k] = colk[i];
         __syncthreads();
     }
 
-    // ---- right-hand sides in registers
     const int c0 = warp * FC;
     double b[4][FC];
 #pragma unroll
@@ -281,31 +318,19 @@ __global__ void __launch_bounds__(512, 1) k_lsq_small(const kvc_unit * __restric
 #pragma unroll
         for (int c = 0; c < FC; c++) {
             double v = 0.0;
-            if (r < n && c0 + c < dv) {
-                if (dual) {
-                    v = (double)Y[(long long)r * dv + c0 + c];
-                } else {
-                    for (int q = 0; q < nq; q++)
-                        v = fma((double)X[(long long)q * t + r], (double)Y[(long long)q * dv + c0 + c], v);
-                }
-            }
+            if (r < n && c0 + c < dv) v = dual ? (double)Y[(long long)r * dv + c0 + c] : Zg[(long long)r * dv + c0 + c];
             b[s][c] = v;
         }
     }
-    // ---- forward: L w = b. Row k = 32*S + kk lives in slot S of lane kk;
-    // S is a compile-time loop index so b never needs dynamic indexing.
 #pragma unroll
     for (int S = 0; S < 4; S++) {
         for (int kk = 0; kk < 32; kk++) {
             const int k = 32 * S + kk;
             if (k >= n) break;
-            const double lkk = G[k * n + k];
+            const double il = rinv[k];
             double z[FC];
 #pragma unroll
-            for (int c = 0; c < FC; c++) {
-                const double v = (lkk > 0.0) ? b[S][c] / lkk : 0.0;
-                z[c] = __shfl_sync(0xffffffffu, v, kk);
-            }
+            for (int c = 0; c < FC; c++) z[c] = __shfl_sync(0xffffffffu, b[S][c] * il, kk);
             if (lane == kk) {
 #pragma unroll
                 for (int c = 0; c < FC; c++) b[S][c] = z[c];
@@ -314,26 +339,22 @@ __global__ void __launch_bounds__(512, 1) k_lsq_small(const kvc_unit * __restric
             for (int s2 = S; s2 < 4; s2++) {
                 const int r = lane + 32 * s2;
                 if (r > k && r < n) {
-                    const double l = G[r * n + k];
+                    const double l = G[r * ld + k];
 #pragma unroll
                     for (int c = 0; c < FC; c++) b[s2][c] -= l * z[c];
                 }
             }
         }
     }
-    // ---- backward: L^T x = w
 #pragma unroll
     for (int S = 3; S >= 0; S--) {
         for (int kk = 31; kk >= 0; kk--) {
             const int k = 32 * S + kk;
             if (k >= n) continue;
-            const double lkk = G[k * n + k];
+            const double il = rinv[k];
             double z[FC];
 #pragma unroll
-            for (int c = 0; c < FC; c++) {
-                const double v = (lkk > 0.0) ? b[S][c] / lkk : 0.0;
-                z[c] = __shfl_sync(0xffffffffu, v, kk);
-            }
+            for (int c = 0; c < FC; c++) z[c] = __shfl_sync(0xffffffffu, b[S][c] * il, kk);
             if (lane == kk) {
 #pragma unroll
                 for (int c = 0; c < FC; c++) b[S][c] = z[c];
@@ -342,14 +363,25 @@ __global__ void __launch_bounds__(512, 1) k_lsq_small(const kvc_unit * __restric
             for (int s2 = 0; s2 <= S; s2++) {
                 const int r = lane + 32 * s2;
                 if (r < k) {
-                    const double l = G[k * n + r];
+                    const double l = G[k * ld + r];
 #pragma unroll
                     for (int c = 0; c < FC; c++) b[s2][c] -= l * z[c];
                 }
             }
         }
     }
-    if (!dual) {
+    if (dual) {
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const int r = lane + 32 * s;
+            if (r >= n) continue;
+#pragma unroll
+            for (int c = 0; c < FC; c++)
+                if (c0 + c < dv) Zg[(long long)r * dv + c0 + c] = b[s][c];
+        }
+    } else {
+        const kvc_layer_out lo = outs[u.layer];
+        float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
 #pragma unroll
         for (int s = 0; s < 4; s++) {
             const int r = lane + 32 * s;
@@ -358,35 +390,6 @@ __global__ void __launch_bounds__(512, 1) k_lsq_small(const kvc_unit * __restric
             for (int c = 0; c < FC; c++)
                 if (c0 + c < dv) cv[(long long)r * dv + c0 + c] = (float)b[s][c];
         }
-        return;
-    }
-    __syncthreads();                            // every warp is done with L
-    double * Z = G;                             // [n][dv]
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-        const int r = lane + 32 * s;
-        if (r >= n) continue;
-#pragma unroll
-        for (int c = 0; c < FC; c++)
-            if (c0 + c < dv) Z[r * dv + c0 + c] = b[s][c];
-    }
-    __syncthreads();
-    // ---- C_v[j][cb:cb+16] = sum_a X[a][j] Z[a][cb:cb+16]
-    const int nblk = (dv + 15) / 16;
-    for (int e = tid; e < t * nblk; e += blockDim.x) {
-        const int j = e % t, cb = (e / t) * 16;
-        double acc[16];
-#pragma unroll
-        for (int c = 0; c < 16; c++) acc[c] = 0.0;
-        for (int a = 0; a < nq; a++) {
-            const double x = (double)X[(long long)a * t + j];
-            const double * zr = Z + a * dv + cb;
-#pragma unroll
-            for (int c = 0; c < 16; c++) acc[c] = fma(x, zr[c < dv - cb ? c : 0], acc[c]);
-        }
-#pragma unroll
-        for (int c = 0; c < 16; c++)
-            if (cb + c < dv) cv[(long long)j * dv + cb + c] = (float)acc[c];
     }
 }
 
@@ -397,16 +400,21 @@ size_t kvc_lsq_smem_bytes(int n) {
     return b;
 }
 
-int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, size_t smem_bytes,
+int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, int max_t, size_t smem_bytes,
                    const kvc_params_dev & P, const float * fs, double * gs,
                    const kvc_layer_out * d_outs, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
-    int tn = (max_n + GT - 1) / GT;
-    k_gram<<<dim3(tn * tn, P.H, n_units), 256, 0, st>>>(d_units, P, fs, gs);
+    const int tg = (max_n + DT - 1) / DT;
+    k_dgemm<<<dim3(tg * tg, P.H, n_units), 256, 0, st>>>(d_units, P, fs, gs, d_outs, DG_GRAM);
     KVC_CUDA(cudaGetLastError());
-    const size_t fast_smem = (size_t)FN * FN * sizeof(double);
-    KVC_CUDA(cudaFuncSetAttribute(k_lsq_small, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fast_smem));
-    k_lsq_small<<<dim3(n_units, P.H), 512, fast_smem, st>>>(d_units, P, fs, gs, d_outs);
+    const int to = ((max_t + DT - 1) / DT) * ((P.dv + DT - 1) / DT);
+    k_dgemm<<<dim3(to, P.H, n_units), 256, 0, st>>>(d_units, P, fs, gs, d_outs, DG_RHS);
+    KVC_CUDA(cudaGetLastError());
+    const size_t fast_smem = (size_t)(FN * (FN + 1) + 2 * FN) * sizeof(double);
+    KVC_CUDA(cudaFuncSetAttribute(k_lsq_factor, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fast_smem));
+    k_lsq_factor<<<dim3(n_units, P.H), 512, fast_smem, st>>>(d_units, P, fs, gs, d_outs);
+    KVC_CUDA(cudaGetLastError());
+    k_dgemm<<<dim3(to, P.H, n_units), 256, 0, st>>>(d_units, P, fs, gs, d_outs, DG_OUT);
     KVC_CUDA(cudaGetLastError());
     if (max_n > FN || P.dv > FN) {
         KVC_CUDA(cudaFuncSetAttribute(k_chol_solve, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));

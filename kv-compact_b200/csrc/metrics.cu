@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(256) k_mscore(kvc_metric_args a) {
     }
 }
 
-__global__ void __launch_bounds__(256) k_msoftmax(kvc_metric_args a) {
+__global__ void __launch_bounds__(1024) k_msoftmax(kvc_metric_args a) {
     const int side = blockIdx.z, h = blockIdx.y, q = blockIdx.x;
     const int n = side == 0 ? a.T : a.t;
     float * row = a.S + (((long long)side * a.mh + h) * a.mq + q) * a.ld;
@@ -134,49 +134,74 @@ __global__ void __launch_bounds__(256) k_msoftmax(kvc_metric_args a) {
     for (int j = threadIdx.x; j < n; j += blockDim.x) row[j] = __fmul_rn(row[j], inv);
 }
 
-// partial[side][split][h][q][c] = sum over the split's keys of w[q][j] * row_j[c]
+// partial[side][split][h][q][c] = sum over the split's keys of w[q][j] * row_j[c].
+// 256 threads = 8 query groups x 32 column groups; a thread owns queries
+// 4qg..4qg+3 and columns 4cg..4cg+3 (+128 when d_v > 128): per key it reads
+// one float4 of weights (broadcast in the warp) and one or two float4 of
+// values, for 16 or 32 FMAs.
 __global__ void __launch_bounds__(256) k_mpv(kvc_metric_args a) {
     const int side = blockIdx.z, h = blockIdx.y, split = blockIdx.x;
     const int n = side == 0 ? a.T : a.t;
     const long long per = (n + a.nsplit - 1) / a.nsplit;
     const long long jb = split * per, je = min((long long)n, jb + per);
     const int dv = a.dv, ev = a.H * a.dv;
-    __shared__ float Ws[MQ][PK + 1];
-    __shared__ float Vs[PK][KVC_MAX_D + 4];
+    __shared__ __align__(16) float Ws[PK][MQ];
+    __shared__ __align__(16) float Vs[PK][KVC_MAX_D];
     const float * W = a.S + ((long long)side * a.mh + h) * a.mq * a.ld;
-    const int tid = threadIdx.x;
-    const int q = tid >> 3, cl = tid & 7;        // 32 queries x 8 column lanes
-    float acc[KVC_MAX_D / 8];
+    const int tid = threadIdx.x, qg = tid >> 5, cg = tid & 31;
+    float acc[4][8];
 #pragma unroll
-    for (int i = 0; i < KVC_MAX_D / 8; i++) acc[i] = 0.0f;
-    const int ncol = (dv + 7) / 8;
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int c = 0; c < 8; c++) acc[i][c] = 0.0f;
+    const bool hi = dv > 128;
     for (long long j0 = jb; j0 < je; j0 += PK) {
         for (int e = tid; e < MQ * PK; e += 256) {
-            int qq = e / PK, jj = e % PK;
-            long long j = j0 + jj;
-            Ws[qq][jj] = (qq < a.mq && j < je) ? W[(long long)qq * a.ld + j] : 0.0f;
+            const int qq = e / PK, jj = e % PK;
+            const long long j = j0 + jj;
+            Ws[jj][qq] = (qq < a.mq && j < je) ? W[(long long)qq * a.ld + j] : 0.0f;
         }
         for (int e = tid; e < PK * dv; e += 256) {
-            int jj = e / dv, c = e % dv;
-            long long j = j0 + jj;
+            const int jj = e / dv, c = e % dv;
+            const long long j = j0 + jj;
             float v = 0.0f;
             if (j < je) v = side == 0 ? a.V[j * ev + (long long)h * dv + c] : a.cv[((long long)h * a.t + j) * dv + c];
             Vs[jj][c] = v;
         }
         __syncthreads();
-        for (int jj = 0; jj < PK; jj++) {
-            const float w = Ws[q][jj];
+        const int jn = (int)min((long long)PK, je - j0);
+        for (int jj = 0; jj < jn; jj++) {
+            const float4 w4 = *reinterpret_cast<const float4 *>(&Ws[jj][4 * qg]);
+            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+            float vv[8];
+            if (4 * cg < dv) {
+                const float4 v4 = *reinterpret_cast<const float4 *>(&Vs[jj][4 * cg]);
+                vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
+            } else {
+                vv[0] = vv[1] = vv[2] = vv[3] = 0.0f;
+            }
+            if (hi && 128 + 4 * cg < dv) {
+                const float4 v4 = *reinterpret_cast<const float4 *>(&Vs[jj][128 + 4 * cg]);
+                vv[4] = v4.x; vv[5] = v4.y; vv[6] = v4.z; vv[7] = v4.w;
+            } else {
+                vv[4] = vv[5] = vv[6] = vv[7] = 0.0f;
+            }
 #pragma unroll
-            for (int i = 0; i < KVC_MAX_D / 8; i++)
-                if (i < ncol) acc[i] = fmaf(w, Vs[jj][cl + 8 * i], acc[i]);
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int c = 0; c < 8; c++) acc[i][c] = fmaf(wv[i], vv[c], acc[i][c]);
         }
         __syncthreads();
     }
-    if (q < a.mq) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int q = 4 * qg + i;
+        if (q >= a.mq) continue;
         float * out = a.part + ((((long long)side * a.nsplit + split) * a.mh + h) * a.mq + q) * dv;
-        for (int i = 0; i < ncol; i++) {
-            int c = cl + 8 * i;
-            if (c < dv) out[c] = acc[i];
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const int col = (c < 4) ? 4 * cg + c : 128 + 4 * cg + (c - 4);
+            if (col < dv && (c < 4 || hi)) out[col] = acc[i][c];
         }
     }
 }
@@ -223,7 +248,7 @@ int kvc_metric_pairs(int H, int nq) { return (H < 4 ? H : 4) * (nq < 32 ? nq : 3
 size_t kvc_metric_scratch_floats(int H, int nq, int T, int t, int dv) {
     const long long mh = H < 4 ? H : 4, mq = nq < 32 ? nq : 32;
     const long long ld = T > t ? T : t;
-    const long long nsplit = 64;
+    const long long nsplit = 128;
     return (size_t)(2 * mh * mq * ld + 2 * nsplit * mh * mq * dv + mh * mq * 3 + 64);
 }
 
@@ -235,7 +260,7 @@ int kvc_launch_metrics(const float * K, const float * V, const float * Q, int T,
     a.T = T; a.t = t; a.nq = nq; a.H = H; a.dk = dk; a.dv = dv;
     a.mh = H < 4 ? H : 4;
     a.mq = nq < 32 ? nq : 32;
-    a.nsplit = 64;
+    a.nsplit = 128;
     a.isd = isd;
     a.ld = T > t ? T : t;
     a.S = scratch;
@@ -245,7 +270,7 @@ int kvc_launch_metrics(const float * K, const float * V, const float * Q, int T,
     const int nblk = (int)((a.ld + MK - 1) / MK);
     k_mscore<<<dim3(nblk, a.mh, 2), 256, 0, st>>>(a);
     KVC_CUDA(cudaGetLastError());
-    k_msoftmax<<<dim3(a.mq, a.mh, 2), 256, 0, st>>>(a);
+    k_msoftmax<<<dim3(a.mq, a.mh, 2), 1024, 0, st>>>(a);
     KVC_CUDA(cudaGetLastError());
     k_mpv<<<dim3(a.nsplit, a.mh, 2), 256, 0, st>>>(a);
     KVC_CUDA(cudaGetLastError());

@@ -135,6 +135,33 @@ def test_batched_equals_dropin(kvc, typ):
         assert abs(st["avg_cosine_sim"] - one["stats"]["avg_cosine_sim"]) < 1e-6
 
 
+def test_multibatch_equals_single_batch(kvc, monkeypatch):
+    """Splitting the units into several scratch batches (small budget) gives
+    bit-identical results and stats to one batch."""
+    import torch
+    from kvc_b200 import lib
+    T, H, d = 20000, 4, 64
+    Kq, Vq, Q = _model(kvc, T, H, d, 2, abi.KV_TYPE_Q8_0, 21)
+    params = abi.make_params(kvc, target_ratio=0.2)
+    one = lib.BatchedModel(kvc, Kq, Vq, Q, T, H, d, d, 8, 8, params)
+    one.run()
+    torch.cuda.synchronize()
+    monkeypatch.setenv("KVC_SCRATCH_BUDGET_MB", "8")
+    many = lib.BatchedModel(kvc, Kq, Vq, Q, T, H, d, d, 8, 8, params)
+    many.run()
+    torch.cuda.synchronize()
+    for l in range(2):
+        t = one.t[l]
+        assert torch.equal(one.sel[l][:t], many.sel[l][:t])
+        assert torch.equal(one.cv[l][:H * t * d], many.cv[l][:H * t * d])
+        assert torch.equal(one.kout[l], many.kout[l]) and torch.equal(one.vout[l], many.vout[l])
+        s1, s2 = one.stats(l), many.stats(l)
+        print(f"\nlayer {l}: one-batch stats {s1}, multi-batch stats {s2}")
+        assert s1["avg_cosine_sim"] > 0.9
+        for k in ("avg_cosine_sim", "avg_mse", "avg_agreement"):
+            assert s1[k] == s2[k], (k, s1[k], s2[k])
+
+
 def test_layer_filter_periodic(kvc):
     """params.layer_filter (periodic, interval 4) selects layers 3, 7 of 8."""
     from kvc_b200 import lib
