@@ -243,7 +243,7 @@ def run_kvc(args, cfg, name):
     except Exception:
         uuid = str(local)
     sampler = ClockSampler(uuid)
-    time.sleep(0.3)
+    time.sleep(2.0)     # nvidia-smi's own start-up stays outside the timed region
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
@@ -337,7 +337,7 @@ def run_kvc(args, cfg, name):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="kvc", choices=["kvc", "reference"])
     ap.add_argument("--config", default="cfg4_q8", choices=sorted(CONFIGS))

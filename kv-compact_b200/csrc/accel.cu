@@ -131,7 +131,7 @@ KVC_EXPORT void kv_compact_cuda_pool_free(void) {
     if (!ctx) return;
     std::lock_guard<std::mutex> lk(ctx->mu);
     cudaStreamSynchronize(ctx->stream);
-    for (int s = 0; s < 8; s++) {
+    for (int s = 0; s < (int)(sizeof(ctx->arena) / sizeof(ctx->arena[0])); s++) {
         if (ctx->arena[s]) cudaFree(ctx->arena[s]);
         ctx->arena[s] = nullptr;
         ctx->arena_cap[s] = 0;

@@ -30,8 +30,44 @@ struct dev_out {
     float * beta = nullptr;
     float * cv = nullptr;
     float * Q = nullptr;      // top-level queries on the device
+    float * d_res = nullptr;  // metric triples on the device (null: no metrics)
+    int pairs = 0;
+    std::vector<float> h_res; // their host copy
     kv_compact_stats stats{};
 };
+
+// Device->host copies through the pinned staging buffer: every copy is
+// queued on the stream, one wait, then the staged bytes are spread over host
+// threads into the (freshly malloc'd) destinations.
+struct d2h_piece { void * host; const void * dev; size_t bytes; };
+int gather_to_host(kvc_ctx * ctx, const std::vector<d2h_piece> & v) {
+    size_t tot = 0;
+    for (const auto & x : v) tot += (x.bytes + 255) & ~(size_t)255;
+    void * pin;
+    int rc;
+    if ((rc = kvc_pinned(ctx, tot, &pin))) return rc;
+    std::vector<kvc_copy_piece> pieces;
+    size_t off = 0;
+    for (const auto & x : v) {
+        if (x.bytes) {
+            KVC_CUDA(cudaMemcpyAsync((char *)pin + off, x.dev, x.bytes, cudaMemcpyDeviceToHost, ctx->stream));
+            pieces.push_back({x.host, (char *)pin + off, x.bytes});
+        }
+        off += (x.bytes + 255) & ~(size_t)255;
+    }
+    if ((rc = kvc_wait(ctx))) return rc;
+    kvc_parallel_copy(pieces);
+    return KVC_OK;
+}
+
+// After the stream has drained and h_res holds the triples: stats of the call.
+void finish_dev(kvc_ctx * ctx, dev_out * d) {
+    kvc_phase_ms ph;
+    kvc_phase_collect(ctx, &ph);
+    d->stats.scoring_ms = ph.scoring_ms;
+    d->stats.nnls_ms = ph.refit_ms;
+    if (d->d_res) kvc_metrics_reduce(d->h_res.data(), d->pairs, &d->stats);
+}
 
 // Compact one layer whose fp32 K/V are already on the device.
 int compact_dev(kvc_ctx * ctx, const float * dK, const float * dV, const float * hQ, int T, int n_q, int H,
@@ -80,11 +116,14 @@ int compact_dev(kvc_ctx * ctx, const float * dK, const float * dV, const float *
     job.out.cv = dcv;
     job.out.t_total = t;
     kvc_phase_ms ph;
-    if ((rc = kvc_engine_run(ctx, p, H, dk, dv, &job, 1, &ph))) return rc;
-    out->stats.scoring_ms = ph.scoring_ms;
-    out->stats.nnls_ms = ph.refit_ms;
+    if ((rc = kvc_engine_run(ctx, p, H, dk, dv, &job, 1, &ph, want_metrics))) return rc;
     if (want_metrics) {
-        if ((rc = kvc_engine_metrics(ctx, job, H, dk, dv, &out->stats))) return rc;
+        out->pairs = kvc_metric_pairs(H, pl.nq_top);
+        void * a9;
+        if ((rc = kvc_arena(ctx, 9, ((size_t)out->pairs * 3 + 64) * 4, &a9))) return rc;
+        out->d_res = (float *)a9;
+        out->h_res.assign((size_t)out->pairs * 3, 0.0f);
+        if ((rc = kvc_engine_metrics_launch(ctx, job, H, dk, dv, out->d_res))) return rc;
     }
     out->sel = dsel;
     out->beta = dbeta;
@@ -93,7 +132,10 @@ int compact_dev(kvc_ctx * ctx, const float * dK, const float * dV, const float *
     return KVC_OK;
 }
 
-int fill_result(kvc_ctx * ctx, const dev_out & d, int H, int dv, kv_compact_result * r) {
+// Allocate the reference's result arrays and copy the outputs (plus the
+// metric triples and any `extra` pieces) back; finishes d's stats.
+int fill_result(kvc_ctx * ctx, dev_out & d, int H, int dv, kv_compact_result * r,
+                const std::vector<d2h_piece> & extra = {}) {
     const int t = d.plan.t_total;
     r->t = t;
     r->n_head_kv = H;
@@ -104,13 +146,17 @@ int fill_result(kvc_ctx * ctx, const dev_out & d, int H, int dv, kv_compact_resu
         r->beta[h] = (float *)malloc((size_t)std::max(t, 1) * sizeof(float));
         r->C_v[h] = (float *)malloc((size_t)std::max(t, 1) * dv * sizeof(float));
     }
-    cudaStream_t st = ctx->stream;
-    KVC_CUDA(cudaMemcpyAsync(r->selected_indices, d.sel, (size_t)t * 4, cudaMemcpyDeviceToHost, st));
+    std::vector<d2h_piece> v;
+    v.push_back({r->selected_indices, d.sel, (size_t)t * 4});
     for (int h = 0; h < H; h++) {
-        KVC_CUDA(cudaMemcpyAsync(r->beta[h], d.beta + (size_t)h * t, (size_t)t * 4, cudaMemcpyDeviceToHost, st));
-        KVC_CUDA(cudaMemcpyAsync(r->C_v[h], d.cv + (size_t)h * t * dv, (size_t)t * dv * 4, cudaMemcpyDeviceToHost, st));
+        v.push_back({r->beta[h], d.beta + (size_t)h * t, (size_t)t * 4});
+        v.push_back({r->C_v[h], d.cv + (size_t)h * t * dv, (size_t)t * dv * 4});
     }
-    KVC_CUDA(cudaStreamSynchronize(st));
+    for (const auto & x : extra) v.push_back(x);
+    if (d.d_res) v.push_back({d.h_res.data(), d.d_res, d.h_res.size() * sizeof(float)});
+    int rc = gather_to_host(ctx, v);
+    if (rc) return rc;
+    finish_dev(ctx, &d);
     return KVC_OK;
 }
 
@@ -248,17 +294,21 @@ KVC_EXPORT int kv_compact_multi_round(const float * K_all, const float * V_all, 
         if ((rc = compact_dev(ctx, pK[cur], pV[cur], cheap ? nullptr : Q_ref_all, cur_T, nq_r, H, d_k, d_v, p,
                               &d, true)))
             return rc;
-        if (per_round_stats) per_round_stats[r] = d.stats;
         const int nT = d.plan.t_total;
         std::vector<int> sel(nT);
-        KVC_CUDA(cudaMemcpyAsync(sel.data(), d.sel, (size_t)nT * 4, cudaMemcpyDeviceToHost, st));
-        KVC_CUDA(cudaStreamSynchronize(st));
+        if ((rc = gather_to_host(ctx, {{sel.data(), d.sel, (size_t)nT * 4},
+                                       {d.h_res.data(), d.d_res, d.h_res.size() * sizeof(float)}})))
+            return rc;
+        finish_dev(ctx, &d);
+        if (per_round_stats) per_round_stats[r] = d.stats;
         std::vector<int> no(nT);
         for (int j = 0; j < nT; j++) no[j] = orig[sel[j]];
         if (r == n_rounds - 1) {
+            const kv_compact_stats keep = d.stats;     // already complete
+            d.d_res = nullptr;
             if ((rc = fill_result(ctx, d, H, d_v, result))) return rc;
             memcpy(result->selected_indices, no.data(), (size_t)nT * sizeof(int));
-            result->stats = d.stats;
+            result->stats = keep;
         } else {
             const int nxt = cur ^ 1;
             if ((rc = kvc_launch_gather_rows(pK[cur], ek, d.sel, nT, ek, pK[nxt], ek, st))) return rc;
@@ -369,17 +419,16 @@ KVC_EXPORT int kv_compact_quantized(const uint8_t * K_quant, const uint8_t * V_q
         if ((rc = kvc_launch_encode_gather(dK, (size_t)ek, d.sel, t, ek, k_type, oK, k_row_bytes, st))) return rc;
         if ((rc = kvc_launch_encode_heads(d.cv, H, t, d_v, v_type, oV, v_row_bytes, st))) return rc;
     }
-    if ((rc = fill_result(ctx, d, H, d_v, &result->base))) return rc;
-    result->base.stats = d.stats;
     result->k_type = k_type;
     result->v_type = v_type;
     result->k_row_bytes = k_row_bytes;
     result->v_row_bytes = v_row_bytes;
     result->K_out = (uint8_t *)malloc(std::max<size_t>((size_t)t * k_row_bytes, 1));
     result->V_out = (uint8_t *)malloc(std::max<size_t>((size_t)t * v_row_bytes, 1));
-    KVC_CUDA(cudaMemcpyAsync(result->K_out, oK, (size_t)t * k_row_bytes, cudaMemcpyDeviceToHost, st));
-    KVC_CUDA(cudaMemcpyAsync(result->V_out, oV, (size_t)t * v_row_bytes, cudaMemcpyDeviceToHost, st));
-    KVC_CUDA(cudaStreamSynchronize(st));
+    if ((rc = fill_result(ctx, d, H, d_v, &result->base,
+                          {{result->K_out, oK, (size_t)t * k_row_bytes}, {result->V_out, oV, (size_t)t * v_row_bytes}})))
+        return rc;
+    result->base.stats = d.stats;
     result->base.stats.elapsed_ms = ms_since(t0);
     kvc_resolve_timers(ctx);
     return KVC_OK;

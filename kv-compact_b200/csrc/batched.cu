@@ -154,7 +154,17 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
         J.out.t_total = plans[i].t_total;
     }
     kvc_phase_ms ph;
-    if ((rc = kvc_engine_run(ctx, p, H, dk, dv, jobs.data(), n, want_stats ? &ph : nullptr))) return rc;
+    if ((rc = kvc_engine_run(ctx, p, H, dk, dv, jobs.data(), n, want_stats ? &ph : nullptr, want_stats != 0)))
+        return rc;
+    // requantisation and metric kernels of every layer, then one wait
+    std::vector<int> pair_off(n + 1, 0);
+    for (int i = 0; i < n; i++) pair_off[i + 1] = pair_off[i] + (want_stats ? kvc_metric_pairs(H, plans[i].nq_top) : 0);
+    float * d_res = nullptr;
+    if (want_stats) {
+        void * a9;
+        if ((rc = kvc_arena(ctx, 9, ((size_t)pair_off[n] * 3 + 64) * 4, &a9))) return rc;
+        d_res = (float *)a9;
+    }
     for (int i = 0; i < n; i++) {
         const int l = on[i];
         const int t = plans[i].t_total;
@@ -171,13 +181,21 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
                 return rc;
         }
         memset(&R[l].stats, 0, sizeof(R[l].stats));
-        if (want_stats) {
-            if ((rc = kvc_engine_metrics(ctx, jobs[i], H, dk, dv, &R[l].stats))) return rc;
+        if (want_stats && (rc = kvc_engine_metrics_launch(ctx, jobs[i], H, dk, dv, d_res + (size_t)pair_off[i] * 3)))
+            return rc;
+    }
+    if ((rc = kvc_wait(ctx))) return rc;
+    if (want_stats) {
+        std::vector<float> h((size_t)pair_off[n] * 3);
+        KVC_CUDA(cudaMemcpyAsync(h.data(), d_res, h.size() * sizeof(float), cudaMemcpyDeviceToHost, st));
+        kvc_phase_collect(ctx, &ph);
+        for (int i = 0; i < n; i++) {
+            const int l = on[i];
+            kvc_metrics_reduce(h.data() + (size_t)pair_off[i] * 3, pair_off[i + 1] - pair_off[i], &R[l].stats);
             R[l].stats.scoring_ms = ph.scoring_ms / n;
             R[l].stats.nnls_ms = ph.refit_ms / n;
         }
     }
-    KVC_CUDA(cudaStreamSynchronize(st));
     kvc_resolve_timers(ctx);
     return KVC_OK;
 }

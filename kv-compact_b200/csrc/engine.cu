@@ -13,6 +13,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <thread>
 
 // ---------------------------------------------------------------------------
 // planning (host)
@@ -174,6 +175,83 @@ int kvc_arena(kvc_ctx * ctx, int slot, size_t bytes, void ** out) {
     return KVC_OK;
 }
 
+int kvc_wait(kvc_ctx * ctx) {
+    KVC_CUDA(cudaEventRecord(ctx->ev[0], ctx->stream));
+    cudaError_t e;
+    while ((e = cudaEventQuery(ctx->ev[0])) == cudaErrorNotReady) {
+    }
+    KVC_CUDA(e);
+    return KVC_OK;
+}
+
+int kvc_pinned(kvc_ctx * ctx, size_t bytes, void ** out) {
+    if (bytes == 0) bytes = 256;
+    if (ctx->pinned_cap < bytes) {
+        if (ctx->pinned) {
+            KVC_CUDA(cudaStreamSynchronize(ctx->stream));
+            cudaFreeHost(ctx->pinned);
+            ctx->pinned = nullptr;
+            ctx->pinned_cap = 0;
+        }
+        size_t cap = bytes + bytes / 8;
+        KVC_CUDA(cudaHostAlloc(&ctx->pinned, cap, cudaHostAllocDefault));
+        ctx->pinned_cap = cap;
+    }
+    *out = ctx->pinned;
+    return KVC_OK;
+}
+
+void kvc_parallel_copy(const std::vector<kvc_copy_piece> & pieces) {
+    size_t total = 0;
+    for (const auto & pc : pieces) total += pc.bytes;
+    unsigned hw = std::thread::hardware_concurrency();
+    int nt = (int)std::min<size_t>(std::max(1u, std::min(hw, 16u)), total / (4u << 20) + 1);
+    if (nt <= 1) {
+        for (const auto & pc : pieces) memcpy(pc.dst, pc.src, pc.bytes);
+        return;
+    }
+    // split the concatenated byte range evenly; thread i copies [i*per, (i+1)*per)
+    const size_t per = (total + nt - 1) / nt;
+    auto work = [&](int i) {
+        size_t lo = (size_t)i * per, hi = std::min(total, lo + per), pos = 0;
+        for (const auto & pc : pieces) {
+            size_t a = std::max(lo, pos), b = std::min(hi, pos + pc.bytes);
+            if (a < b) memcpy((char *)pc.dst + (a - pos), (const char *)pc.src + (a - pos), b - a);
+            pos += pc.bytes;
+            if (pos >= hi) break;
+        }
+    };
+    std::vector<std::thread> th;
+    for (int i = 1; i < nt; i++) th.emplace_back(work, i);
+    work(0);
+    for (auto & x : th) x.join();
+}
+
+static cudaEvent_t phase_event(kvc_ctx * ctx) {
+    if (ctx->ph_used == ctx->ph_ev.size()) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        ctx->ph_ev.push_back(e);
+    }
+    return ctx->ph_ev[ctx->ph_used++];
+}
+
+void kvc_phase_collect(kvc_ctx * ctx, kvc_phase_ms * phase) {
+    double a = 0.0, b = 0.0;
+    for (size_t i = 0; i + 2 < ctx->ph_used; i += 3) {
+        float x = 0.0f, y = 0.0f;
+        cudaEventElapsedTime(&x, ctx->ph_ev[i], ctx->ph_ev[i + 1]);
+        cudaEventElapsedTime(&y, ctx->ph_ev[i + 1], ctx->ph_ev[i + 2]);
+        a += x;
+        b += y;
+    }
+    ctx->ph_used = 0;
+    if (phase) {
+        phase->scoring_ms = a;
+        phase->refit_ms = b;
+    }
+}
+
 static cudaEvent_t next_event(kvc_ctx * ctx, int * idx) {
     if (ctx->ev_used == ctx->ev_pool.size()) {
         cudaEvent_t e;
@@ -271,14 +349,14 @@ static unit_sizes sizes_of(const kvc_plan_unit & u, int H, int dv) {
     const int n = std::min(u.nq, u.t);
     (void)n;
     s.fs = al32((long long)H * u.nq * u.C) + al32((long long)(2 * H + 1) * u.C) + al32((long long)2 * H * u.nq) +
-           al32((long long)H * u.nq * dv) + al32((long long)H * u.nq * u.t);
+           al32((long long)H * u.nq * dv) + al32((long long)H * u.nq * u.t) + al32((long long)2 * H * u.nq);
     s.is = al32(u.t) + al32(4LL * u.C);
     s.gs = al32((long long)H * n * n) + al32((long long)H * n * dv);
     return s;
 }
 
 int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, int dv,
-                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase) {
+                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase, bool metric_partials) {
     if (n_jobs <= 0) return KVC_OK;
     cudaStream_t st = ctx->stream;
     if (p.use_sensitivity && H > 64) return KVC_ERR_SHAPE;
@@ -308,6 +386,30 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         KVC_CUDA(cudaMalloc(&ctx->d_outs, ctx->outs_cap * sizeof(kvc_layer_out)));
     }
     std::vector<kvc_layer_out> outs(n_jobs);
+    for (int l = 0; l < n_jobs; l++) {
+        jobs[l].out.n_chunks = (int)jobs[l].plan->units.size();
+        jobs[l].out.mpart = nullptr;
+    }
+    // per-chunk metric records for layers whose chunks all used the layer's queries
+    if (metric_partials) {
+        size_t mp_total = 0;
+        std::vector<size_t> mp_off(n_jobs, (size_t)-1);
+        for (int l = 0; l < n_jobs; l++) {
+            const kvc_plan & pl = *jobs[l].plan;
+            bool own_q = !pl.units.empty();
+            for (const kvc_plan_unit & pu : pl.units) own_q = own_q && pu.qmode == 0 && pu.nq == pl.nq_top;
+            if (!own_q) continue;
+            mp_off[l] = mp_total;
+            mp_total += (kvc_metric_partial_floats((int)pl.units.size(), H, pl.nq_top, dv) + 63) & ~(size_t)63;
+        }
+        if (mp_total) {
+            void * a8;
+            int rc8;
+            if ((rc8 = kvc_arena(ctx, 8, mp_total * 4, &a8))) return rc8;
+            for (int l = 0; l < n_jobs; l++)
+                if (mp_off[l] != (size_t)-1) jobs[l].out.mpart = (float *)a8 + mp_off[l];
+        }
+    }
     for (int l = 0; l < n_jobs; l++) outs[l] = jobs[l].out;
     KVC_CUDA(cudaMemcpyAsync(ctx->d_outs, outs.data(), n_jobs * sizeof(kvc_layer_out), cudaMemcpyHostToDevice, st));
     for (int l = 0; l < n_jobs; l++)
@@ -332,8 +434,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         if (mb > 0) budget = std::min(budget, mb << 20);
     }
 
-    if (phase) KVC_CUDA(cudaEventRecord(ctx->ev[0], st));
-    double score_ms = 0, refit_ms = 0;
+    if (phase) ctx->ph_used = 0;
 
     size_t pos = 0;
     while (pos < all.size()) {
@@ -366,11 +467,13 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             u.out_off = off;
             u.token_base = pu.start;
             u.active = 1;
+            u.chunk = all[pos].i;
             u.s_off = fs; fs += al32((long long)H * pu.nq * pu.C);
             u.imp_off = fs; fs += al32((long long)(2 * H + 1) * pu.C);
             u.row_off = fs; fs += al32((long long)2 * H * pu.nq);
             u.y_off = fs; fs += al32((long long)H * pu.nq * dv);
             u.x_off = fs; fs += al32((long long)H * pu.nq * pu.t);
+            u.xs_off = fs; fs += al32((long long)2 * H * pu.nq);
             u.w_off = w_base[u.layer] >= 0 ? w_base[u.layer] + pu.start : -1;
             u.sel_off = is; is += al32(pu.t);
             u.c_off = is; is += al32(4LL * pu.C);
@@ -409,7 +512,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         const int nu = (int)U.size();
         const kvc_unit * du = ctx->d_units;
 
-        if (phase) KVC_CUDA(cudaEventRecord(ctx->ev[1], st));
+        if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
         {
             kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1);
             if ((rc = kvc_launch_score(du, nu, max_nq, max_C, P, F, I, 0, st))) return rc;
@@ -423,7 +526,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             if ((rc = kvc_launch_aggregate(du, nu, P, F, st))) return rc;
             if ((rc = kvc_launch_select(du, nu, max_C, P, F, I, ctx->d_outs, st))) return rc;
         }
-        if (phase) KVC_CUDA(cudaEventRecord(ctx->ev[2], st));
+        if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
         {
             kvc_stage_timer tm(ctx, KVC_ST_PV, 1);
             if ((rc = kvc_launch_pv(du, nu, max_nq, P, F, st))) return rc;
@@ -450,46 +553,48 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
                 if ((rc = kvc_launch_lsq(du, nu, max_n, max_t, lsq_smem, P, F, G, ctx->d_outs, st))) return rc;
             }
         }
-        if (phase) {
-            KVC_CUDA(cudaEventRecord(ctx->ev[3], st));
-            KVC_CUDA(cudaEventSynchronize(ctx->ev[3]));
-            float a = 0, b = 0;
-            cudaEventElapsedTime(&a, ctx->ev[1], ctx->ev[2]);
-            cudaEventElapsedTime(&b, ctx->ev[2], ctx->ev[3]);
-            score_ms += a;
-            refit_ms += b;
+        if (metric_partials) {
+            kvc_stage_timer tm(ctx, KVC_ST_METRICS, 1);
+            if ((rc = kvc_launch_metric_partial(du, nu, P, F, ctx->d_outs, st))) return rc;
         }
-    }
-    if (phase) {
-        phase->scoring_ms = score_ms;
-        phase->refit_ms = refit_ms;
+        if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
     }
     return KVC_OK;
 }
 
-int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, int dv, kv_compact_stats * st) {
+int kvc_engine_metrics_launch(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, int dv, float * d_res) {
     const kvc_plan & pl = *job.plan;
-    const int pairs = kvc_metric_pairs(H, pl.nq_top);
     const int t = job.out.t_total;
+    int rc;
+    kvc_stage_timer tm(ctx, KVC_ST_METRICS, job.out.mpart ? 1 : 4);
+    if (job.out.mpart)              // merge the per-chunk records of the last run
+        return kvc_launch_metric_merge(job.out.mpart, job.out.n_chunks, H, pl.nq_top, dv, d_res, ctx->stream);
     const size_t nf = kvc_metric_scratch_floats(H, pl.nq_top, pl.T, t, dv);
     void * a4;
-    int rc;
     if ((rc = kvc_arena(ctx, 4, nf * 4, &a4))) return rc;
-    float * scratch = (float *)a4;
-    float * res = scratch + nf - 64 - (size_t)pairs * 3;
-    float isd = 1.0f / sqrtf((float)dk);
-    {
-        kvc_stage_timer tm(ctx, KVC_ST_METRICS, 1);
-        if ((rc = kvc_launch_metrics(job.K, job.V, job.Q, pl.T, pl.nq_top, H, dk, dv, job.out.sel, job.out.beta,
-                                     job.out.cv, t, isd, scratch, res, ctx->stream)))
-            return rc;
-    }
-    std::vector<float> h(pairs * 3);
-    KVC_CUDA(cudaMemcpyAsync(h.data(), res, pairs * 3 * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-    KVC_CUDA(cudaStreamSynchronize(ctx->stream));
+    const float isd = 1.0f / sqrtf((float)dk);
+    return kvc_launch_metrics(job.K, job.V, job.Q, pl.T, pl.nq_top, H, dk, dv, job.out.sel, job.out.beta,
+                              job.out.cv, t, isd, (float *)a4, d_res, ctx->stream);
+}
+
+int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, int dv, kv_compact_stats * st) {
+    const int pairs = kvc_metric_pairs(H, job.plan->nq_top);
+    void * a9;
+    int rc;
+    if ((rc = kvc_arena(ctx, 9, ((size_t)pairs * 3 + 64) * 4, &a9))) return rc;
+    if ((rc = kvc_engine_metrics_launch(ctx, job, H, dk, dv, (float *)a9))) return rc;
+    if ((rc = kvc_wait(ctx))) return rc;
+    std::vector<float> h((size_t)pairs * 3);
+    KVC_CUDA(cudaMemcpyAsync(h.data(), a9, h.size() * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    kvc_metrics_reduce(h.data(), pairs, st);
+    return KVC_OK;
+}
+
+// Average the per-pair (cosine, MSE, agreement) triples in the reference's
+// order (src/kv-compact-api.cpp:319-324).
+void kvc_metrics_reduce(const float * h, int pairs, kv_compact_stats * st) {
     if (getenv("KVC_DEBUG_METRICS"))
-        fprintf(stderr, "[kvc] metrics T=%d t=%d nq=%d pairs=%d first (cos,mse,agree)=(%g,%g,%g) scratch=%p\n",
-                pl.T, t, pl.nq_top, pairs, h[0], h[1], h[2], (void *)scratch);
+        fprintf(stderr, "[kvc] metrics pairs=%d first (cos,mse,agree)=(%g,%g,%g)\n", pairs, h[0], h[1], h[2]);
     float sc = 0.0f, sm = 0.0f;
     int agree = 0;
     for (int i = 0; i < pairs; i++) {
@@ -500,5 +605,4 @@ int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, 
     st->avg_cosine_sim = sc / (float)pairs;
     st->avg_mse = sm / (float)pairs;
     st->avg_agreement = (float)agree / (float)pairs;
-    return KVC_OK;
 }

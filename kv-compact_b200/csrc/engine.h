@@ -54,8 +54,8 @@ struct kvc_ctx {
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[4] = {};
     std::mutex mu;
-    void * arena[8] = {};
-    size_t arena_cap[8] = {};
+    void * arena[10] = {};
+    size_t arena_cap[10] = {};
     kvc_unit * d_units = nullptr;
     size_t units_cap = 0;
     kvc_layer_out * d_outs = nullptr;
@@ -68,7 +68,26 @@ struct kvc_ctx {
     std::vector<cudaEvent_t> ev_pool;            // reused timing events
     std::vector<std::pair<int, int>> pending;    // (stage, first event index) awaiting resolution
     size_t ev_used = 0;
+    // scoring/refit phase events of kvc_engine_run (three per batch), read by kvc_phase_collect
+    std::vector<cudaEvent_t> ph_ev;
+    size_t ph_used = 0;
+    // pinned host staging for device->host results (grow-only)
+    void * pinned = nullptr;
+    size_t pinned_cap = 0;
 };
+
+// Wait until all work queued on ctx->stream has finished, polling its
+// completion instead of sleeping in the driver: the calling thread resumes as
+// soon as the device is done (no wake-up latency between dependent steps).
+int kvc_wait(kvc_ctx * ctx);
+
+// Grow the pinned staging buffer to at least `bytes`.
+int kvc_pinned(kvc_ctx * ctx, size_t bytes, void ** out);
+
+// Host memcpy of many (dst, src, bytes) pieces spread over worker threads
+// (first-touch page faults of fresh malloc'd outputs dominate a single thread).
+struct kvc_copy_piece { void * dst; const void * src; size_t bytes; };
+void kvc_parallel_copy(const std::vector<kvc_copy_piece> & pieces);
 
 // Accumulate the elapsed times of the stages recorded since the last call
 // (waits for the last recorded event).
@@ -96,12 +115,27 @@ kvc_ctx * kvc_get_ctx(int * rc);
 int kvc_arena(kvc_ctx * ctx, int slot, size_t bytes, void ** out);
 
 // Run the compaction pipeline over all units of `jobs` on ctx->stream.
-// Outputs land in each job's `out` buffers. Stream-ordered; no host sync
-// unless `phase` is non-null (then the phases are timed with events).
+// Outputs land in each job's `out` buffers. Stream-ordered, no host sync. With
+// `phase`, the scoring and refit phases are bracketed by events; read them
+// with kvc_phase_collect once the stream has drained.
+// With `metric_partials`, layers whose chunks all scored the layer's own
+// queries also get per-chunk quality-metric records (jobs[l].out.mpart, in
+// arena slot 8, valid until the next run), which kvc_engine_metrics merges
+// instead of re-reading the whole cache.
 int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, int dv,
-                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase);
+                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase, bool metric_partials);
 
-// Quality metrics of one layer (device), summed on the host in reference order.
+// Scoring / refit milliseconds of the kvc_engine_run calls since the last
+// collection (the stream must have drained).
+void kvc_phase_collect(kvc_ctx * ctx, kvc_phase_ms * phase);
+
+// Quality metrics of one layer: launch the kernels that leave the
+// (cosine, MSE, agreement) triple of each of the kvc_metric_pairs() (head,
+// query) pairs in d_res (stream-ordered), then average the triples on the
+// host in reference order.
+int kvc_engine_metrics_launch(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, int dv, float * d_res);
+void kvc_metrics_reduce(const float * h_res, int pairs, kv_compact_stats * st);
+// Both, with a wait in between.
 int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, int dv,
                        kv_compact_stats * st);
 
@@ -127,6 +161,10 @@ size_t kvc_metric_scratch_floats(int H, int nq, int T, int t, int dv);
 int kvc_launch_metrics(const float * K, const float * V, const float * Q, int T, int nq, int H, int dk, int dv,
                        const int * sel, const float * beta, const float * cv, int t, float isd,
                        float * scratch, float * res, cudaStream_t st);
+size_t kvc_metric_partial_floats(int n_chunks, int H, int nq, int dv);
+int kvc_launch_metric_partial(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, const float * fs,
+                              const kvc_layer_out * d_outs, cudaStream_t st);
+int kvc_launch_metric_merge(const float * mpart, int n_chunks, int H, int nq, int dv, float * res, cudaStream_t st);
 int kvc_launch_gather_rows(const float * src, int src_stride, const int * idx, int rows, int n,
                            float * dst, int dst_stride, cudaStream_t st);
 int kvc_launch_cheap_q(const float * K, int T, int ek, int nq, float * Q, cudaStream_t st);

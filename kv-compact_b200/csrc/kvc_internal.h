@@ -63,6 +63,7 @@ struct kvc_unit {
     int out_off;          // first output slot of this unit within the layer
     int token_base;       // chunk start within the layer (added to indices)
     int active;           // refinement: 0 once the unit stopped swapping
+    int chunk;            // chunk index within its layer
     long long s_off;      // floats: S/A scratch, H blocks of nq*C
     long long imp_off;    // floats: (H+1) blocks of C (per head, then aggregated)
     long long row_off;    // floats: H blocks of nq (row max / row sum)
@@ -73,6 +74,7 @@ struct kvc_unit {
     long long sel_off;    // ints: t selected chunk-local positions
     long long w_off;      // floats: C R-KV weights (or -1: none)
     long long c_off;      // ints/floats: C per-candidate scratch (selection)
+    long long xs_off;     // floats: H blocks of 2*nq (row max, row sum of X before normalising)
 };
 
 struct kvc_layer_out {
@@ -80,6 +82,8 @@ struct kvc_layer_out {
     float * beta;         // [H][t_total]
     float * cv;           // [H][t_total][d_v]
     int t_total;
+    int n_chunks;         // units of this layer
+    float * mpart;        // per-chunk quality-metric partials, or null (metrics.cu)
 };
 
 struct kvc_params_dev {

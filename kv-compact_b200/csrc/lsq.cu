@@ -29,18 +29,22 @@
 #include <math.h>
 
 namespace {
-constexpr int GT = 32;
 constexpr int FN = 128;   // max unknowns of the shared-memory path (k_lsq_factor)
 constexpr int FC = 8;     // right-hand-side columns per warp in k_lsq_factor (16 warps)
 }
 
 enum { DG_GRAM = 0, DG_RHS = 1, DG_OUT = 2 };
-constexpr int DT = 64, DK = 16;
+constexpr int DT = 64, DK = 8;
 
-// One 64x64 tile of C = A B per CTA for the (unit, head, mode) problem.
-__global__ void __launch_bounds__(256) k_dgemm(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                               const float * __restrict__ fs, double * __restrict__ gs,
-                                               const kvc_layer_out * __restrict__ outs, int mode) {
+// One 64x64 tile of C = A B per CTA of 64 threads for the (unit, head, mode)
+// problem. Thread (ty, tx) of the 8x8 grid owns rows 2ty + 16i + {0,1} and
+// columns 2tx + 16j + {0,1} (i, j < 4): per k step it reads four double2 of
+// A and four of B from shared memory for 64 DFMA, and the double2 reads of a
+// quarter-warp cover 128 contiguous bytes. Shared tiles are double-buffered;
+// the next k slab is fetched into registers while the current one is used.
+__global__ void __launch_bounds__(64) k_dgemm(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                              const float * __restrict__ fs, double * __restrict__ gs,
+                                              const kvc_layer_out * __restrict__ outs, int mode) {
     const kvc_unit u = units[blockIdx.z];
     if (!u.active) return;
     const int h = blockIdx.y;
@@ -60,60 +64,79 @@ __global__ void __launch_bounds__(256) k_dgemm(const kvc_unit * __restrict__ uni
     const float * Y = fs + u.y_off + (long long)h * nq * dv;
     const double * Z = gs + u.z_off + (long long)h * n * dv;
 
-    __shared__ __align__(16) double As[DK][DT + 2];
-    __shared__ __align__(16) double Bs[DK][DT + 2];
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    __shared__ __align__(16) double As[2][DK][DT];
+    __shared__ __align__(16) double Bs[2][DK][DT];
+    const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
     const bool rows = (mode == DG_GRAM && dual);     // operands are rows of X (k contiguous)
-    double acc[4][4];
+    // thread tid fetches row/column tid of the tile for the DK k values of a
+    // slab (conflict-free shared stores; `rows` operands read DK consecutive
+    // floats of one row per thread, which L1 coalesces across the slab)
+    double ra[DK], rb[DK];
+    auto fetch = [&](int k0) {
 #pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
-    for (int k0 = 0; k0 < K; k0 += DK) {
-        for (int e = tid; e < DT * DK; e += 256) {
-            int mm, kk;
-            if (rows) { mm = e / DK; kk = e % DK; } else { kk = e / DT; mm = e % DT; }
-            const int m = m0 + mm, k = k0 + kk;
-            double v = 0.0;
-            if (m < M && k < K) v = rows ? (double)X[(long long)m * t + k] : (double)X[(long long)k * t + m];
-            As[kk][mm] = v;
-        }
-        for (int e = tid; e < DT * DK; e += 256) {
-            int nn, kk;
-            if (rows) { nn = e / DK; kk = e % DK; } else { kk = e / DT; nn = e % DT; }
-            const int c = n0 + nn, k = k0 + kk;
-            double v = 0.0;
-            if (c < N && k < K) {
-                if (mode == DG_GRAM) v = dual ? (double)X[(long long)c * t + k] : (double)X[(long long)k * t + c];
-                else if (mode == DG_RHS) v = (double)Y[(long long)k * dv + c];
-                else v = Z[(long long)k * dv + c];
+        for (int r = 0; r < DK; r++) {
+            const int m = m0 + tid, c = n0 + tid, k = k0 + r;
+            double va = 0.0, vb = 0.0;
+            if (k < K) {
+                if (m < M) va = rows ? (double)X[(long long)m * t + k] : (double)X[(long long)k * t + m];
+                if (c < N) {
+                    if (mode == DG_GRAM) vb = dual ? (double)X[(long long)c * t + k] : (double)X[(long long)k * t + c];
+                    else if (mode == DG_RHS) vb = (double)Y[(long long)k * dv + c];
+                    else vb = Z[(long long)k * dv + c];
+                }
             }
-            Bs[kk][nn] = v;
+            ra[r] = va;
+            rb[r] = vb;
         }
-        __syncthreads();
+    };
+    auto stash = [&](int buf) {
+#pragma unroll
+        for (int r = 0; r < DK; r++) {
+            As[buf][r][tid] = ra[r];
+            Bs[buf][r][tid] = rb[r];
+        }
+    };
+    double acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0;
+    fetch(0);
+    stash(0);
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = 0; k0 < K; k0 += DK) {
+        const bool more = k0 + DK < K;
+        if (more) fetch(k0 + DK);
 #pragma unroll
         for (int kk = 0; kk < DK; kk++) {
-            const double2 a01 = *reinterpret_cast<const double2 *>(&As[kk][ty * 4]);
-            const double2 a23 = *reinterpret_cast<const double2 *>(&As[kk][ty * 4 + 2]);
-            const double2 b01 = *reinterpret_cast<const double2 *>(&Bs[kk][tx * 4]);
-            const double2 b23 = *reinterpret_cast<const double2 *>(&Bs[kk][tx * 4 + 2]);
-            const double av[4] = {a01.x, a01.y, a23.x, a23.y};
-            const double bv[4] = {b01.x, b01.y, b23.x, b23.y};
+            double av[8], bv[8];
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int i = 0; i < 4; i++) {
+                const double2 a2 = *reinterpret_cast<const double2 *>(&As[buf][kk][2 * ty + 16 * i]);
+                const double2 b2 = *reinterpret_cast<const double2 *>(&Bs[buf][kk][2 * tx + 16 * i]);
+                av[2 * i] = a2.x; av[2 * i + 1] = a2.y;
+                bv[2 * i] = b2.x; bv[2 * i + 1] = b2.y;
+            }
 #pragma unroll
-                for (int j = 0; j < 4; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
         }
+        if (more) stash(buf ^ 1);
         __syncthreads();
+        buf ^= 1;
     }
+    auto row_of = [&](int i) { return m0 + 2 * ty + 16 * (i >> 1) + (i & 1); };
+    auto col_of = [&](int j) { return n0 + 2 * tx + 16 * (j >> 1) + (j & 1); };
     if (mode == DG_GRAM) {
         double * G = gs + u.g_off + (long long)h * n * n;
         const double ridge = (double)P.ridge;
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < 8; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int a = m0 + ty * 4 + i, b = n0 + tx * 4 + j;
+            for (int j = 0; j < 8; j++) {
+                const int a = row_of(i), b = col_of(j);
                 if (a < n && b < n && b <= a) {
                     const double v = acc[i][j] + (a == b ? ridge : 0.0);
                     G[(long long)a * n + b] = v;
@@ -123,20 +146,20 @@ __global__ void __launch_bounds__(256) k_dgemm(const kvc_unit * __restrict__ uni
     } else if (mode == DG_RHS) {
         double * R = gs + u.z_off + (long long)h * n * dv;
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < 8; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int a = m0 + ty * 4 + i, c = n0 + tx * 4 + j;
+            for (int j = 0; j < 8; j++) {
+                const int a = row_of(i), c = col_of(j);
                 if (a < M && c < N) R[(long long)a * dv + c] = acc[i][j];
             }
     } else {
         const kvc_layer_out lo = outs[u.layer];
         float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < 8; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int a = m0 + ty * 4 + i, c = n0 + tx * 4 + j;
+            for (int j = 0; j < 8; j++) {
+                const int a = row_of(i), c = col_of(j);
                 if (a < M && c < N) cv[(long long)a * dv + c] = (float)acc[i][j];
             }
     }
@@ -264,7 +287,8 @@ __global__ void __launch_bounds__(256) k_chol_solve(const kvc_unit * __restrict_
 // right-hand sides (Y for the dual, X^T Y from
 // k_dgemm for the primal) stay in registers: warp w owns columns [8w, 8w+8),
 // lane l rows l, l+32, l+64, l+96, and both triangular solves run
-// warp-synchronously with reciprocal pivots. The result Z (dual, consumed by
+// warp-synchronously with reciprocal pivots, the solved row of each step
+// broadcast to the warp through a shared-memory slot. The result Z (dual, consumed by
 // the OUT GEMM) or C_v (primal) is written to global memory.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restrict__ units, kvc_params_dev P,
@@ -289,28 +313,33 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
     __syncthreads();
 
     // Right-looking Cholesky, every step parallel over the whole CTA. Each
-    // thread derives the pivot reciprocal itself (no extra barrier); the
-    // scaled column goes to colk first so the rank-1 update never reads a
-    // column entry another thread is rewriting. Two barriers per column.
+    // thread derives the pivot and its reciprocal itself from one rsqrt (no
+    // extra barrier); the scaled column goes to colk first so the rank-1
+    // update never reads a column entry another thread is rewriting. The
+    // update of the lower trailing triangle gives row i to warp (i mod 16)
+    // and its columns to the lanes (contiguous, conflict-free). Two barriers
+    // per column.
     double * colk = rinv + FN;                     // [n]
+    const int nwarp = nthr >> 5;
     for (int k = 0; k < n; k++) {
         const double d = G[k * ld + k];
-        const double l = (d > 0.0 && isfinite(d)) ? sqrt(d) : 0.0;
-        const double il = (l > 0.0) ? 1.0 / l : 0.0;
+        const bool pos = d > 0.0 && isfinite(d);
+        const double il = pos ? rsqrt(d) : 0.0;
         for (int i = k + 1 + tid; i < n; i += nthr) colk[i] = G[i * ld + k] * il;
         if (tid == 0) rinv[k] = il;
         __syncthreads();                           // every thread has read the pivot
-        if (tid == 0) G[k * ld + k] = l;
-        const int m = n - k - 1;                   // trailing size
-        for (int e = tid; e < m * m; e += nthr) {
-            const int i = k + 1 + e / m, j = k + 1 + e % m;
-            if (j <= i) G[i * ld + j] -= colk[i] * colk[j];
+        if (tid == 0) G[k * ld + k] = pos ? d * il : 0.0;
+        for (int i = k + 1 + warp; i < n; i += nwarp) {
+            const double ci = colk[i];
+            double * Gi = G + i * ld;
+            for (int j = k + 1 + lane; j <= i; j += 32) Gi[j] -= ci * colk[j];
+            if (lane == 0) Gi[k] = ci;
         }
-        for (int i = k + 1 + tid; i < n; i += nthr) G[i * ld + k] = colk[i];
         __syncthreads();
     }
 
     const int c0 = warp * FC;
+    double * zb = colk + FN + warp * FC;           // this warp's broadcast slot
     double b[4][FC];
 #pragma unroll
     for (int s = 0; s < 4; s++) {
@@ -327,14 +356,23 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
         for (int kk = 0; kk < 32; kk++) {
             const int k = 32 * S + kk;
             if (k >= n) break;
-            const double il = rinv[k];
+            if (lane == kk) {
+                const double il = rinv[k];
+#pragma unroll
+                for (int c = 0; c < FC; c++) {
+                    b[S][c] *= il;
+                    zb[c] = b[S][c];
+                }
+            }
+            __syncwarp();
             double z[FC];
 #pragma unroll
-            for (int c = 0; c < FC; c++) z[c] = __shfl_sync(0xffffffffu, b[S][c] * il, kk);
-            if (lane == kk) {
-#pragma unroll
-                for (int c = 0; c < FC; c++) b[S][c] = z[c];
+            for (int c = 0; c < FC; c += 2) {
+                const double2 v = *reinterpret_cast<const double2 *>(zb + c);
+                z[c] = v.x;
+                z[c + 1] = v.y;
             }
+            __syncwarp();
 #pragma unroll
             for (int s2 = S; s2 < 4; s2++) {
                 const int r = lane + 32 * s2;
@@ -351,14 +389,23 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
         for (int kk = 31; kk >= 0; kk--) {
             const int k = 32 * S + kk;
             if (k >= n) continue;
-            const double il = rinv[k];
+            if (lane == kk) {
+                const double il = rinv[k];
+#pragma unroll
+                for (int c = 0; c < FC; c++) {
+                    b[S][c] *= il;
+                    zb[c] = b[S][c];
+                }
+            }
+            __syncwarp();
             double z[FC];
 #pragma unroll
-            for (int c = 0; c < FC; c++) z[c] = __shfl_sync(0xffffffffu, b[S][c] * il, kk);
-            if (lane == kk) {
-#pragma unroll
-                for (int c = 0; c < FC; c++) b[S][c] = z[c];
+            for (int c = 0; c < FC; c += 2) {
+                const double2 v = *reinterpret_cast<const double2 *>(zb + c);
+                z[c] = v.x;
+                z[c + 1] = v.y;
             }
+            __syncwarp();
 #pragma unroll
             for (int s2 = 0; s2 <= S; s2++) {
                 const int r = lane + 32 * s2;
@@ -405,16 +452,16 @@ int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, int max_t, 
                    const kvc_layer_out * d_outs, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
     const int tg = (max_n + DT - 1) / DT;
-    k_dgemm<<<dim3(tg * tg, P.H, n_units), 256, 0, st>>>(d_units, P, fs, gs, d_outs, DG_GRAM);
+    k_dgemm<<<dim3(tg * tg, P.H, n_units), 64, 0, st>>>(d_units, P, fs, gs, d_outs, DG_GRAM);
     KVC_CUDA(cudaGetLastError());
     const int to = ((max_t + DT - 1) / DT) * ((P.dv + DT - 1) / DT);
-    k_dgemm<<<dim3(to, P.H, n_units), 256, 0, st>>>(d_units, P, fs, gs, d_outs, DG_RHS);
+    k_dgemm<<<dim3(to, P.H, n_units), 64, 0, st>>>(d_units, P, fs, gs, d_outs, DG_RHS);
     KVC_CUDA(cudaGetLastError());
-    const size_t fast_smem = (size_t)(FN * (FN + 1) + 2 * FN) * sizeof(double);
+    const size_t fast_smem = (size_t)(FN * (FN + 1) + 2 * FN + 16 * FC) * sizeof(double);
     KVC_CUDA(cudaFuncSetAttribute(k_lsq_factor, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fast_smem));
     k_lsq_factor<<<dim3(n_units, P.H), 512, fast_smem, st>>>(d_units, P, fs, gs, d_outs);
     KVC_CUDA(cudaGetLastError());
-    k_dgemm<<<dim3(to, P.H, n_units), 256, 0, st>>>(d_units, P, fs, gs, d_outs, DG_OUT);
+    k_dgemm<<<dim3(to, P.H, n_units), 64, 0, st>>>(d_units, P, fs, gs, d_outs, DG_OUT);
     KVC_CUDA(cudaGetLastError());
     if (max_n > FN || P.dv > FN) {
         KVC_CUDA(cudaFuncSetAttribute(k_chol_solve, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));

@@ -12,6 +12,20 @@
 //   k_mpv       split-K weighted sum of value rows, partial [32 x d_v] per CTA
 //   k_mfinal    fixed-order reduction of the partials, cosine/MSE/argmax
 // The per-pair triples are summed on the host in the reference's order.
+//
+// Chunk-merged form (the pipeline already holds what the metric needs). When
+// every chunk of a layer scored the layer's own reference queries, chunk k
+// has, per (head, query): the row max m_k and exp-sum s_k of its scores, its
+// attention output Y_k = softmax_k(S) V_k, and the same three for the kept
+// keys, m'_k, s'_k and X_k C_v,k with X = softmax(S[:, sel] + beta). A softmax
+// over all T keys is the exp(m_k - M)-weighted merge of the chunk softmaxes
+// (M = max_k m_k), so
+//   orig = sum_k e^(m_k-M) (s_k + 1e-12) Y_k / (sum_k e^(m_k-M) s_k + 1e-12)
+// and comp likewise from the kept-key terms. k_metric_partial stores the
+// per-chunk terms after the last solve, k_metric_merge combines them in fp64
+// and finishes cosine/MSE/argmax like k_mfinal. This is the same quantity in a
+// different summation order (agreement with the direct form ~1e-6 relative);
+// it replaces a second pass over all T keys and values per layer.
 #include "kvc_internal.h"
 
 #include <math.h>
@@ -206,6 +220,29 @@ __global__ void __launch_bounds__(256) k_mpv(kvc_metric_args a) {
     }
 }
 
+// cosine, MSE and argmax agreement of one (head, query) pair from its two
+// d_v-vectors in shared memory (src/kv-compact-api.cpp:285-318); thread 0.
+__device__ void metric_triple(const float * oo, const float * co, int dv, float * res) {
+    float dp = 0.0f, no = 0.0f, nc = 0.0f, mse = 0.0f;
+    for (int d = 0; d < dv; d++) {
+        dp = __fadd_rn(dp, __fmul_rn(oo[d], co[d]));
+        no = __fadd_rn(no, __fmul_rn(oo[d], oo[d]));
+        nc = __fadd_rn(nc, __fmul_rn(co[d], co[d]));
+    }
+    for (int d = 0; d < dv; d++) {
+        float df = __fsub_rn(oo[d], co[d]);
+        mse = __fadd_rn(mse, __fmul_rn(df, df));
+    }
+    int ao = 0, ac = 0;
+    for (int d = 1; d < dv; d++) {
+        if (oo[d] > oo[ao]) ao = d;
+        if (co[d] > co[ac]) ac = d;
+    }
+    res[0] = __fdiv_rn(dp, __fadd_rn(sqrtf(__fmul_rn(no, nc)), 1e-8f));
+    res[1] = __fdiv_rn(mse, (float)dv);
+    res[2] = (ao == ac) ? 1.0f : 0.0f;
+}
+
 __global__ void __launch_bounds__(256) k_mfinal(kvc_metric_args a) {
     const int pair = blockIdx.x;
     const int h = pair / a.mq, q = pair % a.mq;
@@ -221,26 +258,140 @@ __global__ void __launch_bounds__(256) k_mfinal(kvc_metric_args a) {
         co[c] = sc;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float dp = 0.0f, no = 0.0f, nc = 0.0f, mse = 0.0f;
-        for (int d = 0; d < dv; d++) {
-            dp = __fadd_rn(dp, __fmul_rn(oo[d], co[d]));
-            no = __fadd_rn(no, __fmul_rn(oo[d], oo[d]));
-            nc = __fadd_rn(nc, __fmul_rn(co[d], co[d]));
-        }
-        for (int d = 0; d < dv; d++) {
-            float df = __fsub_rn(oo[d], co[d]);
-            mse = __fadd_rn(mse, __fmul_rn(df, df));
-        }
-        int ao = 0, ac = 0;
-        for (int d = 1; d < dv; d++) {
-            if (oo[d] > oo[ao]) ao = d;
-            if (co[d] > co[ac]) ac = d;
-        }
-        a.res[pair * 3 + 0] = __fdiv_rn(dp, __fadd_rn(sqrtf(__fmul_rn(no, nc)), 1e-8f));
-        a.res[pair * 3 + 1] = __fdiv_rn(mse, (float)dv);
-        a.res[pair * 3 + 2] = (ao == ac) ? 1.0f : 0.0f;
+    if (threadIdx.x == 0) metric_triple(oo, co, dv, a.res + pair * 3);
+}
+
+// ---- chunk-merged form ------------------------------------------------------
+// Record of one (chunk, head, query): m, s, m', s', Y[d_v], (X C_v)[d_v];
+// records are laid out [chunk][head][query].
+__host__ __device__ inline int metric_rec(int dv) { return 4 + 2 * dv; }
+
+// grid (units, min(H,4)): per-chunk terms of the first min(n_q,32) queries.
+// Runs for every unit of a layer that has a record buffer, active or not
+// (a unit that stopped refining keeps the X and C_v of its last solve).
+__global__ void __launch_bounds__(256) k_metric_partial(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                        const float * __restrict__ fs,
+                                                        const kvc_layer_out * __restrict__ outs) {
+    const kvc_unit u = units[blockIdx.x];
+    const kvc_layer_out lo = outs[u.layer];
+    if (lo.mpart == nullptr || u.qmode != 0) return;
+    const int h = blockIdx.y, nq = u.nq, t = u.t, dv = P.dv;
+    const int mh = P.H < 4 ? P.H : 4, mq = nq < MQ ? nq : MQ;
+    const int rec = metric_rec(dv);
+    float * out = lo.mpart + ((long long)u.chunk * mh + h) * mq * rec;
+    const float * rmax = fs + u.row_off + (long long)h * 2 * nq;
+    const float * xs = fs + u.xs_off + (long long)h * 2 * nq;
+    const float * Y = fs + u.y_off + (long long)h * nq * dv;
+    const float * X = fs + u.x_off + (long long)h * nq * t;
+    const float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
+    const int tid = threadIdx.x;
+    if (tid < mq) {
+        out[(long long)tid * rec + 0] = rmax[tid];
+        out[(long long)tid * rec + 1] = rmax[nq + tid];
+        out[(long long)tid * rec + 2] = xs[tid];
+        out[(long long)tid * rec + 3] = xs[nq + tid];
     }
+    for (int e = tid; e < mq * dv; e += 256) {
+        const int q = e / dv, c = e % dv;
+        out[(long long)q * rec + 4 + c] = Y[(long long)q * dv + c];
+    }
+    // (X C_v)[q][c]: 8 query groups x 32 column groups, 4 queries x 4 (or 8) columns a thread
+    __shared__ __align__(16) float Ws[PK][MQ];
+    __shared__ __align__(16) float Vs[PK][KVC_MAX_D];
+    const int qg = tid >> 5, cg = tid & 31;
+    const bool hi = dv > 128;
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int c = 0; c < 8; c++) acc[i][c] = 0.0f;
+    for (int j0 = 0; j0 < t; j0 += PK) {
+        for (int e = tid; e < MQ * PK; e += 256) {
+            const int qq = e / PK, jj = e % PK;
+            Ws[jj][qq] = (qq < mq && j0 + jj < t) ? X[(long long)qq * t + j0 + jj] : 0.0f;
+        }
+        for (int e = tid; e < PK * dv; e += 256) {
+            const int jj = e / dv, c = e % dv;
+            Vs[jj][c] = (j0 + jj < t) ? cv[(long long)(j0 + jj) * dv + c] : 0.0f;
+        }
+        __syncthreads();
+        const int jn = min(PK, t - j0);
+        for (int jj = 0; jj < jn; jj++) {
+            const float4 w4 = *reinterpret_cast<const float4 *>(&Ws[jj][4 * qg]);
+            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+            float vv[8];
+            if (4 * cg < dv) {
+                const float4 v4 = *reinterpret_cast<const float4 *>(&Vs[jj][4 * cg]);
+                vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
+            } else {
+                vv[0] = vv[1] = vv[2] = vv[3] = 0.0f;
+            }
+            if (hi && 128 + 4 * cg < dv) {
+                const float4 v4 = *reinterpret_cast<const float4 *>(&Vs[jj][128 + 4 * cg]);
+                vv[4] = v4.x; vv[5] = v4.y; vv[6] = v4.z; vv[7] = v4.w;
+            } else {
+                vv[4] = vv[5] = vv[6] = vv[7] = 0.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int c = 0; c < 8; c++) acc[i][c] = fmaf(wv[i], vv[c], acc[i][c]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int q = 4 * qg + i;
+        if (q >= mq) continue;
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const int col = (c < 4) ? 4 * cg + c : 128 + 4 * cg + (c - 4);
+            if (col < dv && (c < 4 || hi)) out[(long long)q * rec + 4 + dv + col] = acc[i][c];
+        }
+    }
+}
+
+// grid min(H,4) * min(n_q,32): merge the chunk records of one (head, query)
+// pair in fp64, then the metric triple.
+__global__ void __launch_bounds__(256) k_metric_merge(const float * __restrict__ mpart, int n_chunks, int mh,
+                                                      int mq, int dv, float * __restrict__ res) {
+    const int pair = blockIdx.x;
+    const int h = pair / mq, q = pair % mq;
+    const int rec = metric_rec(dv);
+    const long long cstride = (long long)mh * mq * rec;
+    const float * r0 = mpart + ((long long)h * mq + q) * rec;
+    __shared__ float red[2][32];
+    __shared__ float oo[KVC_MAX_D], co[KVC_MAX_D];
+    float M = -INFINITY, Mc = -INFINITY;
+    for (int k = threadIdx.x; k < n_chunks; k += blockDim.x) {
+        M = fmaxf(M, r0[k * cstride + 0]);
+        Mc = fmaxf(Mc, r0[k * cstride + 2]);
+    }
+    for (int o = 16; o; o >>= 1) {
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        Mc = fmaxf(Mc, __shfl_xor_sync(0xffffffffu, Mc, o));
+    }
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) { red[0][w] = M; red[1][w] = Mc; }
+    __syncthreads();
+    M = red[0][0];
+    Mc = red[1][0];
+    for (int i = 1; i < nw; i++) { M = fmaxf(M, red[0][i]); Mc = fmaxf(Mc, red[1][i]); }
+    for (int c = threadIdx.x; c < dv; c += blockDim.x) {
+        double no = 0.0, do_ = 0.0, nc = 0.0, dc = 0.0;
+        for (int k = 0; k < n_chunks; k++) {
+            const float * r = r0 + k * cstride;
+            const double eo = exp((double)r[0] - (double)M), ec = exp((double)r[2] - (double)Mc);
+            no += eo * ((double)r[1] + 1e-12) * (double)r[4 + c];
+            do_ += eo * (double)r[1];
+            nc += ec * ((double)r[3] + 1e-12) * (double)r[4 + dv + c];
+            dc += ec * (double)r[3];
+        }
+        oo[c] = (float)(no / (do_ + 1e-12));
+        co[c] = (float)(nc / (dc + 1e-12));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) metric_triple(oo, co, dv, res + pair * 3);
 }
 
 int kvc_metric_pairs(int H, int nq) { return (H < 4 ? H : 4) * (nq < 32 ? nq : 32); }
@@ -275,6 +426,28 @@ int kvc_launch_metrics(const float * K, const float * V, const float * Q, int T,
     k_mpv<<<dim3(a.nsplit, a.mh, 2), 256, 0, st>>>(a);
     KVC_CUDA(cudaGetLastError());
     k_mfinal<<<a.mh * a.mq, 128, 0, st>>>(a);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+size_t kvc_metric_partial_floats(int n_chunks, int H, int nq, int dv) {
+    const long long mh = H < 4 ? H : 4, mq = nq < 32 ? nq : 32;
+    return (size_t)(n_chunks * mh * mq * metric_rec(dv));
+}
+
+int kvc_launch_metric_partial(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, const float * fs,
+                              const kvc_layer_out * d_outs, cudaStream_t st) {
+    const int mh = P.H < 4 ? P.H : 4;
+    if (n_units <= 0 || mh <= 0) return KVC_OK;
+    k_metric_partial<<<dim3(n_units, mh), 256, 0, st>>>(d_units, P, fs, d_outs);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+int kvc_launch_metric_merge(const float * mpart, int n_chunks, int H, int nq, int dv, float * res, cudaStream_t st) {
+    const int mh = H < 4 ? H : 4, mq = nq < 32 ? nq : 32;
+    if (mh * mq <= 0 || n_chunks <= 0) return KVC_OK;
+    k_metric_merge<<<mh * mq, 256, 0, st>>>(mpart, n_chunks, mh, mq, dv, res);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }

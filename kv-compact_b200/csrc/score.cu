@@ -285,6 +285,11 @@ __global__ void __launch_bounds__(256) k_softmax_x(const kvc_unit * __restrict__
         for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
         float inv = __fdiv_rn(1.0f, __fadd_rn(s, 1e-12f));
         for (int j = lane; j < t; j += 32) row[j] = __fmul_rn(row[j], inv);
+        if (lane == 0 && u.xs_off > 0) {     // kept for the chunk-merged quality metrics
+            float * xs = fs + u.xs_off + (long long)h * 2 * nq;
+            xs[q] = m;
+            xs[nq + q] = s;
+        }
     }
     (void)beta_all;
 }
