@@ -8,8 +8,8 @@
 //   which is enough to reorder keys whose importances differ by less than
 //   that. So every S element here is accumulated in exactly the reference's
 //   order with explicitly rounded multiply and add: S is bit-identical to the
-//   reference's. The kernel is a 64x64-tile SIMT GEMM whose inner loop runs
-//   over d in order for 16 independent accumulators per thread.
+//   reference's. The kernel is a 128x128 (or 64x256) tile SIMT GEMM whose
+//   inner loop runs over d in order for 64 independent accumulators per thread.
 //   The same kernel builds S[:, sel] for the value refit (gather mode).
 //
 // Stage 2, k_softmax_importance: row softmax with max shift and
@@ -45,99 +45,142 @@ __device__ __forceinline__ const float * qrow_ptr(const kvc_unit & u, int q, int
     return u.K + (long long)cheap_pos(q, u.nq, u.C) * ek + (long long)h * dk;
 }
 
-// Load a [rows x SK] slab starting at column d0 from row pointers into
-// smem transposed ([SK][SB+4]); zero outside bounds.
-__device__ __forceinline__ void load_slab(float (*dst)[SB + 4], const float * const * rowp, int nrows,
-                                          int d0, int dk, bool vec_ok) {
-    int tid = threadIdx.x;
-    int r = tid >> 2;            // 0..63
-    int c = (tid & 3) * 8;       // 0,8,16,24
-    const float * p = (r < nrows) ? rowp[r] : nullptr;
-    float v[8];
-    if (p && vec_ok && d0 + c + 8 <= dk) {
-        float4 a = *reinterpret_cast<const float4 *>(p + d0 + c);
-        float4 b = *reinterpret_cast<const float4 *>(p + d0 + c + 4);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    } else {
+// Load rows [0, NR) of a [NR x SK] slab starting at column d0 into shared
+// memory transposed (dst[k][row]); zero outside bounds. 256 threads: thread
+// tid takes row tid % NR and SK*NR/256 consecutive columns of it in float4
+// pieces, so a warp's transposed stores hit 32 consecutive rows.
+template <int NR>
+__device__ __forceinline__ void load_rows(float (*dst)[NR + 4], const float * const * rowp, int d0, int dk,
+                                          bool vec_ok) {
+    constexpr int PER = SK * NR / ST;        // floats per thread: 16 (NR=128) or 32 (NR=256) or 8 (NR=64)
+    const int r = threadIdx.x % NR;
+    const int c0 = (threadIdx.x / NR) * PER;
+    const float * p = rowp[r];
 #pragma unroll
-        for (int i = 0; i < 8; i++) v[i] = (p && d0 + c + i < dk) ? p[d0 + c + i] : 0.0f;
+    for (int i = 0; i < PER; i += 4) {
+        const int c = c0 + i;
+        float v[4];
+        if (p && vec_ok && d0 + c + 4 <= dk) {
+            const float4 a = *reinterpret_cast<const float4 *>(p + d0 + c);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; e++) v[e] = (p && d0 + c + e < dk) ? p[d0 + c + e] : 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++) dst[c + e][r] = v[e];
     }
-#pragma unroll
-    for (int i = 0; i < 8; i++) dst[c + i][r] = v[i];
 }
 
 }  // namespace
 
 // mode 0: all C keys of the chunk -> S block (ld C)
 // mode 1: the t selected keys     -> X block (ld t), X later softmaxed in place
-__global__ void __launch_bounds__(ST) k_score(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                              float * __restrict__ fs, const int * __restrict__ is,
-                                              int mode) {
+// CTA tile TQ queries x TK keys (TQ*TK = 16384), 256 threads, 8x8 outputs per
+// thread: rows 4ty+{0..3} and TQ/2+4ty+{0..3}, columns 4tx+{0..3} and
+// TK/2+4tx+{0..3}, so both operand reads per d are two conflict-free
+// float4 loads for 64 multiply-add pairs. Each output is one accumulator
+// updated in d order: acc = fl(acc + fl(q*k)).
+template <int TQ>
+__global__ void __launch_bounds__(ST, 2) k_score(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                 float * __restrict__ fs, const int * __restrict__ is, int mode) {
+    constexpr int TK = 16384 / TQ;
+    constexpr int NTX = TK / 8;               // threads along keys
     const kvc_unit u = units[blockIdx.z];
     if (!u.active) return;
     const int h = blockIdx.y;
     const int ncols = mode == 0 ? u.C : u.t;
-    const int tq = (u.nq + SB - 1) / SB, tk = (ncols + SB - 1) / SB;
+    const int tq = (u.nq + TQ - 1) / TQ, tk = (ncols + TK - 1) / TK;
     if ((int)blockIdx.x >= tq * tk) return;
-    const int q0 = (blockIdx.x / tk) * SB, j0 = (blockIdx.x % tk) * SB;
+    const int q0 = (blockIdx.x / tk) * TQ, j0 = (blockIdx.x % tk) * TK;
     const int ek = P.H * P.dk, dk = P.dk;
     const int * sel = is + u.sel_off;
 
-    __shared__ float Qs[SK][SB + 4];
-    __shared__ float Ks[SK][SB + 4];
-    __shared__ const float * qp[SB];
-    __shared__ const float * kp[SB];
-    int tid = threadIdx.x;
-    if (tid < SB) {
-        int q = q0 + tid;
-        qp[tid] = q < u.nq ? qrow_ptr(u, q, h, ek, dk) : nullptr;
-    } else if (tid < 2 * SB) {
-        int j = j0 + tid - SB;
-        if (j < ncols) {
-            int key = mode == 0 ? j : sel[j];
-            kp[tid - SB] = u.K + (long long)key * ek + (long long)h * dk;
+    __shared__ __align__(16) float Qs[SK][TQ + 4];
+    __shared__ __align__(16) float Ks[SK][TK + 4];
+    __shared__ const float * qp[TQ];
+    __shared__ const float * kp[TK];
+    const int tid = threadIdx.x;
+    for (int i = tid; i < TQ + TK; i += ST) {
+        if (i < TQ) {
+            const int q = q0 + i;
+            qp[i] = q < u.nq ? qrow_ptr(u, q, h, ek, dk) : nullptr;
         } else {
-            kp[tid - SB] = nullptr;
+            const int j = j0 + i - TQ;
+            if (j < ncols) {
+                const int key = mode == 0 ? j : sel[j];
+                kp[i - TQ] = u.K + (long long)key * ek + (long long)h * dk;
+            } else {
+                kp[i - TQ] = nullptr;
+            }
         }
     }
     __syncthreads();
     const bool vec_ok = ((ek & 3) == 0) && ((dk & 3) == 0) &&
                         ((((uintptr_t)u.K) & 15) == 0) && (u.qmode == 1 || (((uintptr_t)u.Q) & 15) == 0);
-    const int ty = tid >> 4, tx = tid & 15;
-    float acc[4][4];
+    const int ty = tid / NTX, tx = tid % NTX;
+    float acc[8][8];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 8; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
 
     for (int d0 = 0; d0 < dk; d0 += SK) {
-        load_slab(Qs, qp, SB, d0, dk, vec_ok);
-        load_slab(Ks, kp, SB, d0, dk, vec_ok);
+        load_rows<TQ>(Qs, qp, d0, dk, vec_ok);
+        load_rows<TK>(Ks, kp, d0, dk, vec_ok);
         __syncthreads();
         const int kend = min(SK, dk - d0);
-        for (int kk = 0; kk < kend; kk++) {
-            float4 a = *reinterpret_cast<const float4 *>(&Qs[kk][ty * 4]);
-            float4 b = *reinterpret_cast<const float4 *>(&Ks[kk][tx * 4]);
-            float av[4] = {a.x, a.y, a.z, a.w};
-            float bv[4] = {b.x, b.y, b.z, b.w};
+        if (kend == SK) {
+#pragma unroll 4
+            for (int kk = 0; kk < SK; kk++) {
+                const float4 a0 = *reinterpret_cast<const float4 *>(&Qs[kk][4 * ty]);
+                const float4 a1 = *reinterpret_cast<const float4 *>(&Qs[kk][TQ / 2 + 4 * ty]);
+                const float4 b0 = *reinterpret_cast<const float4 *>(&Ks[kk][4 * tx]);
+                const float4 b1 = *reinterpret_cast<const float4 *>(&Ks[kk][TK / 2 + 4 * tx]);
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+                for (int i = 0; i < 8; i++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+                    for (int j = 0; j < 8; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+            }
+        } else {
+            for (int kk = 0; kk < kend; kk++) {
+                const float4 a0 = *reinterpret_cast<const float4 *>(&Qs[kk][4 * ty]);
+                const float4 a1 = *reinterpret_cast<const float4 *>(&Qs[kk][TQ / 2 + 4 * ty]);
+                const float4 b0 = *reinterpret_cast<const float4 *>(&Ks[kk][4 * tx]);
+                const float4 b1 = *reinterpret_cast<const float4 *>(&Ks[kk][TK / 2 + 4 * tx]);
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+            }
         }
         __syncthreads();
     }
     const int ld = ncols;
     float * out = fs + (mode == 0 ? u.s_off + (long long)h * u.nq * u.C : u.x_off + (long long)h * u.nq * u.t);
+    const bool vst = (ld & 3) == 0 && ((((uintptr_t)out) & 15) == 0);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int q = q0 + ty * 4 + i;
+    for (int i = 0; i < 8; i++) {
+        const int q = q0 + (i < 4 ? 4 * ty + i : TQ / 2 + 4 * ty + i - 4);
         if (q >= u.nq) continue;
+        float * row = out + (long long)q * ld;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            int c = j0 + tx * 4 + j;
-            if (c < ncols) out[(long long)q * ld + c] = __fmul_rn(acc[i][j], P.isd);
+        for (int hb = 0; hb < 2; hb++) {
+            const int c = j0 + hb * (TK / 2) + 4 * tx;
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) v[e] = __fmul_rn(acc[i][4 * hb + e], P.isd);
+            if (vst && c + 4 <= ncols) {
+                *reinterpret_cast<float4 *>(row + c) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    if (c + e < ncols) row[c + e] = v[e];
+            }
         }
     }
 }
@@ -297,9 +340,13 @@ __global__ void __launch_bounds__(256) k_softmax_x(const kvc_unit * __restrict__
 int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_cols,
                      const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
-    int tiles = ((max_nq + SB - 1) / SB) * ((max_cols + SB - 1) / SB);
-    dim3 grid(tiles, P.H, n_units);
-    k_score<<<grid, ST, 0, st>>>(d_units, P, fs, is, mode);
+    if (max_nq > 64) {
+        const int tiles = ((max_nq + 127) / 128) * ((max_cols + 127) / 128);
+        k_score<128><<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs, is, mode);
+    } else {
+        const int tiles = ((max_nq + 63) / 64) * ((max_cols + 255) / 256);
+        k_score<64><<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs, is, mode);
+    }
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
