@@ -181,6 +181,11 @@ int kvc_wait(kvc_ctx * ctx) {
     while ((e = cudaEventQuery(ctx->ev[0])) == cudaErrorNotReady) {
     }
     KVC_CUDA(e);
+    const int te = kvc_tc_take_error(ctx->stream);
+    if (te) {
+        fprintf(stderr, "[kvc] tensor-core kernel reported error %d (bounded wait ran out)\n", te);
+        return KVC_ERR_CUDA;
+    }
     return KVC_OK;
 }
 

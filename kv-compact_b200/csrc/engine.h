@@ -146,6 +146,9 @@ int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const k
                                   float * fs, cudaStream_t st);
 int kvc_launch_pv(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
                   float * fs, cudaStream_t st);
+bool kvc_pv_tc_ok(int max_nq, int dv);
+int kvc_launch_pv_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, cudaStream_t st);
+int kvc_tc_take_error(cudaStream_t st);
 int kvc_launch_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
                          float * fs, const kvc_layer_out * d_outs, cudaStream_t st);
 int kvc_launch_aggregate(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,

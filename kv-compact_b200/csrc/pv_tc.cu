@@ -1,0 +1,239 @@
+// pv_tc.cu — refit target Y_h = A_h V_h on the tcgen05 tensor cores.
+//
+// Y is the right-hand side of the value refit (src/kv-compact-api.cpp:754-783,
+// include/kv-compact-math.h:70-80): A = softmax weights of the chunk's
+// reference queries [n_q x C], V = the chunk's value rows of head h
+// [C x d_v]. The refit tolerates fp32-level rounding (never bit-compared), so
+// the product runs on the tensor cores in kind::tf32 with the 3xTF32 split:
+// every fp32 operand x ~= hi + lo, hi = x rounded to TF32, lo = (x - hi)
+// rounded to TF32 (both exactly representable for the tensor core), and
+//   A V ~= A_lo V_hi + A_hi V_lo + A_hi V_hi
+// accumulated in fp32 in TMEM — relative error ~1e-6, the same order as an
+// fp32 SIMT product.
+//
+// One CTA of 4 warps per (unit, head): M = 128 query rows (zero-padded),
+// N = d_v, K = the chunk's keys in stages of 16. Per stage every thread loads
+// its share of A (float4 along keys) and V (coalesced along d_v) into
+// registers, splits it and stores hi/lo tiles into shared memory in the
+// K-major no-swizzle canonical layout; thread 0 issues the six MMAs of the
+// stage and commits them to the stage buffer's mbarrier. Two stage buffers:
+// the loads of stage s+1 are in flight while the tensor core works on stage
+// s, and a buffer is rewritten only after its mbarrier reports that the MMAs
+// reading it completed. Every mbarrier wait is bounded; a wait that runs out
+// records an error (kvc_tc_take_error) and the CTA frees its TMEM and stops.
+#include "engine.h"
+#include "tc_sm100.h"
+
+namespace {
+constexpr int PV_M = 128;                    // tile rows (queries)
+constexpr int PV_KS = 16;                    // keys per stage
+constexpr int PV_LBO = 128;                  // bytes between 16-byte K chunks (one core matrix)
+constexpr int PV_SBO = (PV_KS / 4) * PV_LBO; // bytes between 8-row groups
+constexpr uint32_t PV_POLLS = 1u << 20;      // bound of every mbarrier wait
+
+__device__ int g_tc_error;                   // first error code of a tcgen05 kernel (0: none)
+
+template <int DV>
+constexpr uint32_t pv_stage_bytes() { return 2u * (PV_M / 8) * PV_SBO + 2u * (DV / 8) * PV_SBO; }
+template <int DV>
+constexpr uint32_t pv_tmem_cols() { return DV <= 32 ? 32 : (DV <= 64 ? 64 : (DV <= 128 ? 128 : 256)); }
+}  // namespace
+
+template <int DV>
+__global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                               float * __restrict__ fs) {
+    using namespace kvc_tc;
+    constexpr int NPB = DV / 32;                       // (row, k-quad) pairs of V per thread and stage
+    constexpr uint32_t A_BYTES = (PV_M / 8) * PV_SBO;  // one A tile (hi or lo)
+    constexpr uint32_t B_BYTES = (DV / 8) * PV_SBO;    // one B tile
+    constexpr uint32_t STAGE = pv_stage_bytes<DV>();
+    constexpr uint32_t NCOLS = pv_tmem_cols<DV>();
+    const kvc_unit u = units[blockIdx.x];
+    const int h = blockIdx.y;
+    const int ev = P.H * DV, nq = u.nq, C = u.C;
+    const float * A = fs + u.s_off + (long long)h * nq * C;
+    const float * V = u.V + (long long)h * DV;
+    float * Y = fs + u.y_off + (long long)h * nq * DV;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t mbar[2];
+    __shared__ uint32_t tmem_slot;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (warp == 0) tmem_alloc(&tmem_slot, NCOLS);
+    if (tid == 0) {
+        mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
+        mbar_init_fence();
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    constexpr uint32_t IDESC = idesc_tf32(PV_M, DV);
+    const int nst = (C + PV_KS - 1) / PV_KS;
+    const bool avec = ((C & 3) == 0) && ((((uintptr_t)A) & 15) == 0);
+
+    float4 ra[4];
+    float rb[NPB][4];
+    auto load = [&](int s) {
+        const int k0 = s * PV_KS;
+#pragma unroll
+        for (int it = 0; it < 4; it++) {               // A rows: a quarter-warp covers 8 rows of one k-quad
+            const int idx = it * 128 + tid;
+            const int r = ((idx >> 5) << 3) | (idx & 7), kq = (idx >> 3) & 3;
+            const int k = k0 + 4 * kq;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < nq) {
+                const float * p = A + (long long)r * C + k;
+                if (avec && k + 4 <= C) {
+                    v = *reinterpret_cast<const float4 *>(p);
+                } else {
+                    if (k + 0 < C) v.x = p[0];
+                    if (k + 1 < C) v.y = p[1];
+                    if (k + 2 < C) v.z = p[2];
+                    if (k + 3 < C) v.w = p[3];
+                }
+            }
+            ra[it] = v;
+        }
+#pragma unroll
+        for (int pb = 0; pb < NPB; pb++) {             // V: lanes run along d_v (coalesced rows)
+            const int idx = pb * 128 + tid;
+            const int n = idx % DV, kq = idx / DV;
+            const int k = k0 + 4 * kq;
+#pragma unroll
+            for (int e = 0; e < 4; e++) rb[pb][e] = (k + e < C) ? V[(long long)(k + e) * ev + n] : 0.0f;
+        }
+    };
+    auto store = [&](int b) {
+        uint8_t * base = smem + b * STAGE;
+#pragma unroll
+        for (int it = 0; it < 4; it++) {
+            const int idx = it * 128 + tid;
+            const int r = ((idx >> 5) << 3) | (idx & 7), kq = (idx >> 3) & 3;
+            const uint32_t off = (r >> 3) * PV_SBO + kq * PV_LBO + (r & 7) * 16;
+            float4 hi, lo;
+            tf32_split(ra[it].x, hi.x, lo.x);
+            tf32_split(ra[it].y, hi.y, lo.y);
+            tf32_split(ra[it].z, hi.z, lo.z);
+            tf32_split(ra[it].w, hi.w, lo.w);
+            *reinterpret_cast<float4 *>(base + off) = hi;
+            *reinterpret_cast<float4 *>(base + A_BYTES + off) = lo;
+        }
+#pragma unroll
+        for (int pb = 0; pb < NPB; pb++) {
+            const int idx = pb * 128 + tid;
+            const int n = idx % DV, kq = idx / DV;
+            const uint32_t off = (n >> 3) * PV_SBO + kq * PV_LBO + (n & 7) * 16;
+            float4 hi, lo;
+            tf32_split(rb[pb][0], hi.x, lo.x);
+            tf32_split(rb[pb][1], hi.y, lo.y);
+            tf32_split(rb[pb][2], hi.z, lo.z);
+            tf32_split(rb[pb][3], hi.w, lo.w);
+            *reinterpret_cast<float4 *>(base + 2 * A_BYTES + off) = hi;
+            *reinterpret_cast<float4 *>(base + 2 * A_BYTES + B_BYTES + off) = lo;
+        }
+    };
+
+    load(0);
+    int s = 0, err = 0;
+    for (; s < nst; s++) {
+        const int b = s & 1;
+        bool ok = true;
+        if (s >= 2) ok = mbar_wait(&mbar[b], (uint32_t)(((s - 2) >> 1) & 1), PV_POLLS);
+        store(b);
+        if (s + 1 < nst) load(s + 1);
+        fence_smem_to_async();
+        if (__syncthreads_or(!ok)) {          // every thread takes the same decision
+            err = 1;
+            break;
+        }
+        if (tid == 0) {
+            fence_after_sync();
+            const uint32_t sa = smem_u32(smem + b * STAGE);
+#pragma unroll
+            for (int ks = 0; ks < PV_KS / 8; ks++) {
+                const uint32_t ko = ks * 2 * PV_LBO;
+                const uint64_t ahi = sdesc(sa + ko, PV_LBO, PV_SBO);
+                const uint64_t alo = sdesc(sa + A_BYTES + ko, PV_LBO, PV_SBO);
+                const uint64_t bhi = sdesc(sa + 2 * A_BYTES + ko, PV_LBO, PV_SBO);
+                const uint64_t blo = sdesc(sa + 2 * A_BYTES + B_BYTES + ko, PV_LBO, PV_SBO);
+                mma_tf32(tmem, alo, bhi, IDESC, (s | ks) != 0);
+                mma_tf32(tmem, ahi, blo, IDESC, 1u);
+                mma_tf32(tmem, ahi, bhi, IDESC, 1u);
+            }
+            commit(&mbar[b]);
+        }
+    }
+    // the last issued commit covers every MMA of the CTA
+    const int last = s - 1;
+    bool ok = true;
+    if (last >= 0) ok = mbar_wait(&mbar[last & 1], (uint32_t)((last >> 1) & 1), PV_POLLS);
+    if (__syncthreads_or(!ok)) err |= 2;
+    fence_after_sync();
+    if (!err) {
+        const int q = 32 * warp + lane;
+#pragma unroll
+        for (int c0 = 0; c0 < DV; c0 += 16) {
+            float v[16];
+            tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+            if (q < nq) {
+                float4 * dst = reinterpret_cast<float4 *>(Y + (long long)q * DV + c0);
+#pragma unroll
+                for (int i = 0; i < 4; i++) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            }
+        }
+    } else if (tid == 0) {
+        atomicCAS(&g_tc_error, 0, 100 + err);
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tmem_free(tmem, NCOLS);
+}
+
+// Whether k_pv_tc handles this shape (else the SIMT k_pv does).
+bool kvc_pv_tc_ok(int max_nq, int dv) {
+    return max_nq <= PV_M && (dv == 64 || dv == 128 || dv == 256) && getenv("KVC_NO_TC") == nullptr;
+}
+
+int kvc_launch_pv_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    const dim3 grid(n_units, P.H);
+    switch (P.dv) {
+        case 64: {
+            const uint32_t sm = 2 * pv_stage_bytes<64>();
+            KVC_CUDA(cudaFuncSetAttribute(k_pv_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+            k_pv_tc<64><<<grid, 128, sm, st>>>(d_units, P, fs);
+            break;
+        }
+        case 128: {
+            const uint32_t sm = 2 * pv_stage_bytes<128>();
+            KVC_CUDA(cudaFuncSetAttribute(k_pv_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+            k_pv_tc<128><<<grid, 128, sm, st>>>(d_units, P, fs);
+            break;
+        }
+        case 256: {
+            const uint32_t sm = 2 * pv_stage_bytes<256>();
+            KVC_CUDA(cudaFuncSetAttribute(k_pv_tc<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+            k_pv_tc<256><<<grid, 128, sm, st>>>(d_units, P, fs);
+            break;
+        }
+        default:
+            return KVC_ERR_SHAPE;
+    }
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+// Read and clear the error code left by a tcgen05 kernel (stream must be idle).
+int kvc_tc_take_error(cudaStream_t st) {
+    int h = 0;
+    const int zero = 0;
+    if (cudaMemcpyFromSymbolAsync(&h, g_tc_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return -1;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return -1;
+    if (h && cudaMemcpyToSymbolAsync(g_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) == cudaSuccess)
+        cudaStreamSynchronize(st);
+    return h;
+}

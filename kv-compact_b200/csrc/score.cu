@@ -21,7 +21,7 @@
 // Stage 3, k_pv: Y_h = A_h V_h (math.h:70-80 via src/kv-compact-api.cpp:754-783),
 //   a 64x64-tile SIMT GEMM with fp32 FMA (Y only feeds the least-squares
 //   right-hand side, which is tolerance-checked).
-#include "kvc_internal.h"
+#include "engine.h"
 
 #include <math.h>
 
@@ -362,6 +362,7 @@ int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const k
 int kvc_launch_pv(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
                   float * fs, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
+    if (kvc_pv_tc_ok(max_nq, P.dv)) return kvc_launch_pv_tc(d_units, n_units, P, fs, st);
     int tiles = ((max_nq + SB - 1) / SB) * ((P.dv + SB - 1) / SB);
     k_pv<<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs);
     KVC_CUDA(cudaGetLastError());

@@ -1,0 +1,130 @@
+// tc_sm100.h — thin inline-PTX wrappers for the 5th-generation tensor cores
+// (tcgen05) and shared-memory mbarriers on sm_100a.
+//
+// Operand tiles live in shared memory in the K-major, no-swizzle canonical
+// layout: "core matrices" of 8 rows x 16 bytes stored contiguously (128 B),
+// consecutive 16-byte K chunks LBO bytes apart, consecutive 8-row groups SBO
+// bytes apart. The accumulator lives in tensor memory (TMEM): row i of a
+// 128-row tile is TMEM lane i, column j is TMEM column base + j, and warp w
+// of the CTA may read lanes [32w, 32w + 32).
+#pragma once
+
+#include <stdint.h>
+
+namespace kvc_tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void * p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// Shared-memory matrix descriptor (sm_100 format: version 1, no swizzle).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;                       // descriptor version for sm_100
+    return d;                                     // base offset 0, layout SWIZZLE_NONE
+}
+
+// Instruction descriptor of kind::tf32: fp32 accumulate, both operands
+// TF32 and K-major, M x N tile.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+    return (1u << 4)                      // D format F32
+         | (2u << 7)                      // A format TF32
+         | (2u << 10)                     // B format TF32
+         | ((uint32_t)(N >> 3) << 17)
+         | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n"
+        :: "r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// Arrive once on the mbarrier when all previously issued tcgen05.mma of this
+// thread have completed.
+__device__ __forceinline__ void commit(uint64_t * mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(smem_u32(mbar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t * slot, uint32_t ncols) {     // one full warp
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t ncols) {       // the allocating warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Generic-proxy shared-memory writes made visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_smem_to_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float * v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t * mbar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(mbar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Wait for the completion of the mbarrier phase with the given parity, at
+// most `limit` polls. Returns false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t * mbar, uint32_t parity, uint32_t limit) {
+    const uint32_t a = smem_u32(mbar);
+    for (uint32_t i = 0; i < limit; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// Round an fp32 value to the nearest TF32 value (10 explicit mantissa bits,
+// ties away from zero), returned as fp32 with the 13 low bits clear — the
+// tensor core then reads it exactly.
+__device__ __forceinline__ float tf32_round(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
+// Split x into a TF32 head and a TF32 tail: hi = round(x), lo = round(x - hi)
+// (x - hi is exact in fp32). |x - hi - lo| <= 2^-22 |x|, and rounding both
+// parts to nearest keeps the split unbiased (plain truncation would shrink
+// every product by up to 2^-20 in the same direction).
+__device__ __forceinline__ void tf32_split(float x, float & hi, float & lo) {
+    hi = tf32_round(x);
+    lo = tf32_round(__fsub_rn(x, hi));
+}
+
+}  // namespace kvc_tc

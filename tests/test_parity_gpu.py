@@ -139,5 +139,39 @@ def test_seam_refit_target(kvc):
         np.testing.assert_allclose(Y[h], ref, rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("nq,T,H,d", [(128, 1000, 2, 128), (37, 333, 3, 64), (128, 17, 1, 256), (64, 1280, 2, 128)])
+def test_refit_target_tensor_core(kvc, nq, T, H, d, monkeypatch):
+    """Y = W V on the tcgen05 path (3xTF32, d_v in {64, 128, 256}, n_q <= 128)
+    against an fp64 product and against the SIMT fp32 kernel (KVC_NO_TC=1).
+    SIMT: within 1e-5 of the largest |Y|. Tensor cores: within 3e-5 — their
+    fp32 accumulation truncates each partial sum toward zero, a bias that
+    grows with the number of accumulation steps (~1e-5 at 1,280 keys)."""
+    rng = np.random.default_rng(7 + nq + T)
+    W = [rng.random((nq, T)).astype(np.float32) for _ in range(H)]
+    W = [(w / w.sum(axis=1, keepdims=True)).astype(np.float32) for w in W]      # softmax-like rows
+    V = rng.standard_normal((T, H * d)).astype(np.float32)
+    FP = ctypes.POINTER(ctypes.c_float)
+
+    def run():
+        Y = [np.full((nq, d), np.nan, np.float32) for _ in range(H)]
+        wa = (FP * H)(*[w.ctypes.data_as(FP) for w in W])
+        ya = (FP * H)(*[y.ctypes.data_as(FP) for y in Y])
+        assert kvc["_lib"].kv_compact_cuda_refit_target_all_heads(wa, abi.fptr(V), ya, nq, T, H, d) == 0
+        return Y
+
+    Y_tc = run()
+    monkeypatch.setenv("KVC_NO_TC", "1")
+    Y_simt = run()
+    monkeypatch.delenv("KVC_NO_TC")
+    for h in range(H):
+        ref = W[h].astype(np.float64) @ V[:, h * d:(h + 1) * d].astype(np.float64)
+        scale = np.abs(ref).max()
+        err_tc = np.abs(Y_tc[h] - ref).max() / scale
+        err_simt = np.abs(Y_simt[h] - ref).max() / scale
+        print(f"\nY rel error: tensor cores {err_tc:.2e}, SIMT {err_simt:.2e}")
+        assert err_tc <= 3e-5, err_tc
+        assert err_simt <= 1e-5, err_simt
+
+
 def test_device_available(kvc):
     assert kvc["_lib"].kv_compact_cuda_available() == 1
