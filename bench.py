@@ -179,35 +179,100 @@ def run_reference(args, cfg, name):
     print(json.dumps(line))
 
 
-def roofline_entry(stage_times, cfg, n_steps, clocks, peaks):
-    """Roofline of the stage with the largest device time."""
+# DRAM bytes per (layer, KV head) of 100k tokens measured by ncu for the
+# kernels that can dominate a step (dram__bytes_read.sum + dram__bytes_write.sum
+# of one launch over one cfg4 layer, divided by its 8 heads; the captures are
+# summarised in profiles/). None where no capture of the current kernel exists.
+NCU_TRAFFIC_PER_LAYER_HEAD = {
+    "k_score": None,
+    "k_pv_tc": None,
+    "k_lsq_factor": None,
+}
+
+
+def chunk_plan(cfg):
+    """(C, t) of every chunk of one layer, as the library plans them
+    (auto chunk size 256 / ratio when more than 256 keys are kept)."""
+    T, r = cfg["T"], cfg["ratio"]
+    cs = T if int(T * r) <= 256 else max(64, int(256.0 / r))
+    out = []
+    for s0 in range(0, T, cs):
+        c = min(cs, T - s0)
+        out.append((c, max(1, int(c * r))))
+    return out
+
+
+def stage_rooflines(stage_times, cfg, n_steps, clocks, peaks):
+    """Roofline of every timed stage of the step: algorithmic work per launch
+    / measured average launch time, against the bound that applies."""
     T, H, d = cfg["T"], cfg["H"], cfg["d"]
     L = len(filtered_layers(cfg))
     nq = cfg["window"] * cfg["group"]
-    tokens = T * L
-    name, (ms, launches) = max(stage_times.items(), key=lambda kv: kv[1][0])
-    per_launch_ms = ms / max(launches, 1)
-    launches_per_step = launches / max(n_steps, 1)
+    units = chunk_plan(cfg)
+    t = sum(tu for _, tu in units)
     sm_max = (clocks.get("sm_max_mhz") or 1965.0) * 1e6
-    fp32_issue = 148 * 128 * sm_max            # fp32 instructions/s (one flop each without FMA)
-    if name == "score":
-        # 2*n_q*d flops per (token, head): separate multiply and add per term
-        work = 2.0 * nq * d * tokens * H / launches_per_step
-        return {"kernel": "k_score", "bound": "fp32_simt", "achieved": work / (per_launch_ms * 1e-3) / 1e12,
-                "peak": fp32_issue / 1e12, "unit": "TFLOP/s",
-                "peak_source": "derived: 148 SMs x 128 FP32 lanes x max SM clock, no-FMA issue rate "
-                               "(MEASURED_PEAKS.json has no FP32 figure)",
-                "frac": (work / (per_launch_ms * 1e-3)) / fp32_issue, "traffic": None,
-                "ms_per_launch": per_launch_ms}
-    if name == "refit_target":
-        work = 2.0 * nq * d * tokens * H / launches_per_step
-        peak = 2 * fp32_issue
-        return {"kernel": "k_pv", "bound": "fp32_simt", "achieved": work / (per_launch_ms * 1e-3) / 1e12,
-                "peak": peak / 1e12, "unit": "TFLOP/s", "peak_source": "derived FP32 FMA peak",
-                "frac": work / (per_launch_ms * 1e-3) / peak, "traffic": None, "ms_per_launch": per_launch_ms}
-    hbm = peaks.get("hbm_gbs", 6650.0)
-    return {"kernel": name, "bound": "unclassified", "achieved": None, "peak": hbm, "unit": "GB/s",
-            "frac": None, "traffic": None, "ms_per_launch": per_launch_ms}
+    hbm = peaks.get("hbm_gbs")
+    hbm_src = "MEASURED_PEAKS.json hbm_gbs (of measured)"
+    if hbm is None:
+        hbm, hbm_src = 6650.0, "fallback 6.65 TB/s (of fallback)"
+    hbm *= 1e9
+    fp32_issue = 148 * 128 * sm_max                 # FP32 instructions/s (separate multiply and add)
+    fp64 = 148 * 64 * 2 * sm_max                    # fp64 flop/s (DFMA)
+    fp64_src = "derived: 148 SMs x 64 FP64 lanes x 2 flop x max SM clock (no measured FP64 figure)"
+    bpe = {abi.KV_TYPE_Q8_0: 34 / 32, abi.KV_TYPE_Q4_0: 18 / 32, abi.KV_TYPE_Q4_1: 20 / 32, abi.KV_TYPE_F16: 2.0}
+    kb, vb = bpe[cfg["ktype"]], bpe[cfg["vtype"]]
+    # fp64 FMA of the LS refit per (unit, head): n = min(n_q, t_u) unknowns;
+    # Gram n(n+1)/2 x k (k = t_u in the dual form, n_q in the primal), Cholesky n^3/3,
+    # two triangular solves n^2 d, output t_u x d x n (dual) or right-hand side t_u x d x n_q (primal)
+    gram = fac = outp = 0.0
+    for _, tu in units:
+        n = min(nq, tu)
+        k = tu if nq < tu else nq
+        gram += n * (n + 1) / 2 * k
+        fac += n ** 3 / 3 + n * n * d
+        outp += tu * d * (n if nq < tu else nq)
+    per_lh = lambda x: x * H * L                  # noqa: E731
+    model = {
+        "score": ("k_score", "fp32_issue", "T instr/s", 2.0 * nq * d * T * H * L, fp32_issue,
+                  "derived: 148 SMs x 128 FP32 lanes x max SM clock; bit-exact scores need a separate "
+                  "rounded multiply and add per term (no FMA, no tensor cores)"),
+        "refit_target": ("k_pv_tc", "hbm", "GB/s", 4.0 * (nq + d) * T * H * L + 4.0 * nq * d * H * L * len(units),
+                         hbm, hbm_src),
+        "softmax_importance": ("k_softmax_importance", "hbm", "GB/s", 2 * 4.0 * nq * T * H * L, hbm, hbm_src),
+        "decode": ("k_decode_blocks", "hbm", "GB/s", (T * H * d * (kb + vb) + 8.0 * T * H * d) * L, hbm, hbm_src),
+        "requant": ("k_encode_gather + k_encode_heads", "hbm", "GB/s",
+                    (8.0 * t * H * d + t * H * d * (kb + vb)) * L, hbm, hbm_src),
+        "ls_gram": ("k_dgemm (Gram)", "fp64", "TFLOP/s", 2.0 * per_lh(gram), fp64, fp64_src),
+        "ls_factor": ("k_lsq_factor", "fp64", "TFLOP/s", 2.0 * per_lh(fac), fp64, fp64_src),
+        "ls_out": ("k_dgemm (C_v = X^T Z)", "fp64", "TFLOP/s", 2.0 * per_lh(outp), fp64, fp64_src),
+    }
+    out = {}
+    for name, (ms, launches) in stage_times.items():
+        if name not in model or not launches:
+            continue
+        kern, bound, unit, work, peak, src = model[name]
+        launches_per_step = launches / max(n_steps, 1)
+        per_launch_ms = ms / launches
+        achieved = work / launches_per_step / (per_launch_ms * 1e-3)
+        div = 1e9 if unit == "GB/s" else 1e12
+        out[name] = {"kernel": kern, "bound": bound, "achieved": achieved / div, "peak": peak / div, "unit": unit,
+                     "frac": achieved / peak, "ms_per_launch": per_launch_ms,
+                     "launches_per_step": launches_per_step, "work_per_step": work, "peak_source": src}
+    return out
+
+
+def roofline_entry(stage_times, cfg, n_steps, clocks, peaks):
+    """Roofline of the stage with the largest device time per step."""
+    rl = stage_rooflines(stage_times, cfg, n_steps, clocks, peaks)
+    if not rl:
+        return None, rl
+    name = max(rl, key=lambda k: stage_times[k][0])
+    e = dict(rl[name])
+    per_lh = NCU_TRAFFIC_PER_LAYER_HEAD.get(e["kernel"])
+    L = len(filtered_layers(cfg))
+    e["traffic"] = None if per_lh is None else per_lh * cfg["H"] * L / e["launches_per_step"]
+    e["traffic_unit"] = "bytes per launch (ncu DRAM read+write, scaled from a one-layer capture)"
+    return e, rl
 
 
 def run_kvc(args, cfg, name):
@@ -315,7 +380,7 @@ def run_kvc(args, cfg, name):
         peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
     except Exception:
         pass
-    roof = roofline_entry(stages, cfg, args.steps, clocks, peaks)
+    roof, roof_all = roofline_entry(stages, cfg, args.steps, clocks, peaks)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -327,6 +392,9 @@ def run_kvc(args, cfg, name):
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
             "clocks": clocks,
             "stage_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in stages.items() if v[1]},
+            "stage_roofline": {k: {"kernel": v["kernel"], "bound": v["bound"], "frac": round(v["frac"], 3),
+                                   "achieved": round(v["achieved"], 2), "unit": v["unit"]}
+                               for k, v in roof_all.items()},
         }
         print(json.dumps(line))
     if world > 1:

@@ -81,8 +81,9 @@ uint64_t kvc_launch_count(void);
 
 /* Per-stage device timing of the current device's library stream: copies the
  * accumulated milliseconds and launch counts of up to n stages (decode, score,
- * softmax+importance, select, refit target, beta, X build, LS solve,
- * refinement, metrics, requant) into the arrays (either may be NULL), resets
+ * softmax+importance, select, refit target, beta, X build, LS Gram products,
+ * refinement, metrics, requant, LS factor+solve, LS output product) into the
+ * arrays (either may be NULL), resets
  * them, and turns event timing on (enable != 0) or off. Returns the number of
  * stages, or a negative error code. */
 int kvc_profile(int enable, double * stage_ms, uint64_t * stage_launches, int n);

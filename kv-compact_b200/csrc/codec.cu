@@ -187,29 +187,56 @@ size_t kvc_host_encode_row(const float * src, int type, uint8_t * dst, int n) {
 }
 
 // ---- device kernels --------------------------------------------------------
-// Decode `rows` rows of n values. One thread per 32-value block (or per
-// element for F16/F32); consecutive threads touch consecutive bytes, and each
-// thread writes its 32 floats as 8 float4 stores.
+// Block formats run 8 threads per 32-value block, 4 values per thread, so a
+// warp covers 4 consecutive blocks: it reads their bytes contiguously and
+// writes (decode) or reads (encode) 512 contiguous bytes of floats. Every
+// value goes through the same arithmetic as decode_block / encode_block.
+
+// Values 4*sub .. 4*sub+3 of one block.
+__device__ __forceinline__ void decode_quad(const uint8_t * b, int type, int sub, float * o) {
+    const float d = kvc_h2f(ld16(b));
+    if (type == 8) {
+        const uint16_t w0 = ld16(b + 2 + 4 * sub), w1 = ld16(b + 4 + 4 * sub);
+        const int8_t q[4] = {(int8_t)(w0 & 0xFF), (int8_t)(w0 >> 8), (int8_t)(w1 & 0xFF), (int8_t)(w1 >> 8)};
+#pragma unroll
+        for (int i = 0; i < 4; i++) o[i] = kvc_mul(d, (float)q[i]);
+    } else if (type == 2) {
+        const uint16_t w = ld16(b + 2 + 2 * sub);
+        const uint8_t q0 = (uint8_t)(w & 0xFF), q1 = (uint8_t)(w >> 8);
+        o[0] = kvc_mul(d, kvc_sub((float)(q0 & 0xF), 8.0f));
+        o[1] = kvc_mul(d, kvc_sub((float)(q0 >> 4), 8.0f));
+        o[2] = kvc_mul(d, kvc_sub((float)(q1 & 0xF), 8.0f));
+        o[3] = kvc_mul(d, kvc_sub((float)(q1 >> 4), 8.0f));
+    } else {
+        const float m = kvc_h2f(ld16(b + 2));
+        const uint16_t w = ld16(b + 4 + 2 * sub);
+        const uint8_t q0 = (uint8_t)(w & 0xFF), q1 = (uint8_t)(w >> 8);
+        o[0] = kvc_add(kvc_mul(d, (float)(q0 & 0xF)), m);
+        o[1] = kvc_add(kvc_mul(d, (float)(q0 >> 4)), m);
+        o[2] = kvc_add(kvc_mul(d, (float)(q1 & 0xF)), m);
+        o[3] = kvc_add(kvc_mul(d, (float)(q1 >> 4)), m);
+    }
+}
+
 __global__ void k_decode_blocks(const uint8_t * __restrict__ src, size_t rb, int type,
                                 float * __restrict__ dst, int rows, int n) {
-    int nb = n / QK;
-    long long total = (long long)rows * nb;
-    int bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
+    const int nb = n / QK;
+    const long long total = (long long)rows * nb * 8;
+    const int bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
-        long long r = i / nb;
-        int b = (int)(i - r * nb);
-        const uint8_t * p = src + r * rb + (size_t)b * bb;
-        uint8_t raw[34];
-        for (int k = 0; k < bb; k++) raw[k] = __ldg(p + k);
-        float o[QK];
-        decode_block(raw, type, o);
-        float * q = dst + r * (long long)n + (long long)b * QK;
+        const long long gb = i >> 3;
+        const int sub = (int)(i & 7);
+        const long long r = gb / nb;
+        const int b = (int)(gb - r * nb);
+        float o[4];
+        decode_quad(src + r * rb + (size_t)b * bb, type, sub, o);
+        float * q = dst + r * (long long)n + (long long)b * QK + 4 * sub;
         if ((((uintptr_t)q) & 15) == 0) {
-            for (int k = 0; k < QK; k += 4)
-                *reinterpret_cast<float4 *>(q + k) = make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
+            *reinterpret_cast<float4 *>(q) = make_float4(o[0], o[1], o[2], o[3]);
         } else {
-            for (int k = 0; k < QK; k++) q[k] = o[k];
+#pragma unroll
+            for (int k = 0; k < 4; k++) q[k] = o[k];
         }
     }
 }
@@ -245,7 +272,7 @@ int kvc_launch_decode(const uint8_t * src, size_t rb, int type, float * dst, int
                       cudaStream_t st) {
     if (rows <= 0 || n <= 0) return KVC_OK;
     if (is_block(type)) {
-        long long work = (long long)rows * (n / QK);
+        long long work = (long long)rows * (n / QK) * 8;
         k_decode_blocks<<<grid_for(work, 256), 256, 0, st>>>(src, rb, type, dst, rows, n);
     } else {
         long long work = (long long)rows * n;
@@ -255,74 +282,156 @@ int kvc_launch_decode(const uint8_t * src, size_t rb, int type, float * dst, int
     return KVC_OK;
 }
 
+// Encode values 4*sub .. 4*sub+3 of a block held by the 8 lanes of an
+// aligned lane group (x: this lane's 4 values, x0: the block's first value);
+// the block statistics are combined with shuffles inside the group.
+__device__ __forceinline__ void encode_quad(const float * x, float x0, int type, int sub, uint8_t * o) {
+    if (type == 8 || type == 2) {
+        float amax = 0.0f;                               // NaN never wins: skipped as in encode_block
+#pragma unroll
+        for (int i = 0; i < 4; i++) { const float a = fabsf(x[i]); if (a > amax) amax = a; }
+#pragma unroll
+        for (int off = 4; off; off >>= 1) {
+            const float b = __shfl_xor_sync(0xffffffffu, amax, off, 8);
+            if (b > amax) amax = b;
+        }
+        const float lim = (type == 8) ? 127.0f : 7.0f;
+        const float d = kvc_div(amax, lim);
+        if (sub == 0) st16(o, kvc_f2h_trunc(d));
+        const float id = (d != 0.0f) ? kvc_div(lim, amax) : 0.0f;
+        if (type == 8) {
+            uint8_t q[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) q[i] = (uint8_t)(int8_t)kvc_roundf(kvc_clamp(kvc_mul(x[i], id), -128.0f, 127.0f));
+            st16(o + 2 + 4 * sub, (uint16_t)(q[0] | (q[1] << 8)));
+            st16(o + 4 + 4 * sub, (uint16_t)(q[2] | (q[3] << 8)));
+        } else {
+            uint8_t q[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                q[i] = (uint8_t)kvc_clamp(kvc_roundf(kvc_add(kvc_mul(x[i], id), 8.0f)), 0.0f, 15.0f);
+            st16(o + 2 + 2 * sub, (uint16_t)((q[0] | (q[1] << 4)) | ((q[2] | (q[3] << 4)) << 8)));
+        }
+    } else {
+        float lo = x0, hi = x0;                          // a NaN first value poisons both, as in encode_block
+#pragma unroll
+        for (int i = 0; i < 4; i++) { if (x[i] < lo) lo = x[i]; if (x[i] > hi) hi = x[i]; }
+#pragma unroll
+        for (int off = 4; off; off >>= 1) {
+            const float a = __shfl_xor_sync(0xffffffffu, lo, off, 8);
+            const float b = __shfl_xor_sync(0xffffffffu, hi, off, 8);
+            if (a < lo) lo = a;
+            if (b > hi) hi = b;
+        }
+        const float rng = kvc_sub(hi, lo);
+        const float d = kvc_div(rng, 15.0f);
+        if (sub == 0) {
+            st16(o, kvc_f2h_trunc(d));
+            st16(o + 2, kvc_f2h_trunc(lo));
+        }
+        const float id = (d != 0.0f) ? kvc_div(15.0f, rng) : 0.0f;
+        uint8_t q[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) q[i] = (uint8_t)kvc_clamp(kvc_roundf(kvc_mul(kvc_sub(x[i], lo), id)), 0.0f, 15.0f);
+        st16(o + 4 + 2 * sub, (uint16_t)((q[0] | (q[1] << 4)) | ((q[2] | (q[3] << 4)) << 8)));
+    }
+}
+
 __device__ __forceinline__ bool dev_is_block(int type) { return type == 8 || type == 2 || type == 3; }
+
+// Block formats: thread i handles quarter `i & 7` of block `i >> 3`. The
+// loop bound is rounded up to whole warps so every lane of a group reaches
+// the shuffles; lanes past the end only take part in them.
+__device__ __forceinline__ long long warp_round(long long n) { return (n + 31) & ~31LL; }
 
 // K_out rows: row j = src[rows_idx[j]] (fp32, stride src_stride) re-encoded.
 __global__ void k_encode_gather(const float * __restrict__ src, size_t stride,
                                 const int * __restrict__ idx, int rows, int n, int type,
                                 uint8_t * __restrict__ dst, size_t drb) {
-    bool blk = dev_is_block(type);
-    int per_row = blk ? n / QK : n;
-    long long total = (long long)rows * per_row;
+    if (dev_is_block(type)) {
+        const int nb = n / QK, bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
+        const long long total = (long long)rows * nb * 8;
+        for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < warp_round(total);
+             i += (long long)gridDim.x * blockDim.x) {
+            const bool live = i < total;
+            const long long gb = live ? (i >> 3) : 0;
+            const int sub = (int)(i & 7);
+            const long long r = gb / nb;
+            const int b = (int)(gb - r * nb);
+            const float * row = src + (idx ? (long long)idx[r] : r) * (long long)stride + (long long)b * QK;
+            float x[4];
+            if ((((uintptr_t)(row + 4 * sub)) & 15) == 0) {
+                const float4 v = *reinterpret_cast<const float4 *>(row + 4 * sub);
+                x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; k++) x[k] = row[4 * sub + k];
+            }
+            uint8_t tmp[34];
+            uint8_t * o = live ? dst + r * drb + (size_t)b * bb : tmp;
+            encode_quad(x, row[0], type, sub, o);
+        }
+        return;
+    }
+    const long long total = (long long)rows * n;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
-        long long r = i / per_row;
-        int b = (int)(i - r * per_row);
-        const float * row = src + (idx ? (long long)idx[r] : r) * (long long)stride;
+        const long long r = i / n;
+        const int e = (int)(i - r * n);
+        const float v = src[(idx ? (long long)idx[r] : r) * (long long)stride + e];
         uint8_t * o = dst + r * drb;
-        if (blk) {
-            float x[QK];
-            for (int k = 0; k < QK; k++) x[k] = row[b * QK + k];
-            uint8_t tmp[34];
-            encode_block(x, type, tmp);
-            int bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
-            for (int k = 0; k < bb; k++) o[(size_t)b * bb + k] = tmp[k];
-        } else if (type == 1) {
-            st16(o + 2 * b, kvc_f2h_trunc(row[b]));
-        } else {
-            float v = row[b];
-            memcpy(o + 4 * b, &v, 4);
-        }
+        if (type == 1) st16(o + 2 * e, kvc_f2h_trunc(v));
+        else memcpy(o + 4 * e, &v, 4);
     }
 }
 
 // V_out rows: row j, element e = h*dv + k comes from cv[h][j][k].
 __global__ void k_encode_heads(const float * __restrict__ cv, int H, int t, int dv, int type,
                                uint8_t * __restrict__ dst, size_t drb) {
-    int n = H * dv;
-    bool blk = dev_is_block(type);
-    int per_row = blk ? n / QK : n;
-    long long total = (long long)t * per_row;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        long long j = i / per_row;
-        int b = (int)(i - j * per_row);
-        uint8_t * o = dst + j * drb;
-        if (blk) {
-            float x[QK];
-            for (int k = 0; k < QK; k++) {
-                int e = b * QK + k;
-                int h = e / dv, c = e - h * dv;
+    const int n = H * dv;
+    if (dev_is_block(type)) {
+        const int nb = n / QK, bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
+        const long long total = (long long)t * nb * 8;
+        for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < warp_round(total);
+             i += (long long)gridDim.x * blockDim.x) {
+            const bool live = i < total;
+            const long long gb = live ? (i >> 3) : 0;
+            const int sub = (int)(i & 7);
+            const long long j = gb / nb;
+            const int b = (int)(gb - j * nb);
+            float x[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int e = b * QK + 4 * sub + k;
+                const int h = e / dv, c = e - h * dv;
                 x[k] = cv[((long long)h * t + j) * dv + c];
             }
+            const int e0 = b * QK, h0 = e0 / dv;
+            const float x0 = cv[((long long)h0 * t + j) * dv + (e0 - h0 * dv)];
             uint8_t tmp[34];
-            encode_block(x, type, tmp);
-            int bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
-            for (int k = 0; k < bb; k++) o[(size_t)b * bb + k] = tmp[k];
-        } else {
-            int h = b / dv, c = b - h * dv;
-            float v = cv[((long long)h * t + j) * dv + c];
-            if (type == 1) st16(o + 2 * b, kvc_f2h_trunc(v));
-            else memcpy(o + 4 * b, &v, 4);
+            uint8_t * o = live ? dst + j * drb + (size_t)b * bb : tmp;
+            encode_quad(x, x0, type, sub, o);
         }
+        return;
+    }
+    const long long total = (long long)t * n;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long j = i / n;
+        const int b = (int)(i - j * n);
+        const int h = b / dv, c = b - h * dv;
+        const float v = cv[((long long)h * t + j) * dv + c];
+        uint8_t * o = dst + j * drb;
+        if (type == 1) st16(o + 2 * b, kvc_f2h_trunc(v));
+        else memcpy(o + 4 * b, &v, 4);
     }
 }
 
 int kvc_launch_encode_gather(const float * src, size_t stride, const int * idx, int rows, int n,
                              int type, uint8_t * dst, size_t drb, cudaStream_t st) {
     if (rows <= 0) return KVC_OK;
-    long long work = (long long)rows * (is_block(type) ? n / QK : n);
-    k_encode_gather<<<grid_for(work, 128), 128, 0, st>>>(src, stride, idx, rows, n, type, dst, drb);
+    long long work = (long long)rows * (is_block(type) ? (n / QK) * 8 : n);
+    k_encode_gather<<<grid_for(work, 256), 256, 0, st>>>(src, stride, idx, rows, n, type, dst, drb);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
@@ -330,8 +439,8 @@ int kvc_launch_encode_gather(const float * src, size_t stride, const int * idx, 
 int kvc_launch_encode_heads(const float * cv, int H, int t, int dv, int type, uint8_t * dst,
                             size_t drb, cudaStream_t st) {
     if (t <= 0) return KVC_OK;
-    long long work = (long long)t * (is_block(type) ? (H * dv) / QK : H * dv);
-    k_encode_heads<<<grid_for(work, 128), 128, 0, st>>>(cv, H, t, dv, type, dst, drb);
+    long long work = (long long)t * (is_block(type) ? ((H * dv) / QK) * 8 : H * dv);
+    k_encode_heads<<<grid_for(work, 256), 256, 0, st>>>(cv, H, t, dv, type, dst, drb);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }

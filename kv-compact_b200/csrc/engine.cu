@@ -10,6 +10,7 @@
 #include "engine.h"
 
 #include <math.h>
+#include <limits.h>
 #include <stdlib.h>
 
 #include <algorithm>
@@ -427,16 +428,38 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     for (int l = 0; l < n_jobs; l++)
         for (int i = 0; i < (int)jobs[l].plan->units.size(); i++) all.push_back({l, i});
 
-    size_t free_b = 0, total_b = 0;
-    cudaMemGetInfo(&free_b, &total_b);
-    long long budget = (long long)std::min<size_t>((size_t)(free_b * 0.6), (size_t)48 << 30);
-    // bytes already held by our arenas can be reused
-    budget += (long long)(ctx->arena_cap[0] + ctx->arena_cap[1] + ctx->arena_cap[2]);
+    // Scratch of all units at once, counted as the batch loop below places it.
+    // When the arenas already hold that much (every call after the first on
+    // the same shapes) the whole job is one batch and the device is not
+    // queried: cudaMemGetInfo can take tens of milliseconds on a busy host.
+    long long fs_all = 0, is_all = 0, gs_all = 0;
+    for (int l = 0; l < n_jobs; l++)
+        if (jobs[l].rkv_w) fs_all += al32(jobs[l].plan->T);
+    for (const ref & rf : all) {
+        const kvc_plan_unit & pu = jobs[rf.l].plan->units[rf.i];
+        const unit_sizes us = sizes_of(pu, H, dv);
+        fs_all += us.fs;
+        is_all += us.is;
+        const int n = std::min(pu.nq, pu.t);
+        long long gper = (long long)n * n;
+        if (!p.skip_beta) gper = std::max<long long>(gper, (long long)kvc_nnls_doubles_per_head(pu.t, pu.nq));
+        gs_all += al32((long long)H * gper) + al32((long long)H * n * dv);
+    }
+    long long env_cap = 0;
     // KVC_SCRATCH_BUDGET_MB caps the scratch of one batch (testing the
     // multi-batch path, or leaving room for other users of the device)
-    if (const char * env = getenv("KVC_SCRATCH_BUDGET_MB")) {
-        long long mb = atoll(env);
-        if (mb > 0) budget = std::min(budget, mb << 20);
+    if (const char * env = getenv("KVC_SCRATCH_BUDGET_MB")) env_cap = atoll(env) << 20;
+    long long budget;
+    if (env_cap <= 0 && (size_t)fs_all * 4 <= ctx->arena_cap[0] && (size_t)is_all * 4 <= ctx->arena_cap[1] &&
+        (size_t)gs_all * 8 <= ctx->arena_cap[2]) {
+        budget = LLONG_MAX;
+    } else {
+        size_t free_b = 0, total_b = 0;
+        cudaMemGetInfo(&free_b, &total_b);
+        budget = (long long)std::min<size_t>((size_t)(free_b * 0.6), (size_t)48 << 30);
+        // bytes already held by our arenas can be reused
+        budget += (long long)(ctx->arena_cap[0] + ctx->arena_cap[1] + ctx->arena_cap[2]);
+        if (env_cap > 0) budget = std::min(budget, env_cap);
     }
 
     if (phase) ctx->ph_used = 0;
@@ -447,6 +470,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         std::vector<kvc_unit> U;
         long long fs = 0, is = 0, gs = 0;
         int max_nq = 1, max_C = 1, max_t = 1, max_n = 1;
+        bool any_primal = false, any_dual = false;
         size_t lsq_smem = 0;
         // R-KV weights live at the front of the float arena, per layer
         std::vector<long long> w_base(n_jobs, -1);
@@ -492,6 +516,8 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             max_C = std::max(max_C, pu.C);
             max_t = std::max(max_t, pu.t);
             max_n = std::max(max_n, n);
+            if (pu.nq < pu.t) any_dual = true;
+            else any_primal = true;
             lsq_smem = std::max(lsq_smem, kvc_lsq_smem_bytes(n));
             U.push_back(u);
             pos++;
@@ -554,8 +580,16 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
                 if ((rc = kvc_launch_softmax_x(du, nu, max_nq, P, F, ctx->d_outs, st))) return rc;
             }
             {
-                kvc_stage_timer tm(ctx, KVC_ST_LSQ, (max_n > 128 || dv > 128) ? 5 : 4);
-                if ((rc = kvc_launch_lsq(du, nu, max_n, max_t, lsq_smem, P, F, G, ctx->d_outs, st))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_LSQ, any_primal ? 2 : 1);
+                if ((rc = kvc_launch_lsq_gram(du, nu, max_n, max_t, P, F, G, ctx->d_outs, any_primal, st))) return rc;
+            }
+            {
+                kvc_stage_timer tm(ctx, KVC_ST_LSQ_FACTOR, (max_n > 128 || dv > 128) ? 2 : 1);
+                if ((rc = kvc_launch_lsq_factor(du, nu, max_n, lsq_smem, P, F, G, ctx->d_outs, st))) return rc;
+            }
+            {
+                kvc_stage_timer tm(ctx, KVC_ST_LSQ_OUT, any_dual ? 1 : 0);
+                if ((rc = kvc_launch_lsq_out(du, nu, max_t, P, F, G, ctx->d_outs, any_dual, st))) return rc;
             }
         }
         if (metric_partials) {

@@ -7,7 +7,7 @@
 #include "../../include/kv-compact-api.h"
 #include "kvc_internal.h"
 
-#define KVC_N_STAGES 11
+#define KVC_N_STAGES 13
 
 // One chunk of one layer as the reference's kv_compact would process it.
 struct kvc_plan_unit {
@@ -96,7 +96,8 @@ void kvc_resolve_timers(kvc_ctx * ctx);
 // Stage ids for per-stage timing.
 enum {
     KVC_ST_DECODE = 0, KVC_ST_SCORE, KVC_ST_SOFTMAX, KVC_ST_SELECT, KVC_ST_PV, KVC_ST_BETA,
-    KVC_ST_XBUILD, KVC_ST_LSQ, KVC_ST_REFINE, KVC_ST_METRICS, KVC_ST_REQUANT,
+    KVC_ST_XBUILD, KVC_ST_LSQ, KVC_ST_REFINE, KVC_ST_METRICS, KVC_ST_REQUANT, KVC_ST_LSQ_FACTOR,
+    KVC_ST_LSQ_OUT,
 };
 
 // Brackets one stage with events on ctx->stream when profiling is on.
@@ -156,9 +157,19 @@ int kvc_launch_aggregate(const kvc_unit * d_units, int n_units, const kvc_params
 int kvc_launch_select(const kvc_unit * d_units, int n_units, int max_C, const kvc_params_dev & P, float * fs,
                       int * is, const kvc_layer_out * d_outs, cudaStream_t st);
 size_t kvc_lsq_smem_bytes(int n);
-int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, int max_t, size_t smem_bytes,
-                   const kvc_params_dev & P, const float * fs, double * gs,
-                   const kvc_layer_out * d_outs, cudaStream_t st);
+// LS refit in three launches: Gram (and primal right-hand side) products,
+// factorisation + solves, output product (dual form).
+// `any_primal` / `any_dual`: whether some unit solves the primal (t <= n_q) /
+// dual form; launches only one form needs are skipped otherwise.
+int kvc_launch_lsq_gram(const kvc_unit * d_units, int n_units, int max_n, int max_t, const kvc_params_dev & P,
+                        const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_primal,
+                        cudaStream_t st);
+int kvc_launch_lsq_factor(const kvc_unit * d_units, int n_units, int max_n, size_t smem_bytes,
+                          const kvc_params_dev & P, const float * fs, double * gs,
+                          const kvc_layer_out * d_outs, cudaStream_t st);
+int kvc_launch_lsq_out(const kvc_unit * d_units, int n_units, int max_t, const kvc_params_dev & P,
+                       const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_dual,
+                       cudaStream_t st);
 int kvc_metric_pairs(int H, int nq);
 size_t kvc_metric_scratch_floats(int H, int nq, int T, int t, int dv);
 int kvc_launch_metrics(const float * K, const float * V, const float * Q, int T, int nq, int H, int dk, int dv,

@@ -10,41 +10,52 @@
 //   * n_q < t:  dual,    G = X X^T + ridge I  [n_q x n_q], C = X^T G^-1 Y
 //     (identical in exact arithmetic: (X^T X + rI)^-1 X^T = X^T (X X^T + rI)^-1)
 // with the Gram matrix accumulated in fp64 from the fp32 X (products of two
-// fp32 values are exact in fp64), an fp64 Cholesky factorisation and fp64
-// triangular solves. A non-positive pivot marks its unknown singular and
-// zeroes it, the counterpart of the reference skipping pivots below 1e-12.
+// fp32 values are exact in fp64) and an fp64 solve. A non-positive pivot marks
+// its unknown singular and zeroes it, the counterpart of the reference
+// skipping pivots below 1e-12.
 //
-// The dense products run as one batched fp64 GEMM launch each (k_dgemm,
-// 64x64 tiles, 4x4 per thread, over every (unit, head)):
+// The dense products run as one batched fp64 GEMM launch each (k_dgemm on
+// the fp64 tensor cores, 64x64 tiles, over every (unit, head)):
 //   GRAM  G = X X^T (dual) or X^T X (primal), + ridge on the diagonal
 //   RHS   R = X^T Y                          (primal only)
 //   OUT   C_v = X^T Z                        (dual only)
-// and the latency-bound part runs one CTA per (unit, head):
-//   k_lsq_factor  Cholesky of G in shared memory (n <= 128) + both triangular
-//                 solves for all d_v right-hand sides in registers; writes Z
-//                 (dual) or C_v (primal).
-//   k_chol_solve  the same for n > 128 or d_v > 128, G in global memory.
+// and the solve runs one CTA per (unit, head):
+//   k_lsq_factor  block Gauss-Jordan elimination of [G | R] (four unknowns
+//                 per step) in shared memory and registers (n <= 128,
+//                 d_v <= 128); writes Z (dual) or C_v (primal).
+//   k_chol_solve  Cholesky + triangular solves for n > 128 or d_v > 128,
+//                 G in global memory.
 #include "kvc_internal.h"
 
 #include <math.h>
 
 namespace {
 constexpr int FN = 128;   // max unknowns of the shared-memory path (k_lsq_factor)
-constexpr int FC = 8;     // right-hand-side columns per warp in k_lsq_factor (16 warps)
 }
 
 enum { DG_GRAM = 0, DG_RHS = 1, DG_OUT = 2 };
-constexpr int DT = 64, DK = 8;
+constexpr int DT = 64, DK = 16, DLD = 72;   // CTA tile, k slab, shared row stride (doubles)
 
-// One 64x64 tile of C = A B per CTA of 64 threads for the (unit, head, mode)
-// problem. Thread (ty, tx) of the 8x8 grid owns rows 2ty + 16i + {0,1} and
-// columns 2tx + 16j + {0,1} (i, j < 4): per k step it reads four double2 of
-// A and four of B from shared memory for 64 DFMA, and the double2 reads of a
-// quarter-warp cover 128 contiguous bytes. Shared tiles are double-buffered;
-// the next k slab is fetched into registers while the current one is used.
-__global__ void __launch_bounds__(64) k_dgemm(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                              const float * __restrict__ fs, double * __restrict__ gs,
-                                              const kvc_layer_out * __restrict__ outs, int mode) {
+// D (8x8) += A (8x4) B (4x8) on the fp64 tensor cores (warp-wide). Lane l
+// holds A[l/4][l%4], B[l%4][l/4] and D[l/4][2(l%4) + {0,1}].
+__device__ __forceinline__ void dmma(double (&c)[2], double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(c[0]), "+d"(c[1]) : "d"(a), "d"(b));
+}
+
+// One 64x64 tile of C = A B per CTA of 4 warps for the (unit, head, mode)
+// problem, on the fp64 tensor cores (mma m8n8k4): each warp owns a 32x32
+// quarter = 4x4 accumulator tiles, and per k step of 4 loads four A and four
+// B fragments from shared memory for 16 MMAs. Operands are staged as
+// [k][row] slabs of 16 k (row stride 72 doubles: fragment loads hit every
+// bank twice, the minimum for 32 doubles), double-buffered, the next slab
+// fetched into registers while the current one is multiplied. Thread t
+// fetches row t % 64 of the slab for 8 consecutive k, so the shared stores of
+// a warp are 32 consecutive doubles and the global loads run along the
+// source's contiguous dimension or stay within one 32-byte sector per row.
+__global__ void __launch_bounds__(128) k_dgemm(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                               const float * __restrict__ fs, double * __restrict__ gs,
+                                               const kvc_layer_out * __restrict__ outs, int mode) {
     const kvc_unit u = units[blockIdx.z];
     if (!u.active) return;
     const int h = blockIdx.y;
@@ -64,18 +75,18 @@ __global__ void __launch_bounds__(64) k_dgemm(const kvc_unit * __restrict__ unit
     const float * Y = fs + u.y_off + (long long)h * nq * dv;
     const double * Z = gs + u.z_off + (long long)h * n * dv;
 
-    __shared__ __align__(16) double As[2][DK][DT];
-    __shared__ __align__(16) double Bs[2][DK][DT];
-    const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
-    const bool rows = (mode == DG_GRAM && dual);     // operands are rows of X (k contiguous)
-    // thread tid fetches row/column tid of the tile for the DK k values of a
-    // slab (conflict-free shared stores; `rows` operands read DK consecutive
-    // floats of one row per thread, which L1 coalesces across the slab)
-    double ra[DK], rb[DK];
+    __shared__ __align__(16) double As[2][DK][DLD];
+    __shared__ __align__(16) double Bs[2][DK][DLD];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
+    const int fr = tid & 63, fk = (tid >> 6) * 8;       // fetch: row fr, k fk..fk+7 of the slab
+    const bool rows = (mode == DG_GRAM && dual);       // operands are rows of X (k contiguous)
+    double ra[8], rb[8];
     auto fetch = [&](int k0) {
+        const int m = m0 + fr, c = n0 + fr;
 #pragma unroll
-        for (int r = 0; r < DK; r++) {
-            const int m = m0 + tid, c = n0 + tid, k = k0 + r;
+        for (int e = 0; e < 8; e++) {
+            const int k = k0 + fk + e;
             double va = 0.0, vb = 0.0;
             if (k < K) {
                 if (m < M) va = rows ? (double)X[(long long)m * t + k] : (double)X[(long long)k * t + m];
@@ -85,83 +96,86 @@ __global__ void __launch_bounds__(64) k_dgemm(const kvc_unit * __restrict__ unit
                     else vb = Z[(long long)k * dv + c];
                 }
             }
-            ra[r] = va;
-            rb[r] = vb;
+            ra[e] = va;
+            rb[e] = vb;
         }
     };
     auto stash = [&](int buf) {
 #pragma unroll
-        for (int r = 0; r < DK; r++) {
-            As[buf][r][tid] = ra[r];
-            Bs[buf][r][tid] = rb[r];
+        for (int e = 0; e < 8; e++) {
+            As[buf][fk + e][fr] = ra[e];
+            Bs[buf][fk + e][fr] = rb[e];
         }
     };
-    double acc[8][8];
+    double acc[4][4][2];
 #pragma unroll
-    for (int i = 0; i < 8; i++)
+    for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = 0.0;
+        for (int j = 0; j < 4; j++) acc[i][j][0] = acc[i][j][1] = 0.0;
     fetch(0);
     stash(0);
     __syncthreads();
     int buf = 0;
+    const int fm = lane >> 2, fq = lane & 3;
     for (int k0 = 0; k0 < K; k0 += DK) {
         const bool more = k0 + DK < K;
         if (more) fetch(k0 + DK);
 #pragma unroll
-        for (int kk = 0; kk < DK; kk++) {
-            double av[8], bv[8];
+        for (int kk = 0; kk < DK; kk += 4) {
+            double a[4], b[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const double2 a2 = *reinterpret_cast<const double2 *>(&As[buf][kk][2 * ty + 16 * i]);
-                const double2 b2 = *reinterpret_cast<const double2 *>(&Bs[buf][kk][2 * tx + 16 * i]);
-                av[2 * i] = a2.x; av[2 * i + 1] = a2.y;
-                bv[2 * i] = b2.x; bv[2 * i + 1] = b2.y;
+                a[i] = As[buf][kk + fq][wm + 8 * i + fm];
+                b[i] = Bs[buf][kk + fq][wn + 8 * i + fm];
             }
 #pragma unroll
-            for (int i = 0; i < 8; i++)
+            for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 8; j++) acc[i][j] = fma(av[i], bv[j], acc[i][j]);
+                for (int j = 0; j < 4; j++) dmma(acc[i][j], a[i], b[j]);
         }
         if (more) stash(buf ^ 1);
         __syncthreads();
         buf ^= 1;
     }
-    auto row_of = [&](int i) { return m0 + 2 * ty + 16 * (i >> 1) + (i & 1); };
-    auto col_of = [&](int j) { return n0 + 2 * tx + 16 * (j >> 1) + (j & 1); };
     if (mode == DG_GRAM) {
         double * G = gs + u.g_off + (long long)h * n * n;
         const double ridge = (double)P.ridge;
 #pragma unroll
-        for (int i = 0; i < 8; i++)
+        for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const int a = row_of(i), b = col_of(j);
-                if (a < n && b < n && b <= a) {
-                    const double v = acc[i][j] + (a == b ? ridge : 0.0);
-                    G[(long long)a * n + b] = v;
-                    G[(long long)b * n + a] = v;
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int v = 0; v < 2; v++) {
+                    const int a = m0 + wm + 8 * i + fm, b = n0 + wn + 8 * j + 2 * fq + v;
+                    if (a < n && b < n && b <= a) {
+                        const double x = acc[i][j][v] + (a == b ? ridge : 0.0);
+                        G[(long long)a * n + b] = x;
+                        G[(long long)b * n + a] = x;
+                    }
                 }
-            }
     } else if (mode == DG_RHS) {
         double * R = gs + u.z_off + (long long)h * n * dv;
 #pragma unroll
-        for (int i = 0; i < 8; i++)
+        for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const int a = row_of(i), c = col_of(j);
-                if (a < M && c < N) R[(long long)a * dv + c] = acc[i][j];
-            }
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int v = 0; v < 2; v++) {
+                    const int a = m0 + wm + 8 * i + fm, c = n0 + wn + 8 * j + 2 * fq + v;
+                    if (a < M && c < N) R[(long long)a * dv + c] = acc[i][j][v];
+                }
     } else {
         const kvc_layer_out lo = outs[u.layer];
         float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
 #pragma unroll
-        for (int i = 0; i < 8; i++)
+        for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const int a = row_of(i), c = col_of(j);
-                if (a < M && c < N) cv[(long long)a * dv + c] = (float)acc[i][j];
-            }
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int v = 0; v < 2; v++) {
+                    const int a = m0 + wm + 8 * i + fm, c = n0 + wn + 8 * j + 2 * fq + v;
+                    if (a < M && c < N) cv[(long long)a * dv + c] = (float)acc[i][j][v];
+                }
     }
 }
 
@@ -280,16 +294,27 @@ __global__ void __launch_bounds__(256) k_chol_solve(const kvc_unit * __restrict_
 
 
 // ---------------------------------------------------------------------------
-// Factor + solve, n = min(n_q, t) <= 128 and d_v <= 128, one CTA of 16 warps
-// per (unit, head). G (fp64, from k_dgemm) is copied to shared memory with an
-// odd row stride so column walks hit distinct banks, and factorised with a
-// right-looking Cholesky whose steps are spread over all 16 warps. The
-// right-hand sides (Y for the dual, X^T Y from
-// k_dgemm for the primal) stay in registers: warp w owns columns [8w, 8w+8),
-// lane l rows l, l+32, l+64, l+96, and both triangular solves run
-// warp-synchronously with reciprocal pivots, the solved row of each step
-// broadcast to the warp through a shared-memory slot. The result Z (dual, consumed by
-// the OUT GEMM) or C_v (primal) is written to global memory.
+// Solve, n = min(n_q, t) <= 128 and d_v <= 128, one CTA of 16 warps per
+// (unit, head): block Gauss-Jordan elimination of [G | R] in diagonal order
+// without pivoting (R = Y for the dual, X^T Y from k_dgemm for the primal),
+// four unknowns per step. G is symmetric positive definite (Gram matrix +
+// ridge), for which elimination in diagonal order is stable.
+// Step k (unknowns k..k+3): every thread inverts the 4x4 pivot block P by
+// Gauss-Jordan in registers; a pivot that is not positive and finite marks its
+// unknown singular (its row of P^-1 is zeroed, so it drops out and ends at
+// zero — the reference skips pivots below 1e-12). The pivot rows become
+// P^-1 [pivot rows of G and R]; every other row i loses G[i][k..k+3] x (the new
+// pivot rows). Only G's columns right of the block are carried (eliminated
+// columns are implicitly unit vectors); all d_v columns of R are. After the
+// last step R holds G^-1 R. Each step is a rank-4 update that is parallel
+// over all rows and columns, with two barriers; there are no triangular
+// dependency chains.
+// G sits in shared memory (row stride n + 1); R in registers: thread (ty, tx)
+// of the 32 x 16 grid owns rows 4ty..4ty+3 — so the four pivot rows of a step
+// belong to one row of threads — and columns 2tx + 32p + {0, 1} (p < 4),
+// which makes the reads of the new pivot rows conflict-free double2 loads.
+// The result Z (dual, consumed by the OUT product) or C_v (primal) is written
+// to global memory.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restrict__ units, kvc_params_dev P,
                                                        const float * __restrict__ fs, double * __restrict__ gs,
@@ -307,135 +332,163 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
 
     extern __shared__ double G[];
     const int ld = n + 1;
-    double * rinv = G + n * ld;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
-    for (int e = tid; e < n * n; e += nthr) G[(e / n) * ld + (e % n)] = Gg[e];
+    double * PR = G + FN * (FN + 1);           // [4][FN] new pivot rows of G
+    double * RR = PR + 4 * FN;                 // [4][FN] new pivot rows of R
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ty = tid >> 4, tx = tid & 15;
+    for (int e = tid; e < n * n; e += 512) G[(e / n) * ld + (e % n)] = Gg[e];
+    double r[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int row = 4 * ty + i;
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const int col = 2 * tx + 32 * (c >> 1) + (c & 1);
+            double v = 0.0;
+            if (row < n && col < dv) v = dual ? (double)Y[(long long)row * dv + col] : Zg[(long long)row * dv + col];
+            r[i][c] = v;
+        }
+    }
     __syncthreads();
 
-    // Right-looking Cholesky, every step parallel over the whole CTA. Each
-    // thread derives the pivot and its reciprocal itself from one rsqrt (no
-    // extra barrier); the scaled column goes to colk first so the rank-1
-    // update never reads a column entry another thread is rewriting. The
-    // update of the lower trailing triangle gives row i to warp (i mod 16)
-    // and its columns to the lanes (contiguous, conflict-free). Two barriers
-    // per column.
-    double * colk = rinv + FN;                     // [n]
-    const int nwarp = nthr >> 5;
-    for (int k = 0; k < n; k++) {
-        const double d = G[k * ld + k];
-        const bool pos = d > 0.0 && isfinite(d);
-        const double il = pos ? rsqrt(d) : 0.0;
-        for (int i = k + 1 + tid; i < n; i += nthr) colk[i] = G[i * ld + k] * il;
-        if (tid == 0) rinv[k] = il;
-        __syncthreads();                           // every thread has read the pivot
-        if (tid == 0) G[k * ld + k] = pos ? d * il : 0.0;
-        for (int i = k + 1 + warp; i < n; i += nwarp) {
-            const double ci = colk[i];
-            double * Gi = G + i * ld;
-            for (int j = k + 1 + lane; j <= i; j += 32) Gi[j] -= ci * colk[j];
-            if (lane == 0) Gi[k] = ci;
+    for (int k = 0; k < n; k += 4) {
+        // ---- phase A: T = P^-1 (every thread), new pivot rows
+        double T[4][4];
+        {
+            double a[4][4];
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    a[q][c] = (k + q < n && k + c < n) ? G[(k + q) * ld + k + c] : (q == c ? 1.0 : 0.0);
+                    T[q][c] = (q == c) ? 1.0 : 0.0;
+                }
+            bool skip[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const double piv = a[q][q];
+                skip[q] = !(piv > 0.0 && isfinite(piv));
+                const double ip = skip[q] ? 0.0 : 1.0 / piv;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    a[q][c] *= ip;
+                    T[q][c] *= ip;
+                }
+#pragma unroll
+                for (int r2 = 0; r2 < 4; r2++) {
+                    if (r2 == q) continue;
+                    const double f = skip[q] ? 0.0 : a[r2][q];
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        a[r2][c] = fma(-f, a[q][c], a[r2][c]);
+                        T[r2][c] = fma(-f, T[q][c], T[r2][c]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                if (skip[q])
+#pragma unroll
+                    for (int c = 0; c < 4; c++) T[q][c] = 0.0;
+        }
+        for (int j = k + 4 + tid; j < n; j += 512) {          // new pivot rows of G
+            double g[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) g[q] = (k + q < n) ? G[(k + q) * ld + j] : 0.0;
+#pragma unroll
+            for (int q = 0; q < 4; q++) PR[q * FN + j] = T[q][0] * g[0] + T[q][1] * g[1] + T[q][2] * g[2] + T[q][3] * g[3];
+        }
+        if (ty == (k >> 2)) {                                    // new pivot rows of R (this thread row owns them)
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                double nr[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) nr[q] = T[q][0] * r[0][c] + T[q][1] * r[1][c] + T[q][2] * r[2][c] + T[q][3] * r[3][c];
+#pragma unroll
+                for (int q = 0; q < 4; q++) r[q][c] = nr[q];
+            }
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+                for (int p = 0; p < 4; p++)
+                    *reinterpret_cast<double2 *>(RR + q * FN + 2 * tx + 32 * p) = make_double2(r[q][2 * p], r[q][2 * p + 1]);
+        }
+        __syncthreads();
+        // ---- phase B: rank-4 updates of the other rows (multipliers G[i][k..k+3] are not rewritten here)
+        {
+            double pr[4][4];
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                const int j = k + 4 + lane + 32 * m;
+#pragma unroll
+                for (int q = 0; q < 4; q++) pr[m][q] = (j < n) ? PR[q * FN + j] : 0.0;
+            }
+#pragma unroll 2
+            for (int i = warp; i < n; i += 16) {
+                double * Gi = G + i * ld;
+                if (i >= k && i < k + 4) {
+#pragma unroll
+                    for (int m = 0; m < 4; m++) {
+                        const int j = k + 4 + lane + 32 * m;
+                        if (j < n) Gi[j] = PR[(i - k) * FN + j];
+                    }
+                    continue;
+                }
+                double mi[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) mi[q] = (k + q < n) ? Gi[k + q] : 0.0;
+#pragma unroll
+                for (int m = 0; m < 4; m++) {
+                    const int j = k + 4 + lane + 32 * m;
+                    if (j < n) {
+                        double v = Gi[j];
+#pragma unroll
+                        for (int q = 0; q < 4; q++) v = fma(-mi[q], pr[m][q], v);
+                        Gi[j] = v;
+                    }
+                }
+            }
+        }
+        if (ty != (k >> 2)) {
+            double rr[4][8];
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+                for (int p = 0; p < 4; p++) {
+                    const double2 v = *reinterpret_cast<const double2 *>(RR + q * FN + 2 * tx + 32 * p);
+                    rr[q][2 * p] = v.x;
+                    rr[q][2 * p + 1] = v.y;
+                }
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int row = 4 * ty + i;
+                double mi[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) mi[q] = (row < n && k + q < n) ? G[row * ld + k + q] : 0.0;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    double v = r[i][c];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) v = fma(-mi[q], rr[q][c], v);
+                    r[i][c] = v;
+                }
+            }
         }
         __syncthreads();
     }
 
-    const int c0 = warp * FC;
-    double * zb = colk + FN + warp * FC;           // this warp's broadcast slot
-    double b[4][FC];
+    const kvc_layer_out lo = outs[u.layer];
+    float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
 #pragma unroll
-    for (int s = 0; s < 4; s++) {
-        const int r = lane + 32 * s;
+    for (int i = 0; i < 4; i++) {
+        const int row = 4 * ty + i;
+        if (row >= n) continue;
 #pragma unroll
-        for (int c = 0; c < FC; c++) {
-            double v = 0.0;
-            if (r < n && c0 + c < dv) v = dual ? (double)Y[(long long)r * dv + c0 + c] : Zg[(long long)r * dv + c0 + c];
-            b[s][c] = v;
-        }
-    }
-#pragma unroll
-    for (int S = 0; S < 4; S++) {
-        for (int kk = 0; kk < 32; kk++) {
-            const int k = 32 * S + kk;
-            if (k >= n) break;
-            if (lane == kk) {
-                const double il = rinv[k];
-#pragma unroll
-                for (int c = 0; c < FC; c++) {
-                    b[S][c] *= il;
-                    zb[c] = b[S][c];
-                }
-            }
-            __syncwarp();
-            double z[FC];
-#pragma unroll
-            for (int c = 0; c < FC; c += 2) {
-                const double2 v = *reinterpret_cast<const double2 *>(zb + c);
-                z[c] = v.x;
-                z[c + 1] = v.y;
-            }
-            __syncwarp();
-#pragma unroll
-            for (int s2 = S; s2 < 4; s2++) {
-                const int r = lane + 32 * s2;
-                if (r > k && r < n) {
-                    const double l = G[r * ld + k];
-#pragma unroll
-                    for (int c = 0; c < FC; c++) b[s2][c] -= l * z[c];
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int S = 3; S >= 0; S--) {
-        for (int kk = 31; kk >= 0; kk--) {
-            const int k = 32 * S + kk;
-            if (k >= n) continue;
-            if (lane == kk) {
-                const double il = rinv[k];
-#pragma unroll
-                for (int c = 0; c < FC; c++) {
-                    b[S][c] *= il;
-                    zb[c] = b[S][c];
-                }
-            }
-            __syncwarp();
-            double z[FC];
-#pragma unroll
-            for (int c = 0; c < FC; c += 2) {
-                const double2 v = *reinterpret_cast<const double2 *>(zb + c);
-                z[c] = v.x;
-                z[c + 1] = v.y;
-            }
-            __syncwarp();
-#pragma unroll
-            for (int s2 = 0; s2 <= S; s2++) {
-                const int r = lane + 32 * s2;
-                if (r < k) {
-                    const double l = G[k * ld + r];
-#pragma unroll
-                    for (int c = 0; c < FC; c++) b[s2][c] -= l * z[c];
-                }
-            }
-        }
-    }
-    if (dual) {
-#pragma unroll
-        for (int s = 0; s < 4; s++) {
-            const int r = lane + 32 * s;
-            if (r >= n) continue;
-#pragma unroll
-            for (int c = 0; c < FC; c++)
-                if (c0 + c < dv) Zg[(long long)r * dv + c0 + c] = b[s][c];
-        }
-    } else {
-        const kvc_layer_out lo = outs[u.layer];
-        float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
-#pragma unroll
-        for (int s = 0; s < 4; s++) {
-            const int r = lane + 32 * s;
-            if (r >= n) continue;
-#pragma unroll
-            for (int c = 0; c < FC; c++)
-                if (c0 + c < dv) cv[(long long)r * dv + c0 + c] = (float)b[s][c];
+        for (int c = 0; c < 8; c++) {
+            const int col = 2 * tx + 32 * (c >> 1) + (c & 1);
+            if (col >= dv) continue;
+            if (dual) Zg[(long long)row * dv + col] = r[i][c];
+            else cv[(long long)row * dv + col] = (float)r[i][c];
         }
     }
 }
@@ -447,26 +500,43 @@ size_t kvc_lsq_smem_bytes(int n) {
     return b;
 }
 
-int kvc_launch_lsq(const kvc_unit * d_units, int n_units, int max_n, int max_t, size_t smem_bytes,
-                   const kvc_params_dev & P, const float * fs, double * gs,
-                   const kvc_layer_out * d_outs, cudaStream_t st) {
+int kvc_launch_lsq_gram(const kvc_unit * d_units, int n_units, int max_n, int max_t, const kvc_params_dev & P,
+                        const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_primal,
+                        cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
     const int tg = (max_n + DT - 1) / DT;
-    k_dgemm<<<dim3(tg * tg, P.H, n_units), 64, 0, st>>>(d_units, P, fs, gs, d_outs, DG_GRAM);
+    k_dgemm<<<dim3(tg * tg, P.H, n_units), 128, 0, st>>>(d_units, P, fs, gs, d_outs, DG_GRAM);
     KVC_CUDA(cudaGetLastError());
-    const int to = ((max_t + DT - 1) / DT) * ((P.dv + DT - 1) / DT);
-    k_dgemm<<<dim3(to, P.H, n_units), 64, 0, st>>>(d_units, P, fs, gs, d_outs, DG_RHS);
-    KVC_CUDA(cudaGetLastError());
-    const size_t fast_smem = (size_t)(FN * (FN + 1) + 2 * FN + 16 * FC) * sizeof(double);
+    if (any_primal) {
+        const int to = ((max_t + DT - 1) / DT) * ((P.dv + DT - 1) / DT);
+        k_dgemm<<<dim3(to, P.H, n_units), 128, 0, st>>>(d_units, P, fs, gs, d_outs, DG_RHS);
+        KVC_CUDA(cudaGetLastError());
+    }
+    return KVC_OK;
+}
+
+int kvc_launch_lsq_factor(const kvc_unit * d_units, int n_units, int max_n, size_t smem_bytes,
+                          const kvc_params_dev & P, const float * fs, double * gs,
+                          const kvc_layer_out * d_outs, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    const size_t fast_smem = (size_t)(FN * (FN + 1) + 8 * FN) * sizeof(double);
     KVC_CUDA(cudaFuncSetAttribute(k_lsq_factor, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fast_smem));
     k_lsq_factor<<<dim3(n_units, P.H), 512, fast_smem, st>>>(d_units, P, fs, gs, d_outs);
-    KVC_CUDA(cudaGetLastError());
-    k_dgemm<<<dim3(to, P.H, n_units), 64, 0, st>>>(d_units, P, fs, gs, d_outs, DG_OUT);
     KVC_CUDA(cudaGetLastError());
     if (max_n > FN || P.dv > FN) {
         KVC_CUDA(cudaFuncSetAttribute(k_chol_solve, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
         k_chol_solve<<<dim3(n_units, P.H), 256, smem_bytes, st>>>(d_units, P, fs, gs, d_outs);
         KVC_CUDA(cudaGetLastError());
     }
+    return KVC_OK;
+}
+
+int kvc_launch_lsq_out(const kvc_unit * d_units, int n_units, int max_t, const kvc_params_dev & P,
+                       const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_dual,
+                       cudaStream_t st) {
+    if (n_units <= 0 || !any_dual) return KVC_OK;
+    const int to = ((max_t + DT - 1) / DT) * ((P.dv + DT - 1) / DT);
+    k_dgemm<<<dim3(to, P.H, n_units), 128, 0, st>>>(d_units, P, fs, gs, d_outs, DG_OUT);
+    KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }

@@ -22,8 +22,8 @@ SEAM_SYMBOLS = [
 ]
 BATCHED_SYMBOLS = ["kvc_plan_layers", "kvc_compact_layers_dev", "kvc_launch_count", "kvc_profile",
                    "kvc_quantize_rows_dev", "kvc_dequantize_rows_dev"]
-STAGES = ["decode", "score", "softmax_importance", "select", "refit_target", "beta", "x_build", "ls_solve",
-          "refine", "metrics", "requant"]
+STAGES = ["decode", "score", "softmax_importance", "select", "refit_target", "beta", "x_build", "ls_gram",
+          "refine", "metrics", "requant", "ls_factor", "ls_out"]
 
 
 class ModelDesc(Structure):

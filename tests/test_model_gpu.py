@@ -188,10 +188,19 @@ def test_device_codecs_match_host(kvc, typ):
     X = (rng.standard_normal((257, 512)) * rng.choice([1e-6, 1e-2, 1.0, 3e4], size=(257, 1))).astype(np.float32)
     X[3] = 0.0
     X[4, ::3] = -0.0
+    X[5, 0] = np.nan          # a block whose first value is NaN
+    X[6, 7] = np.nan          # NaN inside a block
+    X[7, 40] = np.inf
+    X[8, 64:96] = 1e-40       # subnormal block
     B_dev = lib.quantize_dev(kvc, torch.from_numpy(X).cuda(), typ).cpu().numpy()
     np.testing.assert_array_equal(B_dev, abi.quantize_rows(kvc, X, typ))
     D_dev = lib.dequantize_dev(kvc, torch.from_numpy(B_dev).cuda(), typ, 512).cpu().numpy()
     np.testing.assert_array_equal(D_dev, abi.dequantize_rows(kvc, B_dev, typ, 512))
+    # a row count that is not a multiple of 4 blocks per warp, and odd row lengths
+    Y = X[:13, :96].copy()
+    if typ in (2, 3, 8):
+        B2 = lib.quantize_dev(kvc, torch.from_numpy(Y).cuda(), typ).cpu().numpy()
+        np.testing.assert_array_equal(B2, abi.quantize_rows(kvc, Y, typ))
 
 
 def test_full_size_cfg4_properties(kvc):
