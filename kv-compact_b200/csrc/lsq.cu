@@ -21,8 +21,9 @@
 //   OUT   C_v = X^T Z                        (dual only)
 // and the solve runs one CTA per (unit, head):
 //   k_lsq_factor  block Gauss-Jordan elimination of [G | R] (four unknowns
-//                 per step) in shared memory and registers (n <= 128,
-//                 d_v <= 128); writes Z (dual) or C_v (primal).
+//                 per step, rank-4 updates on the fp64 tensor cores) with G in
+//                 shared memory and R in MMA fragments (n <= 128, d_v <= 128);
+//                 writes Z (dual) or C_v (primal).
 //   k_chol_solve  Cholesky + triangular solves for n > 128 or d_v > 128,
 //                 G in global memory.
 #include "kvc_internal.h"
@@ -297,25 +298,25 @@ __global__ void __launch_bounds__(256) k_chol_solve(const kvc_unit * __restrict_
 // Solve, n = min(n_q, t) <= 128 and d_v <= 128, one CTA of 16 warps per
 // (unit, head): block Gauss-Jordan elimination of [G | R] in diagonal order
 // without pivoting (R = Y for the dual, X^T Y from k_dgemm for the primal),
-// four unknowns per step. G is symmetric positive definite (Gram matrix +
-// ridge), for which elimination in diagonal order is stable.
-// Step k (unknowns k..k+3): every thread inverts the 4x4 pivot block P by
-// Gauss-Jordan in registers; a pivot that is not positive and finite marks its
-// unknown singular (its row of P^-1 is zeroed, so it drops out and ends at
-// zero — the reference skips pivots below 1e-12). The pivot rows become
-// P^-1 [pivot rows of G and R]; every other row i loses G[i][k..k+3] x (the new
-// pivot rows). Only G's columns right of the block are carried (eliminated
-// columns are implicitly unit vectors); all d_v columns of R are. After the
-// last step R holds G^-1 R. Each step is a rank-4 update that is parallel
-// over all rows and columns, with two barriers; there are no triangular
-// dependency chains.
-// G sits in shared memory (row stride n + 1); R in registers: thread (ty, tx)
-// of the 32 x 16 grid owns rows 4ty..4ty+3 — so the four pivot rows of a step
-// belong to one row of threads — and columns 2tx + 32p + {0, 1} (p < 4),
-// which makes the reads of the new pivot rows conflict-free double2 loads.
-// The result Z (dual, consumed by the OUT product) or C_v (primal) is written
-// to global memory.
+// four unknowns per step, on the fp64 tensor cores. G is symmetric positive
+// definite (Gram matrix + ridge), for which elimination in diagonal order is
+// stable.
+// Step k (unknowns k..k+3): P = G[k..k+3][k..k+3] is inverted by Gauss-Jordan
+// in registers; a pivot that is not positive and finite marks its unknown
+// singular (its row of P^-1 is zeroed, so it drops out and ends at zero — the
+// reference skips pivots below 1e-12). The pivot rows become P^-1 (pivot rows
+// of G and R); every other row i loses M[i] x (the new pivot rows), with
+// M[i] = G[i][k..k+3]. That rank-4 update is an m8n8k4 MMA per 8x8 tile: G's
+// tiles right of the block (read from and written back to shared memory) and
+// all of R (held in MMA accumulator fragments, warp w owning a 32x32 quarter-
+// block). Three barriers per step; no triangular dependency chains. n is
+// padded to a multiple of 8 with identity rows, which stay untouched.
+// After the last step R holds G^-1 R: Z (dual, consumed by the OUT product) or
+// C_v (primal) is written to global memory.
 // ---------------------------------------------------------------------------
+constexpr int GLD = FN + 8;     // G row stride: the 16-byte C-tile loads of a quarter-warp hit 8 bank groups
+constexpr int PLD = FN + 4;     // pivot-row stride: B-fragment loads hit every bank twice
+
 __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restrict__ units, kvc_params_dev P,
                                                        const float * __restrict__ fs, double * __restrict__ gs,
                                                        const kvc_layer_out * __restrict__ outs) {
@@ -329,38 +330,46 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
     const float * Y = fs + u.y_off + (long long)h * nq * dv;
     const double * Gg = gs + u.g_off + (long long)h * n * n;
     double * Zg = gs + u.z_off + (long long)h * n * dv;        // primal: holds X^T Y on entry
+    const int n8 = (n + 7) & ~7;
 
-    extern __shared__ double G[];
-    const int ld = n + 1;
-    double * PR = G + FN * (FN + 1);           // [4][FN] new pivot rows of G
-    double * RR = PR + 4 * FN;                 // [4][FN] new pivot rows of R
+    extern __shared__ __align__(16) double G[];   // [n8][GLD]
+    double * PR = G + FN * GLD;                  // [4][PLD] new pivot rows of G
+    double * RR = PR + 4 * PLD;                  // [4][PLD] new pivot rows of R
+    double * RP = RR + 4 * PLD;                  // [4][PLD] old pivot rows of R
+    double * M = RP + 4 * PLD;                   // [FN][4]  multipliers (0 on pivot rows)
+    double * Ts = M + 4 * FN;                    // [16]     P^-1
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ty = tid >> 4, tx = tid & 15;
-    for (int e = tid; e < n * n; e += 512) G[(e / n) * ld + (e % n)] = Gg[e];
-    double r[4][8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int row = 4 * ty + i;
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-            const int col = 2 * tx + 32 * (c >> 1) + (c & 1);
-            double v = 0.0;
-            if (row < n && col < dv) v = dual ? (double)Y[(long long)row * dv + col] : Zg[(long long)row * dv + col];
-            r[i][c] = v;
-        }
+    const int fr = lane >> 2, fq = lane & 3;     // MMA fragment row / k index of this lane
+    const int wr = warp >> 2, wc = warp & 3;     // this warp's quarter-block of R
+    for (int e = tid; e < n8 * n8; e += 512) {
+        const int i = e / n8, j = e - i * n8;
+        G[i * GLD + j] = (i < n && j < n) ? Gg[(long long)i * n + j] : (i == j ? 1.0 : 0.0);
     }
+    double acc[4][4][2];
+#pragma unroll
+    for (int rt = 0; rt < 4; rt++)
+#pragma unroll
+        for (int ct = 0; ct < 4; ct++)
+#pragma unroll
+            for (int v = 0; v < 2; v++) {
+                const int row = 32 * wr + 8 * rt + fr, col = 32 * wc + 8 * ct + 2 * fq + v;
+                double x = 0.0;
+                if (row < n && col < dv) x = dual ? (double)Y[(long long)row * dv + col] : Zg[(long long)row * dv + col];
+                acc[rt][ct][v] = x;
+            }
     __syncthreads();
 
-    for (int k = 0; k < n; k += 4) {
-        // ---- phase A: T = P^-1 (every thread), new pivot rows
-        double T[4][4];
-        {
-            double a[4][4];
+    for (int k = 0; k < n8; k += 4) {
+        const int jt0 = (k + 4) >> 3;            // first column tile of G still needed
+        const int prt = (k >> 3) & 3, pr0 = k & 7;
+        // ---- A1: P^-1 and the new pivot rows of G (warps 0-3); multipliers; old pivot rows of R
+        if (tid < 128) {
+            double a[4][4], T[4][4];
 #pragma unroll
             for (int q = 0; q < 4; q++)
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
-                    a[q][c] = (k + q < n && k + c < n) ? G[(k + q) * ld + k + c] : (q == c ? 1.0 : 0.0);
+                    a[q][c] = G[(k + q) * GLD + k + c];
                     T[q][c] = (q == c) ? 1.0 : 0.0;
                 }
             bool skip[4];
@@ -390,88 +399,81 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
                 if (skip[q])
 #pragma unroll
                     for (int c = 0; c < 4; c++) T[q][c] = 0.0;
-        }
-        for (int j = k + 4 + tid; j < n; j += 512) {          // new pivot rows of G
-            double g[4];
+            if (tid == 0)
 #pragma unroll
-            for (int q = 0; q < 4; q++) g[q] = (k + q < n) ? G[(k + q) * ld + j] : 0.0;
+                for (int q = 0; q < 16; q++) Ts[q] = T[q >> 2][q & 3];
+            const int j = 8 * jt0 + tid;
+            if (j < n8) {
+                double g[4];
 #pragma unroll
-            for (int q = 0; q < 4; q++) PR[q * FN + j] = T[q][0] * g[0] + T[q][1] * g[1] + T[q][2] * g[2] + T[q][3] * g[3];
-        }
-        if (ty == (k >> 2)) {                                    // new pivot rows of R (this thread row owns them)
+                for (int q = 0; q < 4; q++) g[q] = G[(k + q) * GLD + j];
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-                double nr[4];
-#pragma unroll
-                for (int q = 0; q < 4; q++) nr[q] = T[q][0] * r[0][c] + T[q][1] * r[1][c] + T[q][2] * r[2][c] + T[q][3] * r[3][c];
-#pragma unroll
-                for (int q = 0; q < 4; q++) r[q][c] = nr[q];
+                for (int q = 0; q < 4; q++)
+                    PR[q * PLD + j] = fma(T[q][0], g[0], fma(T[q][1], g[1], fma(T[q][2], g[2], T[q][3] * g[3])));
             }
+        }
+        if (tid < FN) {                          // rows past n8 get zero multipliers too
+            const bool zero = (tid >= k && tid < k + 4) || tid >= n8;
 #pragma unroll
-            for (int q = 0; q < 4; q++)
+            for (int q = 0; q < 4; q++) M[tid * 4 + q] = zero ? 0.0 : G[tid * GLD + k + q];
+        }
+        if (wr == (k >> 5) && fr >= pr0 && fr < pr0 + 4) {
 #pragma unroll
-                for (int p = 0; p < 4; p++)
-                    *reinterpret_cast<double2 *>(RR + q * FN + 2 * tx + 32 * p) = make_double2(r[q][2 * p], r[q][2 * p + 1]);
+            for (int rt = 0; rt < 4; rt++)
+                if (rt == prt)
+#pragma unroll
+                    for (int ct = 0; ct < 4; ct++)
+#pragma unroll
+                        for (int v = 0; v < 2; v++) RP[(fr - pr0) * PLD + 32 * wc + 8 * ct + 2 * fq + v] = acc[rt][ct][v];
         }
         __syncthreads();
-        // ---- phase B: rank-4 updates of the other rows (multipliers G[i][k..k+3] are not rewritten here)
-        {
-            double pr[4][4];
+        // ---- A2: new pivot rows of R; pivot rows of G take their new values
+        if (tid < 128) {
+            const int c = tid;
+            double rp[4];
 #pragma unroll
-            for (int m = 0; m < 4; m++) {
-                const int j = k + 4 + lane + 32 * m;
-#pragma unroll
-                for (int q = 0; q < 4; q++) pr[m][q] = (j < n) ? PR[q * FN + j] : 0.0;
-            }
-#pragma unroll 2
-            for (int i = warp; i < n; i += 16) {
-                double * Gi = G + i * ld;
-                if (i >= k && i < k + 4) {
-#pragma unroll
-                    for (int m = 0; m < 4; m++) {
-                        const int j = k + 4 + lane + 32 * m;
-                        if (j < n) Gi[j] = PR[(i - k) * FN + j];
-                    }
-                    continue;
-                }
-                double mi[4];
-#pragma unroll
-                for (int q = 0; q < 4; q++) mi[q] = (k + q < n) ? Gi[k + q] : 0.0;
-#pragma unroll
-                for (int m = 0; m < 4; m++) {
-                    const int j = k + 4 + lane + 32 * m;
-                    if (j < n) {
-                        double v = Gi[j];
-#pragma unroll
-                        for (int q = 0; q < 4; q++) v = fma(-mi[q], pr[m][q], v);
-                        Gi[j] = v;
-                    }
-                }
-            }
-        }
-        if (ty != (k >> 2)) {
-            double rr[4][8];
+            for (int q = 0; q < 4; q++) rp[q] = RP[q * PLD + c];
 #pragma unroll
             for (int q = 0; q < 4; q++)
+                RR[q * PLD + c] = fma(Ts[4 * q], rp[0], fma(Ts[4 * q + 1], rp[1], fma(Ts[4 * q + 2], rp[2], Ts[4 * q + 3] * rp[3])));
+        } else if (tid < 256) {
+            const int j = 8 * jt0 + (tid - 128);
+            if (j < n8)
 #pragma unroll
-                for (int p = 0; p < 4; p++) {
-                    const double2 v = *reinterpret_cast<const double2 *>(RR + q * FN + 2 * tx + 32 * p);
-                    rr[q][2 * p] = v.x;
-                    rr[q][2 * p + 1] = v.y;
-                }
+                for (int q = 0; q < 4; q++) G[(k + q) * GLD + j] = PR[q * PLD + j];
+        }
+        __syncthreads();
+        // ---- B: rank-4 updates (pivot rows have zero multipliers)
+        if (8 * warp < n8) {                     // G: row tile `warp`, every column tile from jt0
+            const double am = -M[(8 * warp + fr) * 4 + fq];
+            for (int ct = jt0; ct < (n8 >> 3); ct++) {
+                const double b = PR[fq * PLD + 8 * ct + fr];
+                double2 * cp = reinterpret_cast<double2 *>(G + (8 * warp + fr) * GLD + 8 * ct + 2 * fq);
+                const double2 c2 = *cp;
+                double cc[2] = {c2.x, c2.y};
+                dmma(cc, am, b);
+                *cp = make_double2(cc[0], cc[1]);
+            }
+        }
+        {                                        // R: this warp's 4x4 tiles
+            double am[4], bb[4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int row = 4 * ty + i;
-                double mi[4];
+            for (int rt = 0; rt < 4; rt++) am[rt] = -M[(32 * wr + 8 * rt + fr) * 4 + fq];
 #pragma unroll
-                for (int q = 0; q < 4; q++) mi[q] = (row < n && k + q < n) ? G[row * ld + k + q] : 0.0;
+            for (int ct = 0; ct < 4; ct++) bb[ct] = RR[fq * PLD + 32 * wc + 8 * ct + fr];
 #pragma unroll
-                for (int c = 0; c < 8; c++) {
-                    double v = r[i][c];
+            for (int rt = 0; rt < 4; rt++)
 #pragma unroll
-                    for (int q = 0; q < 4; q++) v = fma(-mi[q], rr[q][c], v);
-                    r[i][c] = v;
-                }
+                for (int ct = 0; ct < 4; ct++) dmma(acc[rt][ct], am[rt], bb[ct]);
+            if (wr == (k >> 5) && fr >= pr0 && fr < pr0 + 4) {
+#pragma unroll
+                for (int rt = 0; rt < 4; rt++)
+                    if (rt == prt)
+#pragma unroll
+                        for (int ct = 0; ct < 4; ct++)
+#pragma unroll
+                            for (int v = 0; v < 2; v++)
+                                acc[rt][ct][v] = RR[(fr - pr0) * PLD + 32 * wc + 8 * ct + 2 * fq + v];
             }
         }
         __syncthreads();
@@ -480,17 +482,16 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
     const kvc_layer_out lo = outs[u.layer];
     float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int row = 4 * ty + i;
-        if (row >= n) continue;
+    for (int rt = 0; rt < 4; rt++)
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            const int col = 2 * tx + 32 * (c >> 1) + (c & 1);
-            if (col >= dv) continue;
-            if (dual) Zg[(long long)row * dv + col] = r[i][c];
-            else cv[(long long)row * dv + col] = (float)r[i][c];
-        }
-    }
+        for (int ct = 0; ct < 4; ct++)
+#pragma unroll
+            for (int v = 0; v < 2; v++) {
+                const int row = 32 * wr + 8 * rt + fr, col = 32 * wc + 8 * ct + 2 * fq + v;
+                if (row >= n || col >= dv) continue;
+                if (dual) Zg[(long long)row * dv + col] = acc[rt][ct][v];
+                else cv[(long long)row * dv + col] = (float)acc[rt][ct][v];
+            }
 }
 
 size_t kvc_lsq_smem_bytes(int n) {
@@ -519,7 +520,7 @@ int kvc_launch_lsq_factor(const kvc_unit * d_units, int n_units, int max_n, size
                           const kvc_params_dev & P, const float * fs, double * gs,
                           const kvc_layer_out * d_outs, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
-    const size_t fast_smem = (size_t)(FN * (FN + 1) + 8 * FN) * sizeof(double);
+    const size_t fast_smem = (size_t)(FN * GLD + 12 * PLD + 4 * FN + 16) * sizeof(double);
     KVC_CUDA(cudaFuncSetAttribute(k_lsq_factor, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fast_smem));
     k_lsq_factor<<<dim3(n_units, P.H), 512, fast_smem, st>>>(d_units, P, fs, gs, d_outs);
     KVC_CUDA(cudaGetLastError());
