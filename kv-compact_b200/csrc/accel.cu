@@ -136,6 +136,7 @@ KVC_EXPORT void kv_compact_cuda_pool_free(void) {
         ctx->arena[s] = nullptr;
         ctx->arena_cap[s] = 0;
     }
+    kvc_hpool_release();
 }
 
 }  // extern "C"

@@ -49,10 +49,13 @@ int gather_to_host(kvc_ctx * ctx, const std::vector<d2h_piece> & v) {
     std::vector<kvc_copy_piece> pieces;
     size_t off = 0;
     for (const auto & x : v) {
-        if (x.bytes) {
-            KVC_CUDA(cudaMemcpyAsync((char *)pin + off, x.dev, x.bytes, cudaMemcpyDeviceToHost, ctx->stream));
-            pieces.push_back({x.host, (char *)pin + off, x.bytes});
+        if (!x.bytes) continue;
+        if (kvc_is_pinned(x.host)) {          // page-locked result array: copy straight into it
+            KVC_CUDA(cudaMemcpyAsync(x.host, x.dev, x.bytes, cudaMemcpyDeviceToHost, ctx->stream));
+            continue;
         }
+        KVC_CUDA(cudaMemcpyAsync((char *)pin + off, x.dev, x.bytes, cudaMemcpyDeviceToHost, ctx->stream));
+        pieces.push_back({x.host, (char *)pin + off, x.bytes});
         off += (x.bytes + 255) & ~(size_t)255;
     }
     if ((rc = kvc_wait(ctx))) return rc;
@@ -139,12 +142,12 @@ int fill_result(kvc_ctx * ctx, dev_out & d, int H, int dv, kv_compact_result * r
     const int t = d.plan.t_total;
     r->t = t;
     r->n_head_kv = H;
-    r->selected_indices = (int *)malloc((size_t)std::max(t, 1) * sizeof(int));
+    r->selected_indices = (int *)kvc_hmalloc((size_t)std::max(t, 1) * sizeof(int));
     r->beta = (float **)malloc((size_t)H * sizeof(float *));
     r->C_v = (float **)malloc((size_t)H * sizeof(float *));
     for (int h = 0; h < H; h++) {
-        r->beta[h] = (float *)malloc((size_t)std::max(t, 1) * sizeof(float));
-        r->C_v[h] = (float *)malloc((size_t)std::max(t, 1) * dv * sizeof(float));
+        r->beta[h] = (float *)kvc_hmalloc((size_t)std::max(t, 1) * sizeof(float));
+        r->C_v[h] = (float *)kvc_hmalloc((size_t)std::max(t, 1) * dv * sizeof(float));
     }
     std::vector<d2h_piece> v;
     v.push_back({r->selected_indices, d.sel, (size_t)t * 4});
@@ -162,15 +165,15 @@ int fill_result(kvc_ctx * ctx, dev_out & d, int H, int dv, kv_compact_result * r
 
 void free_result_arrays(kv_compact_result * r) {
     if (!r) return;
-    free(r->selected_indices);
+    kvc_hfree(r->selected_indices);
     r->selected_indices = NULL;
     if (r->beta) {
-        for (int h = 0; h < r->n_head_kv; h++) free(r->beta[h]);
+        for (int h = 0; h < r->n_head_kv; h++) kvc_hfree(r->beta[h]);
         free(r->beta);
         r->beta = NULL;
     }
     if (r->C_v) {
-        for (int h = 0; h < r->n_head_kv; h++) free(r->C_v[h]);
+        for (int h = 0; h < r->n_head_kv; h++) kvc_hfree(r->C_v[h]);
         free(r->C_v);
         r->C_v = NULL;
     }
@@ -423,8 +426,8 @@ KVC_EXPORT int kv_compact_quantized(const uint8_t * K_quant, const uint8_t * V_q
     result->v_type = v_type;
     result->k_row_bytes = k_row_bytes;
     result->v_row_bytes = v_row_bytes;
-    result->K_out = (uint8_t *)malloc(std::max<size_t>((size_t)t * k_row_bytes, 1));
-    result->V_out = (uint8_t *)malloc(std::max<size_t>((size_t)t * v_row_bytes, 1));
+    result->K_out = (uint8_t *)kvc_hmalloc(std::max<size_t>((size_t)t * k_row_bytes, 1));
+    result->V_out = (uint8_t *)kvc_hmalloc(std::max<size_t>((size_t)t * v_row_bytes, 1));
     if ((rc = fill_result(ctx, d, H, d_v, &result->base,
                           {{result->K_out, oK, (size_t)t * k_row_bytes}, {result->V_out, oV, (size_t)t * v_row_bytes}})))
         return rc;
@@ -437,9 +440,9 @@ KVC_EXPORT int kv_compact_quantized(const uint8_t * K_quant, const uint8_t * V_q
 KVC_EXPORT void kv_compact_quant_result_free(kv_compact_quant_result * result) {
     if (!result) return;
     free_result_arrays(&result->base);
-    free(result->K_out);
+    kvc_hfree(result->K_out);
     result->K_out = NULL;
-    free(result->V_out);
+    kvc_hfree(result->V_out);
     result->V_out = NULL;
 }
 

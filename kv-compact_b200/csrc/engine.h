@@ -89,6 +89,13 @@ int kvc_pinned(kvc_ctx * ctx, size_t bytes, void ** out);
 struct kvc_copy_piece { void * dst; const void * src; size_t bytes; };
 void kvc_parallel_copy(const std::vector<kvc_copy_piece> & pieces);
 
+// Result arrays of the drop-in API (hostpool.cu): page-locked blocks from a
+// pool when available (else malloc); kvc_hfree returns them to the pool.
+void * kvc_hmalloc(size_t bytes);
+void kvc_hfree(void * p);
+bool kvc_is_pinned(const void * p);
+void kvc_hpool_release();
+
 // Accumulate the elapsed times of the stages recorded since the last call
 // (waits for the last recorded event).
 void kvc_resolve_timers(kvc_ctx * ctx);

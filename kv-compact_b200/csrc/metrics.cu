@@ -352,7 +352,12 @@ __global__ void __launch_bounds__(256) k_metric_partial(const kvc_unit * __restr
 }
 
 // grid min(H,4) * min(n_q,32): merge the chunk records of one (head, query)
-// pair in fp64, then the metric triple.
+// pair in fp64, then the metric triple. The per-chunk weights
+// e^(m_k - M) (s_k + 1e-12) (and their kept-key counterparts) are computed
+// once into shared memory (up to MERGE_SMEM_CHUNKS chunks; beyond that they
+// are recomputed per column).
+constexpr int MERGE_SMEM_CHUNKS = 2048;
+
 __global__ void __launch_bounds__(256) k_metric_merge(const float * __restrict__ mpart, int n_chunks, int mh,
                                                       int mq, int dv, float * __restrict__ res) {
     const int pair = blockIdx.x;
@@ -360,7 +365,9 @@ __global__ void __launch_bounds__(256) k_metric_merge(const float * __restrict__
     const int rec = metric_rec(dv);
     const long long cstride = (long long)mh * mq * rec;
     const float * r0 = mpart + ((long long)h * mq + q) * rec;
+    extern __shared__ double wsh[];              // [2][n_chunks] orig / comp weights
     __shared__ float red[2][32];
+    __shared__ double dred[2][32];
     __shared__ float oo[KVC_MAX_D], co[KVC_MAX_D];
     float M = -INFINITY, Mc = -INFINITY;
     for (int k = threadIdx.x; k < n_chunks; k += blockDim.x) {
@@ -377,18 +384,44 @@ __global__ void __launch_bounds__(256) k_metric_merge(const float * __restrict__
     M = red[0][0];
     Mc = red[1][0];
     for (int i = 1; i < nw; i++) { M = fmaxf(M, red[0][i]); Mc = fmaxf(Mc, red[1][i]); }
+    const bool cached = n_chunks <= MERGE_SMEM_CHUNKS;
+    double d_o = 0.0, d_c = 0.0;                 // denominators: sum_k e^(m_k - M) s_k
+    for (int k = threadIdx.x; k < n_chunks; k += blockDim.x) {
+        const float * r = r0 + k * cstride;
+        const double eo = exp((double)r[0] - (double)M), ec = exp((double)r[2] - (double)Mc);
+        d_o += eo * (double)r[1];
+        d_c += ec * (double)r[3];
+        if (cached) {
+            wsh[k] = eo * ((double)r[1] + 1e-12);
+            wsh[n_chunks + k] = ec * ((double)r[3] + 1e-12);
+        }
+    }
+    for (int o = 16; o; o >>= 1) {
+        d_o += __shfl_xor_sync(0xffffffffu, d_o, o);
+        d_c += __shfl_xor_sync(0xffffffffu, d_c, o);
+    }
+    if (lane == 0) { dred[0][w] = d_o; dred[1][w] = d_c; }
+    __syncthreads();
+    d_o = 0.0;
+    d_c = 0.0;
+    for (int i = 0; i < nw; i++) { d_o += dred[0][i]; d_c += dred[1][i]; }
     for (int c = threadIdx.x; c < dv; c += blockDim.x) {
-        double no = 0.0, do_ = 0.0, nc = 0.0, dc = 0.0;
+        double no = 0.0, nc = 0.0;
         for (int k = 0; k < n_chunks; k++) {
             const float * r = r0 + k * cstride;
-            const double eo = exp((double)r[0] - (double)M), ec = exp((double)r[2] - (double)Mc);
-            no += eo * ((double)r[1] + 1e-12) * (double)r[4 + c];
-            do_ += eo * (double)r[1];
-            nc += ec * ((double)r[3] + 1e-12) * (double)r[4 + dv + c];
-            dc += ec * (double)r[3];
+            double wo, wc;
+            if (cached) {
+                wo = wsh[k];
+                wc = wsh[n_chunks + k];
+            } else {
+                wo = exp((double)r[0] - (double)M) * ((double)r[1] + 1e-12);
+                wc = exp((double)r[2] - (double)Mc) * ((double)r[3] + 1e-12);
+            }
+            no = fma(wo, (double)r[4 + c], no);
+            nc = fma(wc, (double)r[4 + dv + c], nc);
         }
-        oo[c] = (float)(no / (do_ + 1e-12));
-        co[c] = (float)(nc / (dc + 1e-12));
+        oo[c] = (float)(no / (d_o + 1e-12));
+        co[c] = (float)(nc / (d_c + 1e-12));
     }
     __syncthreads();
     if (threadIdx.x == 0) metric_triple(oo, co, dv, res + pair * 3);
@@ -447,7 +480,8 @@ int kvc_launch_metric_partial(const kvc_unit * d_units, int n_units, const kvc_p
 int kvc_launch_metric_merge(const float * mpart, int n_chunks, int H, int nq, int dv, float * res, cudaStream_t st) {
     const int mh = H < 4 ? H : 4, mq = nq < 32 ? nq : 32;
     if (mh * mq <= 0 || n_chunks <= 0) return KVC_OK;
-    k_metric_merge<<<mh * mq, 256, 0, st>>>(mpart, n_chunks, mh, mq, dv, res);
+    const size_t sm = n_chunks <= MERGE_SMEM_CHUNKS ? 2 * (size_t)n_chunks * sizeof(double) : 0;
+    k_metric_merge<<<mh * mq, 256, sm, st>>>(mpart, n_chunks, mh, mq, dv, res);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
