@@ -22,6 +22,14 @@ double ms_since(clk::time_point t0) {
 }
 
 // arena slots: 0-2 engine scratch, 4 metrics, 3/6 fp32 K/V (ping-pong), 5 io, 7 quantised io
+
+// Returning from a call with an upload still in flight on the copy stream
+// would let the caller reuse its input buffers too early: every return path
+// waits for that stream (a no-op once the engine has consumed the upload).
+struct copy_stream_guard {
+    kvc_ctx * ctx;
+    ~copy_stream_guard() { cudaStreamSynchronize(ctx->copy_stream); }
+};
 enum { SLOT_KV_A = 3, SLOT_IO = 5, SLOT_KV_B = 6, SLOT_QIO = 7 };
 
 struct dev_out {
@@ -73,8 +81,13 @@ void finish_dev(kvc_ctx * ctx, dev_out * d) {
 }
 
 // Compact one layer whose fp32 K/V are already on the device.
+// V may still be on the host (`v_host`, `v_bytes`): the engine uploads it to
+// `v_dev` on the copy stream while the scoring runs, and decodes it into dV
+// when `v_quant` (== v_dev) is given.
 int compact_dev(kvc_ctx * ctx, const float * dK, const float * dV, const float * hQ, int T, int n_q, int H,
-                int dk, int dv, const kv_compact_params & p, dev_out * out, bool want_metrics) {
+                int dk, int dv, const kv_compact_params & p, dev_out * out, bool want_metrics,
+                const void * v_host = nullptr, void * v_dev = nullptr, size_t v_bytes = 0,
+                const uint8_t * v_quant = nullptr, size_t v_rb = 0, int v_type = 0) {
     int rc = kvc_make_plan(T, n_q, hQ == nullptr, H, dk, dv, p, &out->plan);
     if (rc) return rc;
     const kvc_plan & pl = out->plan;
@@ -114,6 +127,12 @@ int compact_dev(kvc_ctx * ctx, const float * dK, const float * dV, const float *
     job.Q = dQ;
     job.rkv_w = rkv ? dW : nullptr;
     job.plan = &pl;
+    job.v_host = v_host;
+    job.v_dev = v_dev;
+    job.v_bytes = v_bytes;
+    job.v_quant = v_quant;
+    job.v_row_bytes = v_rb;
+    job.v_type = v_type;
     job.out.sel = dsel;
     job.out.beta = dbeta;
     job.out.cv = dcv;
@@ -226,16 +245,18 @@ KVC_EXPORT int kv_compact(const float * K_all, const float * V_all, const float 
     kvc_ctx * ctx = kvc_get_ctx(&rc);
     if (!ctx) return rc;
     std::lock_guard<std::mutex> lk(ctx->mu);
+    copy_stream_guard cg{ctx};
     const int H = n_head_kv, ek = H * d_k, ev = H * d_v;
     void * a;
     if ((rc = kvc_arena(ctx, SLOT_KV_A, ((size_t)T * ek + (size_t)T * ev + 64) * 4, &a))) return rc;
     float * dK = (float *)a;
     float * dV = dK + (((size_t)T * ek + 31) & ~31ULL);
+    // K now; V is uploaded by the engine on the copy stream, overlapping the scoring
     KVC_CUDA(cudaMemcpyAsync(dK, K_all, (size_t)T * ek * 4, cudaMemcpyHostToDevice, ctx->stream));
-    KVC_CUDA(cudaMemcpyAsync(dV, V_all, (size_t)T * ev * 4, cudaMemcpyHostToDevice, ctx->stream));
     const float * hQ = (p.use_cheap_qref || !Q_ref_all) ? nullptr : Q_ref_all;
     dev_out d;
-    if ((rc = compact_dev(ctx, dK, dV, hQ, T, n_q, H, d_k, d_v, p, &d, true))) return rc;
+    if ((rc = compact_dev(ctx, dK, dV, hQ, T, n_q, H, d_k, d_v, p, &d, true, V_all, dV, (size_t)T * ev * 4)))
+        return rc;
     if ((rc = fill_result(ctx, d, H, d_v, result))) return rc;
     result->stats = d.stats;
     result->stats.elapsed_ms = ms_since(t0);
@@ -391,6 +412,7 @@ KVC_EXPORT int kv_compact_quantized(const uint8_t * K_quant, const uint8_t * V_q
     kvc_ctx * ctx = kvc_get_ctx(&rc);
     if (!ctx) return rc;
     std::lock_guard<std::mutex> lk(ctx->mu);
+    copy_stream_guard cg{ctx};
     cudaStream_t st = ctx->stream;
     size_t nk = ((size_t)T * ek + 31) & ~31ULL, nv = ((size_t)T * ev + 31) & ~31ULL;
     size_t qk = ((size_t)T * k_row_bytes + 255) & ~255ULL, qv = ((size_t)T * v_row_bytes + 255) & ~255ULL;
@@ -400,17 +422,20 @@ KVC_EXPORT int kv_compact_quantized(const uint8_t * K_quant, const uint8_t * V_q
     float * dV = dK + nk;
     uint8_t * qK = (uint8_t *)(dV + nv);
     uint8_t * qV = qK + qk;
+    // K now; the engine uploads V on the copy stream once its own small
+    // uploads are queued, and decodes it just before the first stage that
+    // reads it (the scoring overlaps the upload)
     KVC_CUDA(cudaMemcpyAsync(qK, K_quant, (size_t)T * k_row_bytes, cudaMemcpyHostToDevice, st));
-    KVC_CUDA(cudaMemcpyAsync(qV, V_quant, (size_t)T * v_row_bytes, cudaMemcpyHostToDevice, st));
     {
-        kvc_stage_timer tm(ctx, KVC_ST_DECODE, 2);
+        kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1);
         if ((rc = kvc_launch_decode(qK, k_row_bytes, k_type, dK, T, ek, st))) return rc;
-        if ((rc = kvc_launch_decode(qV, v_row_bytes, v_type, dV, T, ev, st))) return rc;
     }
     memset(&result->base, 0, sizeof(result->base));
     const float * hQ = (p.use_cheap_qref || !Q_ref_all) ? nullptr : Q_ref_all;
     dev_out d;
-    if ((rc = compact_dev(ctx, dK, dV, hQ, T, n_q, H, d_k, d_v, p, &d, true))) return rc;
+    if ((rc = compact_dev(ctx, dK, dV, hQ, T, n_q, H, d_k, d_v, p, &d, true, V_quant, qV,
+                          (size_t)T * v_row_bytes, qV, v_row_bytes, v_type)))
+        return rc;
     const int t = d.plan.t_total;
     void * b;
     size_t ob = (((size_t)t * k_row_bytes + 255) & ~255ULL) + (size_t)t * v_row_bytes + 256;

@@ -153,6 +153,13 @@ kvc_ctx * kvc_get_ctx(int * rc) {
             return nullptr;
         }
         for (auto & e : c->ev) cudaEventCreate(&e);
+        if (cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_k, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_v, cudaEventDisableTiming) != cudaSuccess) {
+            delete c;
+            if (rc) *rc = KVC_ERR_CUDA;
+            return nullptr;
+        }
         g_ctx[dev] = c;
     }
     if (rc) *rc = KVC_OK;
@@ -463,6 +470,10 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     }
 
     if (phase) ctx->ph_used = 0;
+    if (n_jobs > 1)
+        for (int l = 0; l < n_jobs; l++)
+            if (jobs[l].v_host) return KVC_ERR_SHAPE;   // host-resident V: single-job calls only
+    bool v_upload = n_jobs == 1 && jobs[0].v_host != nullptr, v_pending = false;
 
     size_t pos = 0;
     while (pos < all.size()) {
@@ -540,6 +551,18 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             KVC_CUDA(cudaMalloc(&ctx->d_units, ctx->units_cap * sizeof(kvc_unit)));
         }
         KVC_CUDA(cudaMemcpyAsync(ctx->d_units, U.data(), U.size() * sizeof(kvc_unit), cudaMemcpyHostToDevice, st));
+        if (v_upload) {                              // after this call's small uploads, before the scoring
+            // the copy engine serves uploads in the order they become ready: make
+            // V wait for everything queued so far on the compute stream, or it
+            // would go ahead of the small uploads the scoring needs
+            KVC_CUDA(cudaEventRecord(ctx->ev_k, st));
+            KVC_CUDA(cudaStreamWaitEvent(ctx->copy_stream, ctx->ev_k, 0));
+            KVC_CUDA(cudaMemcpyAsync(jobs[0].v_dev, jobs[0].v_host, jobs[0].v_bytes, cudaMemcpyHostToDevice,
+                                     ctx->copy_stream));
+            KVC_CUDA(cudaEventRecord(ctx->ev_v, ctx->copy_stream));
+            v_upload = false;
+            v_pending = true;
+        }
         const int nu = (int)U.size();
         const kvc_unit * du = ctx->d_units;
 
@@ -558,6 +581,16 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             if ((rc = kvc_launch_select(du, nu, max_C, P, F, I, ctx->d_outs, st))) return rc;
         }
         if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
+        if (v_pending) {                             // values still in flight from the host
+            KVC_CUDA(cudaStreamWaitEvent(st, ctx->ev_v, 0));
+            if (jobs[0].v_quant) {
+                kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1);
+                if ((rc = kvc_launch_decode(jobs[0].v_quant, jobs[0].v_row_bytes, jobs[0].v_type,
+                                            const_cast<float *>(jobs[0].V), jobs[0].plan->T, H * dv, st)))
+                    return rc;
+            }
+            v_pending = false;
+        }
         {
             kvc_stage_timer tm(ctx, KVC_ST_PV, 1);
             if ((rc = kvc_launch_pv(du, nu, max_nq, P, F, st))) return rc;

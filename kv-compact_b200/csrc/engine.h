@@ -41,6 +41,17 @@ struct kvc_layer_job {
     const float * rkv_w = nullptr;  // [T] device R-KV weights or null
     const kvc_plan * plan = nullptr;
     kvc_layer_out out{};            // device outputs (sel, beta, cv, t_total)
+    // V still on the host (drop-in API, single job): once the engine has
+    // queued its own small uploads it copies v_host (v_bytes) to v_dev on the
+    // context's copy stream, overlapping the scoring; before the first stage
+    // that reads V it waits for that copy and, when v_quant is set (== v_dev,
+    // quantised rows), decodes it into V.
+    const void * v_host = nullptr;
+    void * v_dev = nullptr;
+    size_t v_bytes = 0;
+    const uint8_t * v_quant = nullptr;
+    size_t v_row_bytes = 0;
+    int v_type = 0;
 };
 
 struct kvc_phase_ms {
@@ -52,7 +63,9 @@ struct kvc_phase_ms {
 struct kvc_ctx {
     int device = -1;
     cudaStream_t stream = nullptr;
+    cudaStream_t copy_stream = nullptr;         // host->device uploads overlapping compute
     cudaEvent_t ev[4] = {};
+    cudaEvent_t ev_k = nullptr, ev_v = nullptr; // upload completion (no timing)
     std::mutex mu;
     void * arena[10] = {};
     size_t arena_cap[10] = {};
