@@ -470,6 +470,9 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     }
 
     if (phase) ctx->ph_used = 0;
+    bool rows_aligned = (dk % 4) == 0 && ((H * dk) % 4) == 0;
+    for (int l = 0; l < n_jobs; l++)
+        rows_aligned = rows_aligned && (((uintptr_t)jobs[l].K) & 15) == 0 && (((uintptr_t)jobs[l].Q) & 15) == 0;
     if (n_jobs > 1)
         for (int l = 0; l < n_jobs; l++)
             if (jobs[l].v_host) return KVC_ERR_SHAPE;   // host-resident V: single-job calls only
@@ -569,7 +572,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
         {
             kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1);
-            if ((rc = kvc_launch_score(du, nu, max_nq, max_C, P, F, I, 0, st))) return rc;
+            if ((rc = kvc_launch_score(du, nu, max_nq, max_C, P, F, I, 0, st, rows_aligned))) return rc;
         }
         {
             kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1);
@@ -602,7 +605,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             }
             {
                 kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1);     // raw S[:, sel]
-                if ((rc = kvc_launch_score(du, nu, max_nq, max_t, P, F, I, 1, st))) return rc;
+                if ((rc = kvc_launch_score(du, nu, max_nq, max_t, P, F, I, 1, st, rows_aligned))) return rc;
             }
             if (!p.skip_beta) {
                 kvc_stage_timer tm(ctx, KVC_ST_BETA, 2);

@@ -161,8 +161,12 @@ int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, 
                        kv_compact_stats * st);
 
 // Launchers (kernels in score.cu, select.cu, lsq.cu, nnls.cu, metrics.cu).
+// rows_aligned: every K / Q row the units read starts on a 16-byte boundary
+// (H*d_k and d_k multiples of 4, 16-byte aligned bases) — enables the
+// asynchronous-copy variant.
 int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_cols,
-                     const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st);
+                     const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st,
+                     bool rows_aligned = false);
 int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const kvc_params_dev & P,
                                   float * fs, cudaStream_t st);
 int kvc_launch_pv(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,

@@ -185,6 +185,155 @@ __global__ void __launch_bounds__(ST, 2) k_score(const kvc_unit * __restrict__ u
     }
 }
 
+// Same tile, operands staged with cp.async (requires 16-byte aligned rows:
+// d_k and H*d_k multiples of 4 and aligned K/Q bases). Two staging buffers
+// keep the next slab's rows in flight while the current slab is multiplied;
+// each slab is transposed shared-to-shared into the [k][row] layout the
+// float4 operand reads need. The arithmetic is that of k_score<128>.
+constexpr int AS_LD = SK + 4;   // staged row stride (floats): conflict-free float4 reads across rows
+
+__device__ __forceinline__ void cp_async16(void * smem, const void * gmem, int src_bytes) {
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(sa), "l"(gmem), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+size_t kvc_score_async_smem() {
+    return sizeof(float) * (2 * 2 * 128 * AS_LD + 2 * SK * (128 + 4));
+}
+
+__global__ void __launch_bounds__(ST, 2) k_score_async(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                       float * __restrict__ fs, const int * __restrict__ is,
+                                                       int mode) {
+    constexpr int TQ = 128, TK = 128, NTX = TK / 8;
+    const kvc_unit u = units[blockIdx.z];
+    if (!u.active) return;
+    const int h = blockIdx.y;
+    const int ncols = mode == 0 ? u.C : u.t;
+    const int tq = (u.nq + TQ - 1) / TQ, tk = (ncols + TK - 1) / TK;
+    if ((int)blockIdx.x >= tq * tk) return;
+    const int q0 = (blockIdx.x / tk) * TQ, j0 = (blockIdx.x % tk) * TK;
+    const int ek = P.H * P.dk, dk = P.dk;
+    const int * sel = is + u.sel_off;
+
+    extern __shared__ __align__(16) float dsm[];
+    float * Sq = dsm;                                   // [2][TQ][AS_LD] staged Q rows
+    float * Sk = Sq + 2 * TQ * AS_LD;                   // [2][TK][AS_LD] staged K rows
+    float (*Qs)[TQ + 4] = reinterpret_cast<float (*)[TQ + 4]>(Sk + 2 * TK * AS_LD);
+    float (*Ks)[TK + 4] = reinterpret_cast<float (*)[TK + 4]>(Sk + 2 * TK * AS_LD + SK * (TQ + 4));
+    __shared__ const float * qp[TQ];
+    __shared__ const float * kp[TK];
+    const int tid = threadIdx.x;
+    if (tid < TQ) {
+        const int q = q0 + tid;
+        qp[tid] = q < u.nq ? qrow_ptr(u, q, h, ek, dk) : nullptr;
+    } else {
+        const int j = j0 + tid - TQ;
+        if (j < ncols) {
+            const int key = mode == 0 ? j : sel[j];
+            kp[tid - TQ] = u.K + (long long)key * ek + (long long)h * dk;
+        } else {
+            kp[tid - TQ] = nullptr;
+        }
+    }
+    __syncthreads();
+    auto issue = [&](int d0, int b) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int e = tid + ST * i, r = e >> 3, c = (e & 7) * 4;
+            const float * pq = qp[r];
+            const float * pk = kp[r];
+            const int bq = (pq && d0 + c < dk) ? 16 : 0, bk = (pk && d0 + c < dk) ? 16 : 0;
+            cp_async16(Sq + (b * TQ + r) * AS_LD + c, bq ? pq + d0 + c : fs, bq);
+            cp_async16(Sk + (b * TK + r) * AS_LD + c, bk ? pk + d0 + c : fs, bk);
+        }
+        cp_async_commit();
+    };
+    const int ty = tid / NTX, tx = tid % NTX;
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+    const int nslab = (dk + SK - 1) / SK;
+    issue(0, 0);
+    if (nslab > 1) issue(SK, 1);
+    for (int s = 0; s < nslab; s++) {
+        const int b = s & 1;
+        if (s + 1 < nslab) cp_async_wait<1>();
+        else cp_async_wait<0>();
+        __syncthreads();                                // slab s staged; the previous slab's products are done
+        {
+            const int r = tid & (TQ - 1), c0 = (tid >> 7) * 16;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float4 vq = *reinterpret_cast<const float4 *>(Sq + (b * TQ + r) * AS_LD + c0 + 4 * i);
+                const float4 vk = *reinterpret_cast<const float4 *>(Sk + (b * TK + r) * AS_LD + c0 + 4 * i);
+                Qs[c0 + 4 * i + 0][r] = vq.x; Qs[c0 + 4 * i + 1][r] = vq.y;
+                Qs[c0 + 4 * i + 2][r] = vq.z; Qs[c0 + 4 * i + 3][r] = vq.w;
+                Ks[c0 + 4 * i + 0][r] = vk.x; Ks[c0 + 4 * i + 1][r] = vk.y;
+                Ks[c0 + 4 * i + 2][r] = vk.z; Ks[c0 + 4 * i + 3][r] = vk.w;
+            }
+        }
+        __syncthreads();                                // operands ready; staging buffer b free again
+        if (s + 2 < nslab) issue((s + 2) * SK, b);
+        const int kend = min(SK, dk - s * SK);
+        if (kend == SK) {
+#pragma unroll 4
+            for (int kk = 0; kk < SK; kk++) {
+                const float4 a0 = *reinterpret_cast<const float4 *>(&Qs[kk][4 * ty]);
+                const float4 a1 = *reinterpret_cast<const float4 *>(&Qs[kk][TQ / 2 + 4 * ty]);
+                const float4 b0 = *reinterpret_cast<const float4 *>(&Ks[kk][4 * tx]);
+                const float4 b1 = *reinterpret_cast<const float4 *>(&Ks[kk][TK / 2 + 4 * tx]);
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+            }
+        } else {
+            for (int kk = 0; kk < kend; kk++) {
+                const float4 a0 = *reinterpret_cast<const float4 *>(&Qs[kk][4 * ty]);
+                const float4 a1 = *reinterpret_cast<const float4 *>(&Qs[kk][TQ / 2 + 4 * ty]);
+                const float4 b0 = *reinterpret_cast<const float4 *>(&Ks[kk][4 * tx]);
+                const float4 b1 = *reinterpret_cast<const float4 *>(&Ks[kk][TK / 2 + 4 * tx]);
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+            }
+        }
+    }
+    const int ld = ncols;
+    float * out = fs + (mode == 0 ? u.s_off + (long long)h * u.nq * u.C : u.x_off + (long long)h * u.nq * u.t);
+    const bool vst = (ld & 3) == 0 && ((((uintptr_t)out) & 15) == 0);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int q = q0 + (i < 4 ? 4 * ty + i : TQ / 2 + 4 * ty + i - 4);
+        if (q >= u.nq) continue;
+        float * row = out + (long long)q * ld;
+#pragma unroll
+        for (int hb = 0; hb < 2; hb++) {
+            const int c = j0 + hb * (TK / 2) + 4 * tx;
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) v[e] = __fmul_rn(acc[i][4 * hb + e], P.isd);
+            if (vst && c + 4 <= ncols) {
+                *reinterpret_cast<float4 *>(row + c) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    if (c + e < ncols) row[c + e] = v[e];
+            }
+        }
+    }
+}
+
 // One CTA per (unit, head). Phase 1: one warp per row — max, exp, sum,
 // normalise in place. Phase 2: one thread per key — aggregate over queries.
 __global__ void __launch_bounds__(256) k_softmax_importance(const kvc_unit * __restrict__ units,
@@ -338,9 +487,15 @@ __global__ void __launch_bounds__(256) k_softmax_x(const kvc_unit * __restrict__
 }
 
 int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_cols,
-                     const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st) {
+                     const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st,
+                     bool rows_aligned) {
     if (n_units <= 0) return KVC_OK;
-    if (max_nq > 64) {
+    if (max_nq > 64 && rows_aligned) {
+        const int tiles = ((max_nq + 127) / 128) * ((max_cols + 127) / 128);
+        const size_t sm = kvc_score_async_smem();
+        KVC_CUDA(cudaFuncSetAttribute(k_score_async, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        k_score_async<<<dim3(tiles, P.H, n_units), ST, sm, st>>>(d_units, P, fs, is, mode);
+    } else if (max_nq > 64) {
         const int tiles = ((max_nq + 127) / 128) * ((max_cols + 127) / 128);
         k_score<128><<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs, is, mode);
     } else {
