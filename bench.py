@@ -181,12 +181,14 @@ def run_reference(args, cfg, name):
 
 # DRAM bytes per (layer, KV head) of 100k tokens measured by ncu for the
 # kernels that can dominate a step (dram__bytes_read.sum + dram__bytes_write.sum
-# of one launch over one cfg4 layer, divided by its 8 heads; the captures are
-# summarised in profiles/). None where no capture of the current kernel exists.
+# of one launch over one cfg4 layer, divided by its 8 heads), from the capture
+# summarised in profiles/main_kernels_cfg4_q8_1layer.md. Traffic grows in
+# proportion to the layers of a launch, so a full-step launch is scaled by 12.
 NCU_TRAFFIC_PER_LAYER_HEAD = {
-    "k_score": None,
-    "k_pv_tc": None,
-    "k_lsq_factor": None,
+    "k_score": (410.3e6 + 363.9e6) / 8,
+    "k_score_async": (410.3e6 + 363.9e6) / 8,
+    "k_pv_tc": (819.3e6 + 33.6e6) / 8,
+    "k_lsq_factor": (123.5e6 + 43.6e6) / 8,
 }
 
 
@@ -233,7 +235,7 @@ def stage_rooflines(stage_times, cfg, n_steps, clocks, peaks):
         outp += tu * d * (n if nq < tu else nq)
     per_lh = lambda x: x * H * L                  # noqa: E731
     model = {
-        "score": ("k_score", "fp32_issue", "T instr/s", 2.0 * nq * d * T * H * L, fp32_issue,
+        "score": ("k_score_async", "fp32_issue", "T instr/s", 2.0 * nq * d * T * H * L, fp32_issue,
                   "derived: 148 SMs x 128 FP32 lanes x max SM clock; bit-exact scores need a separate "
                   "rounded multiply and add per term (no FMA, no tensor cores)"),
         "refit_target": ("k_pv_tc", "hbm", "GB/s", 4.0 * (nq + d) * T * H * L + 4.0 * nq * d * H * L * len(units),

@@ -484,7 +484,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         std::vector<kvc_unit> U;
         long long fs = 0, is = 0, gs = 0;
         int max_nq = 1, max_C = 1, max_t = 1, max_n = 1;
-        bool any_primal = false, any_dual = false;
+        bool any_primal = false, any_dual = false, lsq_aligned = (dv % 4) == 0;
         size_t lsq_smem = 0;
         // R-KV weights live at the front of the float arena, per layer
         std::vector<long long> w_base(n_jobs, -1);
@@ -532,6 +532,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             max_n = std::max(max_n, n);
             if (pu.nq < pu.t) any_dual = true;
             else any_primal = true;
+            if (pu.t % 4) lsq_aligned = false;
             lsq_smem = std::max(lsq_smem, kvc_lsq_smem_bytes(n));
             U.push_back(u);
             pos++;
@@ -617,7 +618,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             }
             {
                 kvc_stage_timer tm(ctx, KVC_ST_LSQ, any_primal ? 2 : 1);
-                if ((rc = kvc_launch_lsq_gram(du, nu, max_n, max_t, P, F, G, ctx->d_outs, any_primal, st))) return rc;
+                if ((rc = kvc_launch_lsq_gram(du, nu, max_n, max_t, P, F, G, ctx->d_outs, any_primal, lsq_aligned, st))) return rc;
             }
             {
                 kvc_stage_timer tm(ctx, KVC_ST_LSQ_FACTOR, (max_n > 128 || dv > 128) ? 2 : 1);
@@ -625,7 +626,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             }
             {
                 kvc_stage_timer tm(ctx, KVC_ST_LSQ_OUT, any_dual ? 1 : 0);
-                if ((rc = kvc_launch_lsq_out(du, nu, max_t, P, F, G, ctx->d_outs, any_dual, st))) return rc;
+                if ((rc = kvc_launch_lsq_out(du, nu, max_t, P, F, G, ctx->d_outs, any_dual, lsq_aligned, st))) return rc;
             }
         }
         if (metric_partials) {

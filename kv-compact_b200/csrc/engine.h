@@ -185,14 +185,15 @@ size_t kvc_lsq_smem_bytes(int n);
 // factorisation + solves, output product (dual form).
 // `any_primal` / `any_dual`: whether some unit solves the primal (t <= n_q) /
 // dual form; launches only one form needs are skipped otherwise.
+// `aligned`: every unit's t and d_v are multiples of 4 (asynchronous-copy variant).
 int kvc_launch_lsq_gram(const kvc_unit * d_units, int n_units, int max_n, int max_t, const kvc_params_dev & P,
                         const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_primal,
-                        cudaStream_t st);
+                        bool aligned, cudaStream_t st);
 int kvc_launch_lsq_factor(const kvc_unit * d_units, int n_units, int max_n, size_t smem_bytes,
                           const kvc_params_dev & P, const float * fs, double * gs,
                           const kvc_layer_out * d_outs, cudaStream_t st);
 int kvc_launch_lsq_out(const kvc_unit * d_units, int n_units, int max_t, const kvc_params_dev & P,
-                       const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_dual,
+                       const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_dual, bool aligned,
                        cudaStream_t st);
 int kvc_metric_pairs(int H, int nq);
 size_t kvc_metric_scratch_floats(int H, int nq, int T, int t, int dv);

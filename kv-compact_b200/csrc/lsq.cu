@@ -180,6 +180,193 @@ __global__ void __launch_bounds__(128) k_dgemm(const kvc_unit * __restrict__ uni
     }
 }
 
+// Same products with the operands staged by cp.async in a three-slab ring
+// (requires t and d_v multiples of 4, so every 16-byte chunk of X, Y and Z rows
+// is aligned). Operands stay in their source layout in shared memory — rows of
+// X ([m][k], stride 20 floats) for the dual Gram matrix, [k][m] rows (stride
+// 72) otherwise — and are widened to fp64 as the MMA fragments are read
+// (exact). Two slabs are in flight while the third is multiplied. Chunks that
+// straddle the end of a row or of K copy only their valid bytes (the rest is
+// zero-filled), so nothing outside X, Y or Z is read and no stray k term
+// enters a product.
+constexpr int AK_LD = DK + 4;        // [m][k] fp32 rows
+constexpr int AM_LD = DT + 8;        // [k][m] rows (fp32 or fp64)
+constexpr int DG_NST = 3;
+constexpr int DG_STAGE_F = DT * AK_LD > DK * AM_LD ? DT * AK_LD : DK * AM_LD;   // floats per fp32 operand slab
+
+size_t kvc_dgemm_async_smem() {
+    // per stage: A (fp32) + B (fp32, or fp64 for Z)
+    return (size_t)DG_NST * (DG_STAGE_F * sizeof(float) + DK * AM_LD * sizeof(double));
+}
+
+__device__ __forceinline__ void dg_cp16(void * smem, const void * gmem, int bytes) {
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(sa), "l"(gmem), "r"(bytes) : "memory");
+}
+
+__global__ void __launch_bounds__(128) k_dgemm_async(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                     const float * __restrict__ fs, double * __restrict__ gs,
+                                                     const kvc_layer_out * __restrict__ outs, int mode) {
+    const kvc_unit u = units[blockIdx.z];
+    if (!u.active) return;
+    const int h = blockIdx.y;
+    const int nq = u.nq, t = u.t, dv = P.dv;
+    const bool dual = nq < t;
+    const int n = dual ? nq : t;
+    if ((mode == DG_RHS && dual) || (mode == DG_OUT && !dual)) return;
+    if (mode != DG_GRAM && (n > FN || dv > FN)) return;     // k_chol_solve does its own
+    int M, N, K;
+    if (mode == DG_GRAM) { M = n; N = n; K = dual ? t : nq; }
+    else { M = t; N = dv; K = nq; }
+    const int tn = (N + DT - 1) / DT, tm = (M + DT - 1) / DT;
+    if ((int)blockIdx.x >= tm * tn) return;
+    const int m0 = (blockIdx.x / tn) * DT, n0 = (blockIdx.x % tn) * DT;
+    if (mode == DG_GRAM && n0 > m0) return;
+    const float * X = fs + u.x_off + (long long)h * nq * t;
+    const float * Y = fs + u.y_off + (long long)h * nq * dv;
+    const double * Z = gs + u.z_off + (long long)h * n * dv;
+
+    extern __shared__ __align__(16) unsigned char dgsm[];
+    float * Asm = reinterpret_cast<float *>(dgsm);                                  // [NST][DG_STAGE_F]
+    double * Bsm = reinterpret_cast<double *>(dgsm + DG_NST * DG_STAGE_F * sizeof(float));  // [NST][DK*AM_LD]
+    const bool arows = (mode == DG_GRAM && dual);      // A = rows of X ([m][k])
+    const bool brows = arows;                          // B = rows of X too (X X^T)
+    const bool bz = (mode == DG_OUT);                  // B = Z (fp64)
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
+    const int fm = lane >> 2, fq = lane & 3;
+
+    // one slab: A 64 x 16 fp32 = 256 chunks, B 256 (fp32) or 512 (fp64) chunks of 16 bytes
+    auto issue = [&](int k0, int b) {
+        float * As = Asm + b * DG_STAGE_F;
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const int c = tid + 128 * i;               // 0..255
+            int bytes = 0;
+            const float * src = X;
+            float * dst;
+            if (arows) {                               // row m = c / 4, k quad c % 4
+                const int mm = c >> 2, kq = (c & 3) * 4, m = m0 + mm, k = k0 + kq;
+                dst = As + mm * AK_LD + kq;
+                if (m < M && k < K) { bytes = 4 * min(4, K - k); src = X + (long long)m * t + k; }
+            } else {                                   // k row c / 16, m quad c % 16
+                const int kk = c >> 4, mq = (c & 15) * 4, k = k0 + kk, m = m0 + mq;
+                dst = As + kk * AM_LD + mq;
+                if (k < K && m < M) { bytes = 4 * min(4, M - m); src = X + (long long)k * t + m; }
+            }
+            dg_cp16(dst, src, bytes);
+        }
+        if (bz) {
+            double * Bs = Bsm + b * (DK * AM_LD);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int c = tid + 128 * i;           // 0..511: k row c / 32, n pair c % 32
+                const int kk = c >> 5, np = (c & 31) * 2, k = k0 + kk, nn = n0 + np;
+                int bytes = 0;
+                const double * src = Z;
+                if (k < K && nn < N) { bytes = 8 * min(2, N - nn); src = Z + (long long)k * dv + nn; }
+                dg_cp16(Bs + kk * AM_LD + np, src, bytes);
+            }
+        } else {
+            float * Bs = reinterpret_cast<float *>(Bsm + b * (DK * AM_LD));
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int c = tid + 128 * i;
+                int bytes = 0;
+                const float * src = X;
+                float * dst;
+                if (brows) {
+                    const int nn = c >> 2, kq = (c & 3) * 4, col = n0 + nn, k = k0 + kq;
+                    dst = Bs + nn * AK_LD + kq;
+                    if (col < N && k < K) { bytes = 4 * min(4, K - k); src = X + (long long)col * t + k; }
+                } else {
+                    const int kk = c >> 4, nq4 = (c & 15) * 4, k = k0 + kk, col = n0 + nq4;
+                    dst = Bs + kk * AM_LD + nq4;
+                    if (k < K && col < N) {
+                        bytes = 4 * min(4, N - col);
+                        src = (mode == DG_RHS) ? Y + (long long)k * dv + col : X + (long long)k * t + col;
+                    }
+                }
+                dg_cp16(dst, src, bytes);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    double acc[4][4][2];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j][0] = acc[i][j][1] = 0.0;
+    const int nslab = (K + DK - 1) / DK;
+    issue(0, 0);
+    if (nslab > 1) issue(DK, 1);
+    for (int s = 0; s < nslab; s++) {
+        if (s + 1 < nslab) asm volatile("cp.async.wait_group 1;" ::: "memory");
+        else asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();                               // slab s visible; slab s-1 no longer read
+        if (s + 2 < nslab) issue((s + 2) * DK, (s + 2) % DG_NST);
+        const int b = s % DG_NST;
+        const float * As = Asm + b * DG_STAGE_F;
+        const double * Bd = Bsm + b * (DK * AM_LD);
+        const float * Bf = reinterpret_cast<const float *>(Bd);
+#pragma unroll
+        for (int kk = 0; kk < DK; kk += 4) {
+            double a[4], bb[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int m = wm + 8 * i + fm, nn = wn + 8 * i + fm, k = kk + fq;
+                a[i] = arows ? (double)As[m * AK_LD + k] : (double)As[k * AM_LD + m];
+                bb[i] = bz ? Bd[k * AM_LD + nn] : (brows ? (double)Bf[nn * AK_LD + k] : (double)Bf[k * AM_LD + nn]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) dmma(acc[i][j], a[i], bb[j]);
+        }
+    }
+    if (mode == DG_GRAM) {
+        double * G = gs + u.g_off + (long long)h * n * n;
+        const double ridge = (double)P.ridge;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int v = 0; v < 2; v++) {
+                    const int a = m0 + wm + 8 * i + fm, b = n0 + wn + 8 * j + 2 * fq + v;
+                    if (a < n && b < n && b <= a) {
+                        const double x = acc[i][j][v] + (a == b ? ridge : 0.0);
+                        G[(long long)a * n + b] = x;
+                        G[(long long)b * n + a] = x;
+                    }
+                }
+    } else if (mode == DG_RHS) {
+        double * R = gs + u.z_off + (long long)h * n * dv;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int v = 0; v < 2; v++) {
+                    const int a = m0 + wm + 8 * i + fm, c = n0 + wn + 8 * j + 2 * fq + v;
+                    if (a < M && c < N) R[(long long)a * dv + c] = acc[i][j][v];
+                }
+    } else {
+        const kvc_layer_out lo = outs[u.layer];
+        float * cv = lo.cv + ((long long)h * lo.t_total + u.out_off) * dv;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int v = 0; v < 2; v++) {
+                    const int a = m0 + wm + 8 * i + fm, c = n0 + wn + 8 * j + 2 * fq + v;
+                    if (a < M && c < N) cv[(long long)a * dv + c] = (float)acc[i][j][v];
+                }
+    }
+}
+
 // Panel width for n unknowns: keeps the n x PW fp64 panel within 96 KB.
 __host__ __device__ inline int lsq_panel(int n) { return n <= 384 ? 32 : (n <= 1536 ? 8 : 4); }
 
@@ -501,17 +688,29 @@ size_t kvc_lsq_smem_bytes(int n) {
     return b;
 }
 
+static int launch_dgemm(dim3 grid, const kvc_unit * d_units, const kvc_params_dev & P, const float * fs,
+                        double * gs, const kvc_layer_out * d_outs, int mode, bool aligned, cudaStream_t st) {
+    if (aligned) {
+        const size_t sm = kvc_dgemm_async_smem();
+        KVC_CUDA(cudaFuncSetAttribute(k_dgemm_async, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        k_dgemm_async<<<grid, 128, sm, st>>>(d_units, P, fs, gs, d_outs, mode);
+    } else {
+        k_dgemm<<<grid, 128, 0, st>>>(d_units, P, fs, gs, d_outs, mode);
+    }
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
 int kvc_launch_lsq_gram(const kvc_unit * d_units, int n_units, int max_n, int max_t, const kvc_params_dev & P,
                         const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_primal,
-                        cudaStream_t st) {
+                        bool aligned, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
     const int tg = (max_n + DT - 1) / DT;
-    k_dgemm<<<dim3(tg * tg, P.H, n_units), 128, 0, st>>>(d_units, P, fs, gs, d_outs, DG_GRAM);
-    KVC_CUDA(cudaGetLastError());
+    int rc;
+    if ((rc = launch_dgemm(dim3(tg * tg, P.H, n_units), d_units, P, fs, gs, d_outs, DG_GRAM, aligned, st))) return rc;
     if (any_primal) {
         const int to = ((max_t + DT - 1) / DT) * ((P.dv + DT - 1) / DT);
-        k_dgemm<<<dim3(to, P.H, n_units), 128, 0, st>>>(d_units, P, fs, gs, d_outs, DG_RHS);
-        KVC_CUDA(cudaGetLastError());
+        if ((rc = launch_dgemm(dim3(to, P.H, n_units), d_units, P, fs, gs, d_outs, DG_RHS, aligned, st))) return rc;
     }
     return KVC_OK;
 }
@@ -533,11 +732,9 @@ int kvc_launch_lsq_factor(const kvc_unit * d_units, int n_units, int max_n, size
 }
 
 int kvc_launch_lsq_out(const kvc_unit * d_units, int n_units, int max_t, const kvc_params_dev & P,
-                       const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_dual,
+                       const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_dual, bool aligned,
                        cudaStream_t st) {
     if (n_units <= 0 || !any_dual) return KVC_OK;
     const int to = ((max_t + DT - 1) / DT) * ((P.dv + DT - 1) / DT);
-    k_dgemm<<<dim3(to, P.H, n_units), 128, 0, st>>>(d_units, P, fs, gs, d_outs, DG_OUT);
-    KVC_CUDA(cudaGetLastError());
-    return KVC_OK;
+    return launch_dgemm(dim3(to, P.H, n_units), d_units, P, fs, gs, d_outs, DG_OUT, aligned, st);
 }
