@@ -551,41 +551,37 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
         const int prt = (k >> 3) & 3, pr0 = k & 7;
         // ---- A1: P^-1 and the new pivot rows of G (warps 0-3); multipliers; old pivot rows of R
         if (tid < 128) {
-            double a[4][4], T[4][4];
+            // in-place Gauss-Jordan inversion of the pivot block; a skipped
+            // (non-positive) pivot leaves its row and column to be zeroed
+            double T[4][4];
 #pragma unroll
             for (int q = 0; q < 4; q++)
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    a[q][c] = G[(k + q) * GLD + k + c];
-                    T[q][c] = (q == c) ? 1.0 : 0.0;
-                }
+                for (int c = 0; c < 4; c++) T[q][c] = G[(k + q) * GLD + k + c];
             bool skip[4];
 #pragma unroll
             for (int q = 0; q < 4; q++) {
-                const double piv = a[q][q];
+                const double piv = T[q][q];
                 skip[q] = !(piv > 0.0 && isfinite(piv));
-                const double ip = skip[q] ? 0.0 : 1.0 / piv;
+                if (skip[q]) continue;
+                const double ip = 1.0 / piv;
+                T[q][q] = 1.0;
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    a[q][c] *= ip;
-                    T[q][c] *= ip;
-                }
+                for (int c = 0; c < 4; c++) T[q][c] *= ip;
 #pragma unroll
                 for (int r2 = 0; r2 < 4; r2++) {
                     if (r2 == q) continue;
-                    const double f = skip[q] ? 0.0 : a[r2][q];
+                    const double f = T[r2][q];
+                    T[r2][q] = 0.0;
 #pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        a[r2][c] = fma(-f, a[q][c], a[r2][c]);
-                        T[r2][c] = fma(-f, T[q][c], T[r2][c]);
-                    }
+                    for (int c = 0; c < 4; c++) T[r2][c] = fma(-f, T[q][c], T[r2][c]);
                 }
             }
 #pragma unroll
             for (int q = 0; q < 4; q++)
                 if (skip[q])
 #pragma unroll
-                    for (int c = 0; c < 4; c++) T[q][c] = 0.0;
+                    for (int c = 0; c < 4; c++) T[q][c] = T[c][q] = 0.0;
             if (tid == 0)
 #pragma unroll
                 for (int q = 0; q < 16; q++) Ts[q] = T[q >> 2][q & 3];
@@ -631,15 +627,20 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
         }
         __syncthreads();
         // ---- B: rank-4 updates (pivot rows have zero multipliers)
-        if (8 * warp < n8) {                     // G: row tile `warp`, every column tile from jt0
+        if (8 * warp < n8) {                     // G: row tile `warp`, column tiles from jt0, two at a time
             const double am = -M[(8 * warp + fr) * 4 + fq];
-            for (int ct = jt0; ct < (n8 >> 3); ct++) {
-                const double b = PR[fq * PLD + 8 * ct + fr];
-                double2 * cp = reinterpret_cast<double2 *>(G + (8 * warp + fr) * GLD + 8 * ct + 2 * fq);
-                const double2 c2 = *cp;
-                double cc[2] = {c2.x, c2.y};
-                dmma(cc, am, b);
-                *cp = make_double2(cc[0], cc[1]);
+            const int nct = n8 >> 3;
+            for (int ct0 = jt0; ct0 < nct; ct0 += 2) {
+                const int ct1 = min(ct0 + 1, nct - 1);
+                double2 * cp0 = reinterpret_cast<double2 *>(G + (8 * warp + fr) * GLD + 8 * ct0 + 2 * fq);
+                double2 * cp1 = reinterpret_cast<double2 *>(G + (8 * warp + fr) * GLD + 8 * ct1 + 2 * fq);
+                const double b0 = PR[fq * PLD + 8 * ct0 + fr], b1 = PR[fq * PLD + 8 * ct1 + fr];
+                const double2 c0 = *cp0, c1 = *cp1;
+                double cc0[2] = {c0.x, c0.y}, cc1[2] = {c1.x, c1.y};
+                dmma(cc0, am, b0);
+                dmma(cc1, am, b1);
+                *cp0 = make_double2(cc0[0], cc0[1]);
+                if (ct0 + 1 < nct) *cp1 = make_double2(cc1[0], cc1[1]);
             }
         }
         {                                        // R: this warp's 4x4 tiles
