@@ -36,7 +36,7 @@ sys.path.insert(0, os.path.join(REPO, "kv-compact_b200", "python"))
 
 import numpy as np  # noqa: E402
 
-from kvc_b200 import ORACLE_PATH, REF_PATH, abi, workloads  # noqa: E402
+from kvc_b200 import ORACLE_PATH, REF_PATH, abi, dist as kdist, workloads  # noqa: E402
 
 CONFIGS = {
     "cfg4_q8": dict(n_layers=48, interval=4, T=100_000, H=8, d=128, ktype=abi.KV_TYPE_Q8_0,
@@ -145,7 +145,7 @@ def cpu_sample(cfg, Kq_h, Vq_h, Q_h, max_seconds=30.0):
 
 
 def run_reference(args, cfg, name):
-    rank = int(os.environ.get("RANK", "0"))
+    rank, _, _ = kdist.env_ranks()
     if rank != 0:
         return
     import torch
@@ -279,22 +279,17 @@ def roofline_entry(stage_times, cfg, n_steps, clocks, peaks):
 
 def run_kvc(args, cfg, name):
     import torch
-    import torch.distributed as dist
     from kvc_b200 import lib
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, world, local = kdist.env_ranks()
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device")
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    kdist.init("nccl", device)
     fns = lib.load()
     T, H, d = cfg["T"], cfg["H"], cfg["d"]
-    Kq, Vq, Q = make_layers(cfg, 1000 + rank, device, fns)
+    Kq, Vq, Q = make_layers(cfg, kdist.rank_seed(1000, rank), device, fns)
     params = abi.make_params(fns, target_ratio=cfg["ratio"])
     model = lib.BatchedModel(fns, Kq, Vq, Q, T, H, d, d, cfg["ktype"], cfg["vtype"], params)
     for _ in range(args.warmup):
@@ -302,8 +297,7 @@ def run_kvc(args, cfg, name):
     torch.cuda.synchronize()
     lib.profile(fns, True)
     launches0 = fns["_lib"].kvc_launch_count()
-    if world > 1:
-        dist.barrier()
+    kdist.barrier(world)
     torch.cuda.synchronize()
     try:
         uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
@@ -321,12 +315,9 @@ def run_kvc(args, cfg, name):
     launches = fns["_lib"].kvc_launch_count() - launches0
     stages = lib.profile(fns, False)
     ms = e0.elapsed_time(e1) / args.steps
-    t_max = torch.tensor([ms], device=device)
-    if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-        dist.barrier()
-    ms_max = float(t_max.item())
-    value = world * T / (ms_max * 1e-3)
+    ms_max = kdist.max_over_ranks(ms, world, device)
+    kdist.barrier(world)
+    value = kdist.job_tokens_per_s(world, T, ms_max)
 
     # ---- end to end through the drop-in C ABI, host buffers, copies timed
     e2e = None
@@ -355,8 +346,7 @@ def run_kvc(args, cfg, name):
 
         e2e_step()
         n_e2e = max(1, min(args.steps, 3))
-        if world > 1:
-            dist.barrier()
+        kdist.barrier(world)
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record()
@@ -364,12 +354,9 @@ def run_kvc(args, cfg, name):
             h2d, d2h = e2e_step()
         f1.record()
         torch.cuda.synchronize()
-        e_ms = f0.elapsed_time(f1) / n_e2e
-        te = torch.tensor([e_ms], device=device)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": world * T / (float(te.item()) * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "ms_per_step": float(te.item()), "steps": n_e2e,
+        e_ms = kdist.max_over_ranks(f0.elapsed_time(f1) / n_e2e, world, device)
+        e2e = {"value": kdist.job_tokens_per_s(world, T, e_ms), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "steps": n_e2e,
                "path": "kv_compact_quantized per filtered layer, pinned host inputs"}
 
     # ---- CPU baseline on the host cores (rank 0, N=1 only)
@@ -399,9 +386,7 @@ def run_kvc(args, cfg, name):
                                for k, v in roof_all.items()},
         }
         print(json.dumps(line))
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    kdist.finish(world)
 
 
 def main():
