@@ -21,6 +21,8 @@ def init(backend, device=None, timeout_s=300):
     """Join the process group when there is more than one rank; returns (rank, world)."""
     import torch.distributed as dist
     rank, world, _ = env_ranks()
+    # keep stdout to the benchmark's single JSON line (NCCL would add its version banner)
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     if world > 1 and not dist.is_initialized():
         kw = {"timeout": datetime.timedelta(seconds=timeout_s)}
         if device is not None and backend == "nccl":
