@@ -357,12 +357,12 @@ struct unit_sizes {
     long long fs, is, gs;
 };
 
-static unit_sizes sizes_of(const kvc_plan_unit & u, int H, int dv) {
+static unit_sizes sizes_of(const kvc_plan_unit & u, int H, int dv, bool omp) {
     unit_sizes s;
     const int n = std::min(u.nq, u.t);
-    (void)n;
     s.fs = al32((long long)H * u.nq * u.C) + al32((long long)(2 * H + 1) * u.C) + al32((long long)2 * H * u.nq) +
            al32((long long)H * u.nq * dv) + al32((long long)H * u.nq * u.t) + al32((long long)2 * H * u.nq);
+    if (omp) s.fs += al32((long long)kvc_omp_floats(u.C, u.t, u.nq, H));
     s.is = al32(u.t) + al32(4LL * u.C);
     s.gs = al32((long long)H * n * n) + al32((long long)H * n * dv);
     return s;
@@ -374,10 +374,6 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     cudaStream_t st = ctx->stream;
     if (p.use_sensitivity && H > 64) return KVC_ERR_SHAPE;
     if (dk > KVC_MAX_D || dv > KVC_MAX_D) return KVC_ERR_SHAPE;
-    if (p.use_omp) {
-        fprintf(stderr, "[kvc] OMP key selection is not available on the device path\n");
-        return KVC_ERR_SHAPE;
-    }
 
     kvc_params_dev P;
     P.H = H; P.dk = dk; P.dv = dv;
@@ -391,6 +387,9 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     P.nnls_pgd_iters = p.nnls_pgd_iters;
     P.ridge = p.ridge;
     P.isd = 1.0f / sqrtf((float)dk);
+    P.use_omp = p.use_omp ? 1 : 0;
+    P.omp_k_choice = p.omp_k_choice;
+    P.omp_refit_interval = p.omp_refit_interval;
 
     // ---- layer outputs table
     if (ctx->outs_cap < (size_t)n_jobs) {
@@ -444,7 +443,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         if (jobs[l].rkv_w) fs_all += al32(jobs[l].plan->T);
     for (const ref & rf : all) {
         const kvc_plan_unit & pu = jobs[rf.l].plan->units[rf.i];
-        const unit_sizes us = sizes_of(pu, H, dv);
+        const unit_sizes us = sizes_of(pu, H, dv, p.use_omp != 0);
         fs_all += us.fs;
         is_all += us.is;
         const int n = std::min(pu.nq, pu.t);
@@ -493,7 +492,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         size_t first = pos;
         while (pos < all.size()) {
             const kvc_plan_unit & pu = jobs[all[pos].l].plan->units[all[pos].i];
-            unit_sizes s = sizes_of(pu, H, dv);
+            unit_sizes s = sizes_of(pu, H, dv, p.use_omp != 0);
             long long bytes = (fs + s.fs) * 4 + (is + s.is) * 4 + (gs + s.gs) * 8;
             if (pos > first && bytes > budget) break;
             const kvc_layer_job & J = jobs[all[pos].l];
@@ -517,6 +516,8 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             u.y_off = fs; fs += al32((long long)H * pu.nq * dv);
             u.x_off = fs; fs += al32((long long)H * pu.nq * pu.t);
             u.xs_off = fs; fs += al32((long long)2 * H * pu.nq);
+            u.omp_off = -1;
+            if (p.use_omp) { u.omp_off = fs; fs += al32((long long)kvc_omp_floats(pu.C, pu.t, pu.nq, H)); }
             u.w_off = w_base[u.layer] >= 0 ? w_base[u.layer] + pu.start : -1;
             u.sel_off = is; is += al32(pu.t);
             u.c_off = is; is += al32(4LL * pu.C);
@@ -575,6 +576,10 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1);
             if ((rc = kvc_launch_score(du, nu, max_nq, max_C, P, F, I, 0, st, rows_aligned))) return rc;
         }
+        if (P.use_omp) {                             // needs the raw scores: before the softmax
+            kvc_stage_timer tm(ctx, KVC_ST_SELECT, 1);
+            if ((rc = kvc_launch_omp_exp(du, nu, P, F, st))) return rc;
+        }
         {
             kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1);
             if ((rc = kvc_launch_softmax_importance(du, nu, P, F, st))) return rc;
@@ -582,7 +587,11 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         {
             kvc_stage_timer tm(ctx, KVC_ST_SELECT, 2);
             if ((rc = kvc_launch_aggregate(du, nu, P, F, st))) return rc;
-            if ((rc = kvc_launch_select(du, nu, max_C, P, F, I, ctx->d_outs, st))) return rc;
+            if (P.use_omp) {
+                if ((rc = kvc_launch_omp_select(du, nu, P, F, I, ctx->d_outs, st))) return rc;
+            } else if ((rc = kvc_launch_select(du, nu, max_C, P, F, I, ctx->d_outs, st))) {
+                return rc;
+            }
         }
         if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
         if (v_pending) {                             // values still in flight from the host

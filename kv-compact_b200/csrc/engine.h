@@ -204,6 +204,10 @@ size_t kvc_metric_partial_floats(int n_chunks, int H, int nq, int dv);
 int kvc_launch_metric_partial(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, const float * fs,
                               const kvc_layer_out * d_outs, cudaStream_t st);
 int kvc_launch_metric_merge(const float * mpart, int n_chunks, int H, int nq, int dv, float * res, cudaStream_t st);
+size_t kvc_omp_floats(int C, int t, int nq, int H);
+int kvc_launch_omp_exp(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, cudaStream_t st);
+int kvc_launch_omp_select(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, int * is,
+                          const kvc_layer_out * d_outs, cudaStream_t st);
 int kvc_launch_gather_rows(const float * src, int src_stride, const int * idx, int rows, int n,
                            float * dst, int dst_stride, cudaStream_t st);
 int kvc_launch_cheap_q(const float * K, int T, int ek, int nq, float * Q, cudaStream_t st);

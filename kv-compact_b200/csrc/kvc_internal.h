@@ -75,6 +75,7 @@ struct kvc_unit {
     long long w_off;      // floats: C R-KV weights (or -1: none)
     long long c_off;      // ints/floats: C per-candidate scratch (selection)
     long long xs_off;     // floats: H blocks of 2*nq (row max, row sum of X before normalising)
+    long long omp_off;    // floats: OMP selection working arrays (omp.cu), or -1
 };
 
 struct kvc_layer_out {
@@ -98,6 +99,9 @@ struct kvc_params_dev {
     int nnls_pgd_iters;
     float ridge;
     float isd;            // 1/sqrtf(d_k), computed as the reference does
+    int use_omp;
+    int omp_k_choice;
+    int omp_refit_interval;
 };
 
 // f32 arithmetic that is never contracted into FMA, on host and device.

@@ -13,8 +13,8 @@ from kvc_b200 import abi
 
 pytestmark = pytest.mark.gpu
 
-# options not yet on the device path
-UNSUPPORTED = {"use_omp"}
+# options not on the device path
+UNSUPPORTED = set()
 
 
 def supported(case):
@@ -50,7 +50,8 @@ def test_golden_parity(kvc, oracle, name):
     if meta["kind"] == "multi_round":
         # indices map through two rounds; require the set to agree exactly
         np.testing.assert_array_equal(out["indices"], case["indices"])
-    elif p.get("use_diversity"):
+    elif p.get("use_diversity") or p.get("use_omp"):
+        # greedy selections (diversity, OMP): the index sets must agree exactly
         np.testing.assert_array_equal(out["indices"], case["indices"])
     else:
         imp = oracle_importance(oracle, case)
