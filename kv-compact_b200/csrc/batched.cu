@@ -177,7 +177,7 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
         }
         if (R[l].V_out) {
             kvc_stage_timer tm(ctx, KVC_ST_REQUANT, 1);
-            if ((rc = kvc_launch_encode_heads(R[l].C_v, H, t, dv, m->v_type, R[l].V_out, m->v_row_bytes, st)))
+            if ((rc = kvc_launch_encode_heads(R[l].C_v, H, t, t, dv, m->v_type, R[l].V_out, m->v_row_bytes, st)))
                 return rc;
         }
         memset(&R[l].stats, 0, sizeof(R[l].stats));

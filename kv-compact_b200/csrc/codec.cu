@@ -385,13 +385,14 @@ __global__ void k_encode_gather(const float * __restrict__ src, size_t stride,
     }
 }
 
-// V_out rows: row j, element e = h*dv + k comes from cv[h][j][k].
-__global__ void k_encode_heads(const float * __restrict__ cv, int H, int t, int dv, int type,
+// V_out rows: row j (of `rows`), element e = h*dv + k comes from
+// cv[h][j][k], heads `t` rows apart.
+__global__ void k_encode_heads(const float * __restrict__ cv, int H, int t, int rows, int dv, int type,
                                uint8_t * __restrict__ dst, size_t drb) {
     const int n = H * dv;
     if (dev_is_block(type)) {
         const int nb = n / QK, bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
-        const long long total = (long long)t * nb * 8;
+        const long long total = (long long)rows * nb * 8;
         for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < warp_round(total);
              i += (long long)gridDim.x * blockDim.x) {
             const bool live = i < total;
@@ -414,7 +415,7 @@ __global__ void k_encode_heads(const float * __restrict__ cv, int H, int t, int 
         }
         return;
     }
-    const long long total = (long long)t * n;
+    const long long total = (long long)rows * n;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
         const long long j = i / n;
@@ -436,11 +437,11 @@ int kvc_launch_encode_gather(const float * src, size_t stride, const int * idx, 
     return KVC_OK;
 }
 
-int kvc_launch_encode_heads(const float * cv, int H, int t, int dv, int type, uint8_t * dst,
+int kvc_launch_encode_heads(const float * cv, int H, int t, int rows, int dv, int type, uint8_t * dst,
                             size_t drb, cudaStream_t st) {
-    if (t <= 0) return KVC_OK;
-    long long work = (long long)t * (is_block(type) ? ((H * dv) / QK) * 8 : H * dv);
-    k_encode_heads<<<grid_for(work, 256), 256, 0, st>>>(cv, H, t, dv, type, dst, drb);
+    if (rows <= 0) return KVC_OK;
+    long long work = (long long)rows * (is_block(type) ? ((H * dv) / QK) * 8 : H * dv);
+    k_encode_heads<<<grid_for(work, 256), 256, 0, st>>>(cv, H, t, rows, dv, type, dst, drb);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }

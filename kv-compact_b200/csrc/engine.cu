@@ -154,12 +154,20 @@ kvc_ctx * kvc_get_ctx(int * rc) {
         }
         for (auto & e : c->ev) cudaEventCreate(&e);
         if (cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
-            cudaEventCreateWithFlags(&c->ev_k, cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&c->ev_v, cudaEventDisableTiming) != cudaSuccess) {
+            cudaStreamCreateWithFlags(&c->d2h_stream, cudaStreamNonBlocking) != cudaSuccess) {
             delete c;
             if (rc) *rc = KVC_ERR_CUDA;
             return nullptr;
         }
+        bool ok = true;
+        for (auto & gs : c->group_stream) ok = ok && cudaStreamCreateWithFlags(&gs, cudaStreamNonBlocking) == cudaSuccess;
+        if (!ok) {
+            delete c;
+            if (rc) *rc = KVC_ERR_CUDA;
+            return nullptr;
+        }
+        const char * tr = getenv("KVC_TRACE");
+        c->trace = tr && atoi(tr) > 0;
         g_ctx[dev] = c;
     }
     if (rc) *rc = KVC_OK;
@@ -195,6 +203,42 @@ int kvc_wait(kvc_ctx * ctx) {
         return KVC_ERR_CUDA;
     }
     return KVC_OK;
+}
+
+void kvc_trace(kvc_ctx * ctx, const std::string & label, cudaStream_t st) {
+    if (!ctx->trace) return;
+    if (ctx->trace_used == ctx->trace_ev.size()) {
+        cudaEvent_t e = nullptr;
+        cudaEventCreate(&e);
+        ctx->trace_ev.push_back(e);
+        ctx->trace_label.emplace_back();
+    }
+    ctx->trace_label[ctx->trace_used] = label;
+    cudaEventRecord(ctx->trace_ev[ctx->trace_used++], st);
+}
+
+void kvc_trace_dump(kvc_ctx * ctx) {
+    if (!ctx->trace || ctx->trace_used == 0) return;
+    std::string line = "[kvc trace]";
+    for (size_t i = 0; i < ctx->trace_used; i++) {
+        float ms = 0.0f;
+        cudaEventSynchronize(ctx->trace_ev[i]);
+        cudaEventElapsedTime(&ms, ctx->trace_ev[0], ctx->trace_ev[i]);
+        char buf[96];
+        snprintf(buf, sizeof buf, " %s=%.3f", ctx->trace_label[i].c_str(), ms);
+        line += buf;
+    }
+    fprintf(stderr, "%s\n", line.c_str());
+    ctx->trace_used = 0;
+}
+
+cudaEvent_t kvc_sync_event(kvc_ctx * ctx) {
+    if (ctx->sync_used == ctx->sync_ev.size()) {
+        cudaEvent_t e = nullptr;
+        cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+        ctx->sync_ev.push_back(e);
+    }
+    return ctx->sync_ev[ctx->sync_used++];
 }
 
 int kvc_pinned(kvc_ctx * ctx, size_t bytes, void ** out) {
@@ -275,17 +319,18 @@ static cudaEvent_t next_event(kvc_ctx * ctx, int * idx) {
     return ctx->ev_pool[ctx->ev_used++];
 }
 
-kvc_stage_timer::kvc_stage_timer(kvc_ctx * c, int s, int n_launch) : ctx(c), stage(s) {
+kvc_stage_timer::kvc_stage_timer(kvc_ctx * c, int s, int n_launch, cudaStream_t st)
+    : ctx(c), stage(s), stream(st ? st : c->stream) {
     ctx->launches += (uint64_t)n_launch;
     ctx->stage_launches[s] += (uint64_t)n_launch;
     if (!ctx->profiling) return;
-    cudaEventRecord(next_event(ctx, &first), ctx->stream);
+    cudaEventRecord(next_event(ctx, &first), stream);
 }
 
 kvc_stage_timer::~kvc_stage_timer() {
     if (first < 0) return;
     int second;
-    cudaEventRecord(next_event(ctx, &second), ctx->stream);
+    cudaEventRecord(next_event(ctx, &second), stream);
     ctx->pending.push_back({stage, first});
 }
 
@@ -434,10 +479,41 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     for (int l = 0; l < n_jobs; l++)
         for (int i = 0; i < (int)jobs[l].plan->units.size(); i++) all.push_back({l, i});
 
+    kvc_stream_io * io = nullptr;
+    for (int l = 0; l < n_jobs; l++)
+        if (jobs[l].io) {
+            if (n_jobs > 1) return KVC_ERR_SHAPE;   // host-resident inputs: single-job calls only
+            io = jobs[l].io;
+        }
+    // a streamed job is cut into at most io->max_groups groups of consecutive
+    // units whose sizes shrink by io->size_ratio from one to the next (each
+    // at least one unit); group_end[g] is one past the last unit of group g
+    std::vector<size_t> group_end;
+    if (io && io->max_groups > 1 && all.size() > 1) {
+        const int g_n = (int)std::min<size_t>((size_t)io->max_groups, all.size());
+        const double q = io->size_ratio > 0.0 ? io->size_ratio : 1.0;
+        double wsum = 0.0, w = 1.0;
+        for (int g = 0; g < g_n; g++, w *= q) wsum += w;
+        size_t end = 0;
+        w = 1.0;
+        double acc = 0.0;
+        for (int g = 0; g < g_n; g++, w *= q) {
+            acc += w;
+            size_t e = (g == g_n - 1) ? all.size() : (size_t)llround(acc / wsum * (double)all.size());
+            e = std::max(e, end + 1);
+            e = std::min(e, all.size() - (size_t)(g_n - 1 - g));     // leave one unit per later group
+            group_end.push_back(e);
+            end = e;
+        }
+    } else {
+        group_end.push_back(all.size());
+    }
+
     // Scratch of all units at once, counted as the batch loop below places it.
     // When the arenas already hold that much (every call after the first on
-    // the same shapes) the whole job is one batch and the device is not
-    // queried: cudaMemGetInfo can take tens of milliseconds on a busy host.
+    // the same shapes) the whole job is one batch (or, streamed, groups with
+    // scratch of their own) and the device is not queried: cudaMemGetInfo can
+    // take tens of milliseconds on a busy host.
     long long fs_all = 0, is_all = 0, gs_all = 0;
     for (int l = 0; l < n_jobs; l++)
         if (jobs[l].rkv_w) fs_all += al32(jobs[l].plan->T);
@@ -469,31 +545,54 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     }
 
     if (phase) ctx->ph_used = 0;
+    ctx->sync_used = 0;
     bool rows_aligned = (dk % 4) == 0 && ((H * dk) % 4) == 0;
     for (int l = 0; l < n_jobs; l++)
         rows_aligned = rows_aligned && (((uintptr_t)jobs[l].K) & 15) == 0 && (((uintptr_t)jobs[l].Q) & 15) == 0;
-    if (n_jobs > 1)
-        for (int l = 0; l < n_jobs; l++)
-            if (jobs[l].v_host) return KVC_ERR_SHAPE;   // host-resident V: single-job calls only
-    bool v_upload = n_jobs == 1 && jobs[0].v_host != nullptr, v_pending = false;
 
+    // Groups of a streamed job run concurrently (scoring of one beside the
+    // refit of the previous) when the whole job's scratch fits: each group
+    // then keeps scratch of its own.
+    const bool concurrent = io && (fs_all * 4 + is_all * 4 + gs_all * 8) <= budget;
+
+    // ---- batches of consecutive units, each within the scratch budget; a
+    // streamed job is also cut into at most io->max_groups groups. All
+    // batches are laid out before anything is queued, so the arenas grow
+    // once and every unit table goes up in one copy ahead of the bulk rows.
+    struct batch {
+        std::vector<kvc_unit> U;
+        size_t u0 = 0;                           // first entry in the device unit table
+        long long fs = 0, is = 0, gs = 0;        // scratch end offsets
+        std::vector<long long> w_base;           // R-KV weights at the front of the float arena
+        int max_nq = 1, max_C = 1, max_t = 1, max_n = 1;
+        bool any_primal = false, any_dual = false, lsq_aligned = true;
+        size_t lsq_smem = 0;
+        int row0 = 0, row1 = 0;                  // token rows (streamed job)
+        int out0 = 0, out1 = 0;                  // kept-key rows (streamed job)
+    };
+    std::vector<batch> B;
+    long long max_fs = 0, max_is = 0, max_gs = 0;
     size_t pos = 0;
     while (pos < all.size()) {
-        // gather a batch
-        std::vector<kvc_unit> U;
-        long long fs = 0, is = 0, gs = 0;
-        int max_nq = 1, max_C = 1, max_t = 1, max_n = 1;
-        bool any_primal = false, any_dual = false, lsq_aligned = (dv % 4) == 0;
-        size_t lsq_smem = 0;
-        // R-KV weights live at the front of the float arena, per layer
-        std::vector<long long> w_base(n_jobs, -1);
-        for (int l = 0; l < n_jobs; l++)
-            if (jobs[l].rkv_w) { w_base[l] = fs; fs += al32(jobs[l].plan->T); }
-        size_t first = pos;
-        while (pos < all.size()) {
+        batch bt;
+        bt.lsq_aligned = (dv % 4) == 0;
+        if (concurrent && !B.empty()) {          // continue after the previous group's scratch
+            bt.fs = B.back().fs;
+            bt.is = B.back().is;
+            bt.gs = B.back().gs;
+            bt.w_base = B[0].w_base;
+        } else {
+            bt.w_base.assign(n_jobs, -1);
+            for (int l = 0; l < n_jobs; l++)
+                if (jobs[l].rkv_w) { bt.w_base[l] = bt.fs; bt.fs += al32(jobs[l].plan->T); }
+        }
+        const size_t first = pos;
+        size_t gi = 0;
+        while (group_end[gi] <= first) gi++;
+        while (pos < group_end[gi]) {
             const kvc_plan_unit & pu = jobs[all[pos].l].plan->units[all[pos].i];
             unit_sizes s = sizes_of(pu, H, dv, p.use_omp != 0);
-            long long bytes = (fs + s.fs) * 4 + (is + s.is) * 4 + (gs + s.gs) * 8;
+            long long bytes = (bt.fs + s.fs) * 4 + (bt.is + s.is) * 4 + (bt.gs + s.gs) * 8;
             if (pos > first && bytes > budget) break;
             const kvc_layer_job & J = jobs[all[pos].l];
             const int ek = H * dk, ev = H * dv;
@@ -510,139 +609,224 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             u.token_base = pu.start;
             u.active = 1;
             u.chunk = all[pos].i;
-            u.s_off = fs; fs += al32((long long)H * pu.nq * pu.C);
-            u.imp_off = fs; fs += al32((long long)(2 * H + 1) * pu.C);
-            u.row_off = fs; fs += al32((long long)2 * H * pu.nq);
-            u.y_off = fs; fs += al32((long long)H * pu.nq * dv);
-            u.x_off = fs; fs += al32((long long)H * pu.nq * pu.t);
-            u.xs_off = fs; fs += al32((long long)2 * H * pu.nq);
+            u.s_off = bt.fs; bt.fs += al32((long long)H * pu.nq * pu.C);
+            u.imp_off = bt.fs; bt.fs += al32((long long)(2 * H + 1) * pu.C);
+            u.row_off = bt.fs; bt.fs += al32((long long)2 * H * pu.nq);
+            u.y_off = bt.fs; bt.fs += al32((long long)H * pu.nq * dv);
+            u.x_off = bt.fs; bt.fs += al32((long long)H * pu.nq * pu.t);
+            u.xs_off = bt.fs; bt.fs += al32((long long)2 * H * pu.nq);
             u.omp_off = -1;
-            if (p.use_omp) { u.omp_off = fs; fs += al32((long long)kvc_omp_floats(pu.C, pu.t, pu.nq, H)); }
-            u.w_off = w_base[u.layer] >= 0 ? w_base[u.layer] + pu.start : -1;
-            u.sel_off = is; is += al32(pu.t);
-            u.c_off = is; is += al32(4LL * pu.C);
+            if (p.use_omp) { u.omp_off = bt.fs; bt.fs += al32((long long)kvc_omp_floats(pu.C, pu.t, pu.nq, H)); }
+            u.w_off = bt.w_base[u.layer] >= 0 ? bt.w_base[u.layer] + pu.start : -1;
+            u.sel_off = bt.is; bt.is += al32(pu.t);
+            u.c_off = bt.is; bt.is += al32(4LL * pu.C);
             const int n = std::min(pu.nq, pu.t);
             if (n > 3072) return KVC_ERR_SHAPE;
             long long gper = (long long)n * n;
             if (!p.skip_beta) gper = std::max<long long>(gper, (long long)kvc_nnls_doubles_per_head(pu.t, pu.nq));
-            u.g_off = gs; gs += al32((long long)H * gper);
-            u.z_off = gs; gs += al32((long long)H * n * dv);
-            max_nq = std::max(max_nq, pu.nq);
-            max_C = std::max(max_C, pu.C);
-            max_t = std::max(max_t, pu.t);
-            max_n = std::max(max_n, n);
-            if (pu.nq < pu.t) any_dual = true;
-            else any_primal = true;
-            if (pu.t % 4) lsq_aligned = false;
-            lsq_smem = std::max(lsq_smem, kvc_lsq_smem_bytes(n));
-            U.push_back(u);
+            u.g_off = bt.gs; bt.gs += al32((long long)H * gper);
+            u.z_off = bt.gs; bt.gs += al32((long long)H * n * dv);
+            bt.max_nq = std::max(bt.max_nq, pu.nq);
+            bt.max_C = std::max(bt.max_C, pu.C);
+            bt.max_t = std::max(bt.max_t, pu.t);
+            bt.max_n = std::max(bt.max_n, n);
+            if (pu.nq < pu.t) bt.any_dual = true;
+            else bt.any_primal = true;
+            if (pu.t % 4) bt.lsq_aligned = false;
+            bt.lsq_smem = std::max(bt.lsq_smem, kvc_lsq_smem_bytes(n));
+            if (bt.U.empty()) { bt.row0 = pu.start; bt.out0 = off; }
+            bt.row1 = pu.start + pu.C;
+            bt.out1 = off + pu.t;
+            bt.U.push_back(u);
             pos++;
         }
-        void * a0; void * a1; void * a2;
-        int rc;
-        if ((rc = kvc_arena(ctx, 0, (size_t)fs * 4, &a0))) return rc;
-        if ((rc = kvc_arena(ctx, 1, (size_t)is * 4, &a1))) return rc;
-        if ((rc = kvc_arena(ctx, 2, (size_t)gs * 8, &a2))) return rc;
-        float * F = (float *)a0;
-        int * I = (int *)a1;
-        double * G = (double *)a2;
-        for (int l = 0; l < n_jobs; l++)
-            if (w_base[l] >= 0)
-                KVC_CUDA(cudaMemcpyAsync(F + w_base[l], jobs[l].rkv_w, (size_t)jobs[l].plan->T * 4,
-                                         cudaMemcpyDeviceToDevice, st));
-        if (ctx->units_cap < U.size()) {
-            if (ctx->d_units) { KVC_CUDA(cudaStreamSynchronize(st)); cudaFree(ctx->d_units); }
-            ctx->units_cap = U.size() * 2;
-            KVC_CUDA(cudaMalloc(&ctx->d_units, ctx->units_cap * sizeof(kvc_unit)));
-        }
-        KVC_CUDA(cudaMemcpyAsync(ctx->d_units, U.data(), U.size() * sizeof(kvc_unit), cudaMemcpyHostToDevice, st));
-        if (v_upload) {                              // after this call's small uploads, before the scoring
-            // the copy engine serves uploads in the order they become ready: make
-            // V wait for everything queued so far on the compute stream, or it
-            // would go ahead of the small uploads the scoring needs
-            KVC_CUDA(cudaEventRecord(ctx->ev_k, st));
-            KVC_CUDA(cudaStreamWaitEvent(ctx->copy_stream, ctx->ev_k, 0));
-            KVC_CUDA(cudaMemcpyAsync(jobs[0].v_dev, jobs[0].v_host, jobs[0].v_bytes, cudaMemcpyHostToDevice,
-                                     ctx->copy_stream));
-            KVC_CUDA(cudaEventRecord(ctx->ev_v, ctx->copy_stream));
-            v_upload = false;
-            v_pending = true;
-        }
-        const int nu = (int)U.size();
-        const kvc_unit * du = ctx->d_units;
+        bt.u0 = first;
+        max_fs = std::max(max_fs, bt.fs);
+        max_is = std::max(max_is, bt.is);
+        max_gs = std::max(max_gs, bt.gs);
+        B.push_back(std::move(bt));
+    }
+    void * a0; void * a1; void * a2;
+    int rc;
+    if ((rc = kvc_arena(ctx, 0, (size_t)max_fs * 4, &a0))) return rc;
+    if ((rc = kvc_arena(ctx, 1, (size_t)max_is * 4, &a1))) return rc;
+    if ((rc = kvc_arena(ctx, 2, (size_t)max_gs * 8, &a2))) return rc;
+    float * F = (float *)a0;
+    int * I = (int *)a1;
+    double * G = (double *)a2;
+    if (ctx->units_cap < all.size()) {
+        if (ctx->d_units) { KVC_CUDA(cudaStreamSynchronize(st)); cudaFree(ctx->d_units); }
+        ctx->units_cap = all.size() * 2;
+        KVC_CUDA(cudaMalloc(&ctx->d_units, ctx->units_cap * sizeof(kvc_unit)));
+    }
+    {
+        std::vector<kvc_unit> table;
+        table.reserve(all.size());
+        for (const batch & bt : B) table.insert(table.end(), bt.U.begin(), bt.U.end());
+        KVC_CUDA(cudaMemcpyAsync(ctx->d_units, table.data(), table.size() * sizeof(kvc_unit),
+                                 cudaMemcpyHostToDevice, st));
+    }
 
-        if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
+    // ---- bulk uploads of a streamed job, group by group on the copy stream.
+    // The copy engine serves uploads in the order they become ready: the bulk
+    // rows wait for everything queued so far on the compute stream (the small
+    // uploads above and the caller's), or they would go ahead of them.
+    std::vector<cudaEvent_t> ev_k(B.size(), nullptr), ev_v(B.size(), nullptr);
+    if (io) {
+        kvc_trace(ctx, "queued", st);
+        cudaEvent_t e0 = kvc_sync_event(ctx);
+        KVC_CUDA(cudaEventRecord(e0, st));
+        KVC_CUDA(cudaStreamWaitEvent(ctx->copy_stream, e0, 0));
+        for (size_t bi = 0; bi < B.size(); bi++) {
+            const size_t r0 = (size_t)B[bi].row0, nr = (size_t)(B[bi].row1 - B[bi].row0);
+            if (!io->k_resident) {
+                KVC_CUDA(cudaMemcpyAsync(io->k.stage + r0 * io->k.row_bytes, io->k.host + r0 * io->k.row_bytes,
+                                         nr * io->k.row_bytes, cudaMemcpyHostToDevice, ctx->copy_stream));
+                ev_k[bi] = kvc_sync_event(ctx);
+                KVC_CUDA(cudaEventRecord(ev_k[bi], ctx->copy_stream));
+                kvc_trace(ctx, "k" + std::to_string(bi), ctx->copy_stream);
+            }
+            KVC_CUDA(cudaMemcpyAsync(io->v.stage + r0 * io->v.row_bytes, io->v.host + r0 * io->v.row_bytes,
+                                     nr * io->v.row_bytes, cudaMemcpyHostToDevice, ctx->copy_stream));
+            ev_v[bi] = kvc_sync_event(ctx);
+            KVC_CUDA(cudaEventRecord(ev_v[bi], ctx->copy_stream));
+            kvc_trace(ctx, "v" + std::to_string(bi), ctx->copy_stream);
+        }
+    }
+    // rows [r0, r1) of a streamed input are on the device once `e` is reached;
+    // quantised rows are then decoded into the job's fp32 matrix
+    auto arrive = [&](cudaEvent_t e, const kvc_stream_io::input & in, const float * dst, int ncols, int r0,
+                      int r1, cudaStream_t s) -> int {
+        KVC_CUDA(cudaStreamWaitEvent(s, e, 0));
+        if (in.type < 0) return KVC_OK;
+        kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1, s);
+        return kvc_launch_decode(in.stage + (size_t)r0 * in.row_bytes, in.row_bytes, in.type,
+                                 const_cast<float *>(dst) + (size_t)r0 * ncols, r1 - r0, ncols, s);
+    };
+
+    // scoring phase of one batch: scores, softmax + importance, selection
+    auto scoring = [&](const batch & bt, cudaStream_t s) -> int {
+        const int nu = (int)bt.U.size();
+        const kvc_unit * du = ctx->d_units + bt.u0;
+        int e;
         {
-            kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1);
-            if ((rc = kvc_launch_score(du, nu, max_nq, max_C, P, F, I, 0, st, rows_aligned))) return rc;
+            kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1, s);
+            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, I, 0, s, rows_aligned))) return e;
         }
         if (P.use_omp) {                             // needs the raw scores: before the softmax
-            kvc_stage_timer tm(ctx, KVC_ST_SELECT, 1);
-            if ((rc = kvc_launch_omp_exp(du, nu, P, F, st))) return rc;
+            kvc_stage_timer tm(ctx, KVC_ST_SELECT, 1, s);
+            if ((e = kvc_launch_omp_exp(du, nu, P, F, s))) return e;
         }
         {
-            kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1);
-            if ((rc = kvc_launch_softmax_importance(du, nu, P, F, st))) return rc;
+            kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1, s);
+            if ((e = kvc_launch_softmax_importance(du, nu, P, F, s))) return e;
         }
+        kvc_stage_timer tm(ctx, KVC_ST_SELECT, 2, s);
+        if ((e = kvc_launch_aggregate(du, nu, P, F, s))) return e;
+        if (P.use_omp) return kvc_launch_omp_select(du, nu, P, F, I, ctx->d_outs, s);
+        return kvc_launch_select(du, nu, bt.max_C, P, F, I, ctx->d_outs, s);
+    };
+    // refit phase: Y, then per refinement round X (and beta) and the LS
+    // solve for C_v, then the per-chunk metric records
+    auto refit = [&](const batch & bt, cudaStream_t s) -> int {
+        const int nu = (int)bt.U.size();
+        const kvc_unit * du = ctx->d_units + bt.u0;
+        const int max_nq = bt.max_nq, max_t = bt.max_t, max_n = bt.max_n;
+        int e;
         {
-            kvc_stage_timer tm(ctx, KVC_ST_SELECT, 2);
-            if ((rc = kvc_launch_aggregate(du, nu, P, F, st))) return rc;
-            if (P.use_omp) {
-                if ((rc = kvc_launch_omp_select(du, nu, P, F, I, ctx->d_outs, st))) return rc;
-            } else if ((rc = kvc_launch_select(du, nu, max_C, P, F, I, ctx->d_outs, st))) {
-                return rc;
-            }
-        }
-        if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
-        if (v_pending) {                             // values still in flight from the host
-            KVC_CUDA(cudaStreamWaitEvent(st, ctx->ev_v, 0));
-            if (jobs[0].v_quant) {
-                kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1);
-                if ((rc = kvc_launch_decode(jobs[0].v_quant, jobs[0].v_row_bytes, jobs[0].v_type,
-                                            const_cast<float *>(jobs[0].V), jobs[0].plan->T, H * dv, st)))
-                    return rc;
-            }
-            v_pending = false;
-        }
-        {
-            kvc_stage_timer tm(ctx, KVC_ST_PV, 1);
-            if ((rc = kvc_launch_pv(du, nu, max_nq, P, F, st))) return rc;
+            kvc_stage_timer tm(ctx, KVC_ST_PV, 1, s);
+            if ((e = kvc_launch_pv(du, nu, max_nq, P, F, s))) return e;
         }
         for (int r = 0; r <= p.refine_rounds; r++) {
             if (r > 0) {
-                kvc_stage_timer tm(ctx, KVC_ST_REFINE, 1);
-                if ((rc = kvc_launch_refine(du, nu, P, F, I, ctx->d_outs, st))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_REFINE, 1, s);
+                if ((e = kvc_launch_refine(du, nu, P, F, I, ctx->d_outs, s))) return e;
             }
             {
-                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1);     // raw S[:, sel]
-                if ((rc = kvc_launch_score(du, nu, max_nq, max_t, P, F, I, 1, st, rows_aligned))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s);     // raw S[:, sel]
+                if ((e = kvc_launch_score(du, nu, max_nq, max_t, P, F, I, 1, s, rows_aligned))) return e;
             }
             if (!p.skip_beta) {
-                kvc_stage_timer tm(ctx, KVC_ST_BETA, 2);
-                if ((rc = kvc_launch_beta(du, nu, max_nq, max_t, P, F, I, G, ctx->d_outs, st))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_BETA, 2, s);
+                if ((e = kvc_launch_beta(du, nu, max_nq, max_t, P, F, I, G, ctx->d_outs, s))) return e;
             }
             {
-                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1);     // X = softmax(S[:, sel] + beta)
-                if ((rc = kvc_launch_softmax_x(du, nu, max_nq, P, F, ctx->d_outs, st))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s);     // X = softmax(S[:, sel] + beta)
+                if ((e = kvc_launch_softmax_x(du, nu, max_nq, P, F, ctx->d_outs, s))) return e;
             }
             {
-                kvc_stage_timer tm(ctx, KVC_ST_LSQ, any_primal ? 2 : 1);
-                if ((rc = kvc_launch_lsq_gram(du, nu, max_n, max_t, P, F, G, ctx->d_outs, any_primal, lsq_aligned, st))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_LSQ, bt.any_primal ? 2 : 1, s);
+                if ((e = kvc_launch_lsq_gram(du, nu, max_n, max_t, P, F, G, ctx->d_outs, bt.any_primal,
+                                             bt.lsq_aligned, s)))
+                    return e;
             }
             {
-                kvc_stage_timer tm(ctx, KVC_ST_LSQ_FACTOR, (max_n > 128 || dv > 128) ? 2 : 1);
-                if ((rc = kvc_launch_lsq_factor(du, nu, max_n, lsq_smem, P, F, G, ctx->d_outs, st))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_LSQ_FACTOR, (max_n > 128 || dv > 128) ? 2 : 1, s);
+                if ((e = kvc_launch_lsq_factor(du, nu, max_n, bt.lsq_smem, P, F, G, ctx->d_outs, s))) return e;
             }
             {
-                kvc_stage_timer tm(ctx, KVC_ST_LSQ_OUT, any_dual ? 1 : 0);
-                if ((rc = kvc_launch_lsq_out(du, nu, max_t, P, F, G, ctx->d_outs, any_dual, lsq_aligned, st))) return rc;
+                kvc_stage_timer tm(ctx, KVC_ST_LSQ_OUT, bt.any_dual ? 1 : 0, s);
+                if ((e = kvc_launch_lsq_out(du, nu, max_t, P, F, G, ctx->d_outs, bt.any_dual, bt.lsq_aligned, s)))
+                    return e;
             }
         }
         if (metric_partials) {
-            kvc_stage_timer tm(ctx, KVC_ST_METRICS, 1);
-            if ((rc = kvc_launch_metric_partial(du, nu, P, F, ctx->d_outs, st))) return rc;
+            kvc_stage_timer tm(ctx, KVC_ST_METRICS, 1, s);
+            if ((e = kvc_launch_metric_partial(du, nu, P, F, ctx->d_outs, s))) return e;
         }
+        return KVC_OK;
+    };
+    auto weights = [&](const batch & bt, cudaStream_t s) -> int {
+        for (int l = 0; l < n_jobs; l++)
+            if (bt.w_base[l] >= 0)
+                KVC_CUDA(cudaMemcpyAsync(F + bt.w_base[l], jobs[l].rkv_w, (size_t)jobs[l].plan->T * 4,
+                                         cudaMemcpyDeviceToDevice, s));
+        return KVC_OK;
+    };
+
+    if (concurrent) {
+        // group g on group stream g % KVC_GROUP_STREAMS: its scoring as soon
+        // as its K rows are in, its refit once its V rows are in; the streams
+        // start after everything queued so far on the compute stream, which
+        // joins them all at the end
+        if ((rc = weights(B[0], st))) return rc;
+        cudaEvent_t e_setup = kvc_sync_event(ctx);
+        KVC_CUDA(cudaEventRecord(e_setup, st));
+        const size_t n_streams = std::min<size_t>(B.size(), KVC_GROUP_STREAMS);
+        for (size_t i = 0; i < n_streams; i++) KVC_CUDA(cudaStreamWaitEvent(ctx->group_stream[i], e_setup, 0));
+        for (size_t bi = 0; bi < B.size(); bi++) {
+            const batch & bt = B[bi];
+            cudaStream_t gs = ctx->group_stream[bi % KVC_GROUP_STREAMS];
+            if (ev_k[bi] && (rc = arrive(ev_k[bi], io->k, jobs[0].K, H * dk, bt.row0, bt.row1, gs))) return rc;
+            if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), gs));
+            if ((rc = scoring(bt, gs))) return rc;
+            kvc_trace(ctx, "s" + std::to_string(bi), gs);
+            if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), gs));
+            if ((rc = arrive(ev_v[bi], io->v, jobs[0].V, H * dv, bt.row0, bt.row1, gs))) return rc;
+            if ((rc = refit(bt, gs))) return rc;
+            if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), gs));
+            kvc_trace(ctx, "r" + std::to_string(bi), gs);
+            if (io->emit && (rc = io->emit(bt.out0, bt.out1, gs))) return rc;
+        }
+        for (size_t i = 0; i < n_streams; i++) {
+            cudaEvent_t ej = kvc_sync_event(ctx);
+            KVC_CUDA(cudaEventRecord(ej, ctx->group_stream[i]));
+            KVC_CUDA(cudaStreamWaitEvent(st, ej, 0));
+        }
+        return KVC_OK;
+    }
+    for (size_t bi = 0; bi < B.size(); bi++) {
+        const batch & bt = B[bi];
+        if ((rc = weights(bt, st))) return rc;
+        if (io && ev_k[bi] && (rc = arrive(ev_k[bi], io->k, jobs[0].K, H * dk, bt.row0, bt.row1, st))) return rc;
         if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
+        if ((rc = scoring(bt, st))) return rc;
+        if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
+        if (io && (rc = arrive(ev_v[bi], io->v, jobs[0].V, H * dv, bt.row0, bt.row1, st))) return rc;
+        if ((rc = refit(bt, st))) return rc;
+        if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
+        if (io) kvc_trace(ctx, "r" + std::to_string(bi), st);
+        if (io && io->emit && (rc = io->emit(bt.out0, bt.out1, st))) return rc;
     }
     return KVC_OK;
 }

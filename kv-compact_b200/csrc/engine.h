@@ -1,13 +1,16 @@
 // engine.h — host-side planning and the device pipeline over (layer, chunk) units.
 #pragma once
 
+#include <functional>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "../../include/kv-compact-api.h"
 #include "kvc_internal.h"
 
 #define KVC_N_STAGES 13
+#define KVC_GROUP_STREAMS 4
 
 // One chunk of one layer as the reference's kv_compact would process it.
 struct kvc_plan_unit {
@@ -33,6 +36,42 @@ struct kvc_plan {
 int kvc_make_plan(int T, int n_q, bool q_null, int H, int dk, int dv, const kv_compact_params & p,
                   kvc_plan * out);
 
+// Host-resident inputs and outputs of a drop-in call (single job). The
+// engine cuts the layer's chunks into groups and overlaps, group by group,
+// the upload of K/V rows (context copy stream), the compute, and the
+// download of finished output rows (context d2h stream, queued by `emit`):
+//   copy stream:    K_0 V_0 K_1 V_1 ...   (queued once the call's small
+//                                          uploads are queued, so they go first)
+//   group stream g: [wait K_g] decode K_g, scoring/selection of group g,
+//                   [wait V_g] decode V_g, refit of group g, emit(g)
+//   d2h stream:     results of group g while later groups compute
+// Groups run on KVC_GROUP_STREAMS streams in turn, so the kernels of
+// different groups (many of them one short wave each) share the SMs; group
+// sizes may shrink geometrically so the work left after the last upload
+// (the refit and download of the last group) is small. Each group then has
+// scratch of its own; when the whole layer's scratch does not fit the
+// device, groups run one after the other on the compute stream instead.
+// A group's rows are the token rows its chunks cover; its output rows are
+// the kept-key rows [r0, r1) of the layer's result arrays.
+struct kvc_stream_io {
+    // One input matrix: rows of `row_bytes` host bytes at `host`, staged at
+    // `stage` (device, same row layout). type < 0: the rows are fp32 and
+    // `stage` is the job's K / V itself; otherwise quantised rows decoded
+    // into the job's K / V after the upload.
+    struct input {
+        const uint8_t * host = nullptr;
+        uint8_t * stage = nullptr;
+        size_t row_bytes = 0;
+        int type = -1;
+    } k, v;
+    bool k_resident = false;   // K already uploaded and decoded in full (top-level cheap queries)
+    int max_groups = 1;        // upper bound on the number of groups
+    double size_ratio = 1.0;   // size of group g+1 / size of group g
+    // Queue whatever consumes output rows [r0, r1) (requantisation, copies
+    // to the host) on stream `st`, after the group's results.
+    std::function<int(int r0, int r1, cudaStream_t st)> emit;
+};
+
 // Device-side job for one layer: fp32 caches resident on the device.
 struct kvc_layer_job {
     const float * K = nullptr;      // [T x H*dk]
@@ -41,17 +80,7 @@ struct kvc_layer_job {
     const float * rkv_w = nullptr;  // [T] device R-KV weights or null
     const kvc_plan * plan = nullptr;
     kvc_layer_out out{};            // device outputs (sel, beta, cv, t_total)
-    // V still on the host (drop-in API, single job): once the engine has
-    // queued its own small uploads it copies v_host (v_bytes) to v_dev on the
-    // context's copy stream, overlapping the scoring; before the first stage
-    // that reads V it waits for that copy and, when v_quant is set (== v_dev,
-    // quantised rows), decodes it into V.
-    const void * v_host = nullptr;
-    void * v_dev = nullptr;
-    size_t v_bytes = 0;
-    const uint8_t * v_quant = nullptr;
-    size_t v_row_bytes = 0;
-    int v_type = 0;
+    kvc_stream_io * io = nullptr;   // host-resident inputs/outputs (single-job drop-in calls)
 };
 
 struct kvc_phase_ms {
@@ -64,8 +93,11 @@ struct kvc_ctx {
     int device = -1;
     cudaStream_t stream = nullptr;
     cudaStream_t copy_stream = nullptr;         // host->device uploads overlapping compute
+    cudaStream_t d2h_stream = nullptr;          // device->host results overlapping compute
+    cudaStream_t group_stream[KVC_GROUP_STREAMS] = {};   // groups of a streamed call, round robin
     cudaEvent_t ev[4] = {};
-    cudaEvent_t ev_k = nullptr, ev_v = nullptr; // upload completion (no timing)
+    std::vector<cudaEvent_t> sync_ev;           // cross-stream ordering events (no timing), grow-only
+    size_t sync_used = 0;
     std::mutex mu;
     void * arena[10] = {};
     size_t arena_cap[10] = {};
@@ -87,12 +119,27 @@ struct kvc_ctx {
     // pinned host staging for device->host results (grow-only)
     void * pinned = nullptr;
     size_t pinned_cap = 0;
+    // KVC_TRACE=1: timeline of the streamed drop-in calls (kvc_trace / kvc_trace_dump)
+    bool trace = false;
+    std::vector<cudaEvent_t> trace_ev;
+    std::vector<std::string> trace_label;
+    size_t trace_used = 0;
 };
 
 // Wait until all work queued on ctx->stream has finished, polling its
 // completion instead of sleeping in the driver: the calling thread resumes as
 // soon as the device is done (no wake-up latency between dependent steps).
 int kvc_wait(kvc_ctx * ctx);
+
+// Next cross-stream ordering event of the context (reset with sync_used = 0
+// at the start of a call, once no earlier event is still pending).
+cudaEvent_t kvc_sync_event(kvc_ctx * ctx);
+
+// With KVC_TRACE=1 in the environment: mark `label` on stream `st` (a timing
+// event), and after the call's final wait print the marks of the call to
+// stderr in milliseconds since its first mark. No-ops otherwise.
+void kvc_trace(kvc_ctx * ctx, const std::string & label, cudaStream_t st);
+void kvc_trace_dump(kvc_ctx * ctx);
 
 // Grow the pinned staging buffer to at least `bytes`.
 int kvc_pinned(kvc_ctx * ctx, size_t bytes, void ** out);
@@ -120,12 +167,13 @@ enum {
     KVC_ST_LSQ_OUT,
 };
 
-// Brackets one stage with events on ctx->stream when profiling is on.
+// Brackets one stage with events on `st` (default ctx->stream) when profiling is on.
 struct kvc_stage_timer {
     kvc_ctx * ctx;
     int stage;
+    cudaStream_t stream;
     int first = -1;
-    kvc_stage_timer(kvc_ctx * c, int s, int n_launch);
+    kvc_stage_timer(kvc_ctx * c, int s, int n_launch, cudaStream_t st = nullptr);
     ~kvc_stage_timer();
 };
 

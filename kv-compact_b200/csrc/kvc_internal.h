@@ -156,5 +156,6 @@ int kvc_launch_decode(const uint8_t * src, size_t src_row_bytes, int type, float
 int kvc_launch_encode_gather(const float * src, size_t src_stride, const int * rows_idx,
                              int rows, int n, int type, uint8_t * dst, size_t dst_row_bytes,
                              cudaStream_t st);
-int kvc_launch_encode_heads(const float * cv, int H, int t, int dv, int type, uint8_t * dst,
+// V_out rows 0..rows-1 from cv[h][j][:] (heads t rows apart).
+int kvc_launch_encode_heads(const float * cv, int H, int t, int rows, int dv, int type, uint8_t * dst,
                             size_t dst_row_bytes, cudaStream_t st);
