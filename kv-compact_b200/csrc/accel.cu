@@ -116,7 +116,7 @@ KVC_EXPORT int kv_compact_cuda_refit_target_all_heads(const float * const * W, c
     u.y_off = (long long)(dY - dW);
     if (put_unit(ctx, u)) return -1;
     kvc_params_dev P = seam_params(H, d_v, d_v, 1.0f);
-    if (kvc_launch_pv(ctx->d_units, 1, n_q, P, dW, st)) return -1;
+    if (kvc_launch_pv(ctx->d_units, 1, n_q, P, dW, false, st)) return -1;
     ctx->launches += 1;
     for (int h = 0; h < H; h++)
         if (cudaMemcpyAsync(Y_out[h], dY + (size_t)h * n_q * d_v, (size_t)n_q * d_v * 4, cudaMemcpyDeviceToHost,

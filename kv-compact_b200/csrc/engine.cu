@@ -2,7 +2,7 @@
 //
 // Pipeline over a flat list of units (one per (layer, chunk), all heads):
 //   scoring phase:  k_score -> k_softmax_importance -> k_aggregate -> k_select
-//   refit phase:    k_pv (Y) -> beta (NNLS, optional) -> k_score gather (S[:,sel])
+//   refit phase:    k_pv (Y) -> k_gather_x (S[:,sel]) -> beta (NNLS, optional)
 //                   -> k_softmax_x (X) -> k_dgemm + k_lsq_factor (C_v)
 //                   -> refinement rounds (optional)
 // Every stage is one launch over all units of the batch, so a whole model
@@ -735,7 +735,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         int e;
         {
             kvc_stage_timer tm(ctx, KVC_ST_PV, 1, s);
-            if ((e = kvc_launch_pv(du, nu, max_nq, P, F, s))) return e;
+            if ((e = kvc_launch_pv(du, nu, max_nq, P, F, true, s))) return e;
         }
         for (int r = 0; r <= p.refine_rounds; r++) {
             if (r > 0) {
@@ -743,8 +743,8 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
                 if ((e = kvc_launch_refine(du, nu, P, F, I, ctx->d_outs, s))) return e;
             }
             {
-                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s);     // raw S[:, sel]
-                if ((e = kvc_launch_score(du, nu, max_nq, max_t, P, F, I, 1, s, rows_aligned))) return e;
+                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s);     // raw S[:, sel], gathered from S
+                if ((e = kvc_launch_gather_x(du, nu, max_nq, P, F, I, s))) return e;
             }
             if (!p.skip_beta) {
                 kvc_stage_timer tm(ctx, KVC_ST_BETA, 2, s);

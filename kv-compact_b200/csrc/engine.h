@@ -217,10 +217,16 @@ int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_
                      bool rows_aligned = false);
 int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const kvc_params_dev & P,
                                   float * fs, cudaStream_t st);
+// X block of the refit: the raw scores of the kept keys, S[:, sel].
+int kvc_launch_gather_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P, float * fs,
+                        const int * is, cudaStream_t st);
+// Y = A V per (unit, head). from_scores: the S region holds raw scores and A
+// is formed from them and the row statistics (the engine); else it holds A.
 int kvc_launch_pv(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
-                  float * fs, cudaStream_t st);
+                  float * fs, bool from_scores, cudaStream_t st);
 bool kvc_pv_tc_ok(int max_nq, int dv);
-int kvc_launch_pv_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, cudaStream_t st);
+int kvc_launch_pv_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, bool from_scores,
+                     cudaStream_t st);
 int kvc_tc_take_error(cudaStream_t st);
 int kvc_launch_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
                          float * fs, const kvc_layer_out * d_outs, cudaStream_t st);

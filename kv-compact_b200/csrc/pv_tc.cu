@@ -41,7 +41,7 @@ constexpr uint32_t pv_tmem_cols() { return DV <= 32 ? 32 : (DV <= 64 ? 64 : (DV 
 
 template <int DV>
 __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                               float * __restrict__ fs) {
+                                               float * __restrict__ fs, int from_scores) {
     using namespace kvc_tc;
     constexpr int NPB = DV / 32;                       // (row, k-quad) pairs of V per thread and stage
     constexpr uint32_t A_BYTES = (PV_M / 8) * PV_SBO;  // one A tile (hi or lo)
@@ -51,7 +51,8 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
     const kvc_unit u = units[blockIdx.x];
     const int h = blockIdx.y;
     const int ev = P.H * DV, nq = u.nq, C = u.C;
-    const float * A = fs + u.s_off + (long long)h * nq * C;
+    const float * A = fs + u.s_off + (long long)h * nq * C;     // A, or raw scores A is formed from
+    const float * rmax = fs + u.row_off + (long long)h * 2 * nq;
     const float * V = u.V + (long long)h * DV;
     float * Y = fs + u.y_off + (long long)h * nq * DV;
 
@@ -74,6 +75,25 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
     const int nst = (C + PV_KS - 1) / PV_KS;
     const bool avec = ((C & 3) == 0) && ((((uintptr_t)A) & 15) == 0);
 
+    // row statistics of the four A rows this thread stages (the same rows in every stage)
+    float am[4], ainv[4];
+#pragma unroll
+    for (int it = 0; it < 4; it++) {
+        const int idx = it * 128 + tid;
+        const int r = ((idx >> 5) << 3) | (idx & 7);
+        const bool rs = from_scores && r < nq;
+        am[it] = rs ? rmax[r] : 0.0f;
+        ainv[it] = rs ? __fdiv_rn(1.0f, __fadd_rn(rmax[nq + r], 1e-12f)) : 0.0f;
+    }
+    // from scores: A = exp(s - m) * inv, the softmax of score.cu with the
+    // hardware exponential (Y only feeds the least-squares right-hand side and
+    // the quality metrics, both tolerance-checked; its relative error stays
+    // near 1e-6, like the 3xTF32 products); else the given weights; zero
+    // outside the tile
+    auto a_entry = [&](float sv, int it, bool live) {
+        if (!live) return 0.0f;
+        return from_scores ? __fmul_rn(__expf(__fsub_rn(sv, am[it])), ainv[it]) : sv;
+    };
     float4 ra[4];
     float rb[NPB][4];
     auto load = [&](int s) {
@@ -106,18 +126,22 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
             for (int e = 0; e < 4; e++) rb[pb][e] = (k + e < C) ? V[(long long)(k + e) * ev + n] : 0.0f;
         }
     };
-    auto store = [&](int b) {
+    auto store = [&](int b, int s) {
         uint8_t * base = smem + b * STAGE;
 #pragma unroll
         for (int it = 0; it < 4; it++) {
             const int idx = it * 128 + tid;
             const int r = ((idx >> 5) << 3) | (idx & 7), kq = (idx >> 3) & 3;
+            const int k = s * PV_KS + 4 * kq;
             const uint32_t off = (r >> 3) * PV_SBO + kq * PV_LBO + (r & 7) * 16;
+            const bool rl = r < nq;
+            const float a0 = a_entry(ra[it].x, it, rl && k + 0 < C), a1 = a_entry(ra[it].y, it, rl && k + 1 < C);
+            const float a2 = a_entry(ra[it].z, it, rl && k + 2 < C), a3 = a_entry(ra[it].w, it, rl && k + 3 < C);
             float4 hi, lo;
-            tf32_split(ra[it].x, hi.x, lo.x);
-            tf32_split(ra[it].y, hi.y, lo.y);
-            tf32_split(ra[it].z, hi.z, lo.z);
-            tf32_split(ra[it].w, hi.w, lo.w);
+            tf32_split(a0, hi.x, lo.x);
+            tf32_split(a1, hi.y, lo.y);
+            tf32_split(a2, hi.z, lo.z);
+            tf32_split(a3, hi.w, lo.w);
             *reinterpret_cast<float4 *>(base + off) = hi;
             *reinterpret_cast<float4 *>(base + A_BYTES + off) = lo;
         }
@@ -142,7 +166,7 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
         const int b = s & 1;
         bool ok = true;
         if (s >= 2) ok = mbar_wait(&mbar[b], (uint32_t)(((s - 2) >> 1) & 1), PV_POLLS);
-        store(b);
+        store(b, s);
         if (s + 1 < nst) load(s + 1);
         fence_smem_to_async();
         if (__syncthreads_or(!ok)) {          // every thread takes the same decision
@@ -197,26 +221,27 @@ bool kvc_pv_tc_ok(int max_nq, int dv) {
     return max_nq <= PV_M && (dv == 64 || dv == 128 || dv == 256) && getenv("KVC_NO_TC") == nullptr;
 }
 
-int kvc_launch_pv_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, cudaStream_t st) {
+int kvc_launch_pv_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, bool from_scores,
+                     cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
     const dim3 grid(n_units, P.H);
     switch (P.dv) {
         case 64: {
             const uint32_t sm = 2 * pv_stage_bytes<64>();
             KVC_CUDA(cudaFuncSetAttribute(k_pv_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-            k_pv_tc<64><<<grid, 128, sm, st>>>(d_units, P, fs);
+            k_pv_tc<64><<<grid, 128, sm, st>>>(d_units, P, fs, from_scores ? 1 : 0);
             break;
         }
         case 128: {
             const uint32_t sm = 2 * pv_stage_bytes<128>();
             KVC_CUDA(cudaFuncSetAttribute(k_pv_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-            k_pv_tc<128><<<grid, 128, sm, st>>>(d_units, P, fs);
+            k_pv_tc<128><<<grid, 128, sm, st>>>(d_units, P, fs, from_scores ? 1 : 0);
             break;
         }
         case 256: {
             const uint32_t sm = 2 * pv_stage_bytes<256>();
             KVC_CUDA(cudaFuncSetAttribute(k_pv_tc<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-            k_pv_tc<256><<<grid, 128, sm, st>>>(d_units, P, fs);
+            k_pv_tc<256><<<grid, 128, sm, st>>>(d_units, P, fs, from_scores ? 1 : 0);
             break;
         }
         default:

@@ -10,17 +10,21 @@
 //   order with explicitly rounded multiply and add: S is bit-identical to the
 //   reference's. The kernel is a 128x128 (or 64x256) tile SIMT GEMM whose
 //   inner loop runs over d in order for 64 independent accumulators per thread.
-//   The same kernel builds S[:, sel] for the value refit (gather mode).
+//   The kernel can also score only the kept keys (mode 1, S[:, sel]); the
+//   engine gathers those from S instead (k_gather_x).
 //
-// Stage 2, k_softmax_importance: row softmax with max shift and
-//   1/(sum + 1e-12) (math.h:201-248), A overwrites S in place, row max/sum
-//   are kept for the beta fit, and per-key importance aggregates A over the
-//   queries in query order (max, RMS or mean), plus the per-key max used by
-//   sensitivity weighting (math.h:579-594).
+// Stage 2, k_softmax_importance: row softmax statistics with max shift and
+//   1/(sum + 1e-12) (math.h:201-248), kept for the beta fit and the metrics;
+//   per-key importance aggregates A over the queries in query order (max,
+//   RMS or mean), plus the per-key max used by sensitivity weighting
+//   (math.h:579-594). S itself is never overwritten: every consumer of A
+//   forms it from S and the row statistics (softmax_entry), so the refit's
+//   S[:, sel] is a gather (k_gather_x) instead of a second scoring pass.
 //
 // Stage 3, k_pv: Y_h = A_h V_h (math.h:70-80 via src/kv-compact-api.cpp:754-783),
 //   a 64x64-tile SIMT GEMM with fp32 FMA (Y only feeds the least-squares
-//   right-hand side, which is tolerance-checked).
+//   right-hand side, which is tolerance-checked); the tensor-core version is
+//   k_pv_tc (pv_tc.cu).
 #include "engine.h"
 
 #include <math.h>
@@ -334,45 +338,69 @@ __global__ void __launch_bounds__(ST, 2) k_score_async(const kvc_unit * __restri
     }
 }
 
-// One CTA per (unit, head). Phase 1: one warp per row — max, exp, sum,
-// normalise in place. Phase 2: one thread per key — aggregate over queries.
+// A[q][j] of the row softmax, formed from the raw score s, the row max m
+// and inv = 1 / (row exp-sum + 1e-12) with the reference's arithmetic
+// (math.h:201-248): e = expf(s - m), A = e * inv. The scores stay in place;
+// every consumer of A (importance, Y = A V) forms it with this function.
+__device__ __forceinline__ float softmax_entry(float s, float m, float inv) {
+    return __fmul_rn(expf(__fsub_rn(s, m)), inv);
+}
+__device__ __forceinline__ float softmax_inv(float sum) { return __fdiv_rn(1.0f, __fadd_rn(sum, 1e-12f)); }
+
+// One CTA per (unit, head); S is left intact. Phase 1: one warp per row —
+// row max, exp-sum (the second read of the row comes from L1), kept as the
+// row statistics. Phase 2: one thread per key — A formed from S and the row
+// statistics, aggregated over queries in query order (max, RMS or mean),
+// plus the per-key max used by sensitivity weighting (math.h:579-594).
+constexpr int SMI_ROWS = 2048;   // row statistics held in shared memory (more rows: read from global)
+
 __global__ void __launch_bounds__(256) k_softmax_importance(const kvc_unit * __restrict__ units,
                                                            kvc_params_dev P, float * __restrict__ fs) {
     const kvc_unit u = units[blockIdx.y];
     const int h = blockIdx.x;
     const int C = u.C, nq = u.nq;
-    float * S = fs + u.s_off + (long long)h * nq * C;
+    const float * S = fs + u.s_off + (long long)h * nq * C;
     float * rmax = fs + u.row_off + (long long)h * 2 * nq;
     float * rsum = rmax + nq;
+    __shared__ float sm_m[SMI_ROWS], sm_inv[SMI_ROWS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     for (int q = warp; q < nq; q += nw) {
-        float * row = S + (long long)q * C;
+        const float * row = S + (long long)q * C;
         float m = row[0];
         for (int j = lane; j < C; j += 32) { float v = row[j]; if (v > m) m = v; }
         for (int o = 16; o; o >>= 1) { float v = __shfl_xor_sync(0xffffffffu, m, o); if (v > m) m = v; }
         float s = 0.0f;
-        for (int j = lane; j < C; j += 32) {
-            float e = expf(__fsub_rn(row[j], m));
-            row[j] = e;
-            s = __fadd_rn(s, e);
-        }
+        for (int j = lane; j < C; j += 32) s = __fadd_rn(s, expf(__fsub_rn(row[j], m)));
         for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        float inv = __fdiv_rn(1.0f, __fadd_rn(s, 1e-12f));
-        for (int j = lane; j < C; j += 32) row[j] = __fmul_rn(row[j], inv);
-        if (lane == 0) { rmax[q] = m; rsum[q] = s; }
+        if (lane == 0) {
+            rmax[q] = m;
+            rsum[q] = s;
+            if (q < SMI_ROWS) { sm_m[q] = m; sm_inv[q] = softmax_inv(s); }
+        }
     }
     __syncthreads();
     float * imp = fs + u.imp_off + (long long)h * C;
     float * cmax = fs + u.imp_off + (long long)(P.H + h) * C;
     const float inv_m = __fdiv_rn(1.0f, (float)nq);
+    constexpr int QB = 8;                    // rows whose loads are in flight together
     for (int j = threadIdx.x; j < C; j += blockDim.x) {
         float acc = 0.0f, mx = 0.0f;
-        for (int q = 0; q < nq; q++) {
-            float w = S[(long long)q * C + j];
-            if (P.score_method == 0) { if (w > acc) acc = w; }
-            else if (P.score_method == 1) acc = __fadd_rn(acc, __fmul_rn(w, w));
-            else acc = __fadd_rn(acc, w);
-            if (w > mx) mx = w;
+        for (int q0 = 0; q0 < nq; q0 += QB) {
+            float v[QB];
+#pragma unroll
+            for (int k = 0; k < QB; k++) v[k] = q0 + k < nq ? S[(long long)(q0 + k) * C + j] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < QB; k++) {       // aggregated in query order
+                const int q = q0 + k;
+                if (q >= nq) break;
+                const float m = q < SMI_ROWS ? sm_m[q] : rmax[q];
+                const float inv = q < SMI_ROWS ? sm_inv[q] : softmax_inv(rsum[q]);
+                const float w = softmax_entry(v[k], m, inv);
+                if (P.score_method == 0) { if (w > acc) acc = w; }
+                else if (P.score_method == 1) acc = __fadd_rn(acc, __fmul_rn(w, w));
+                else acc = __fadd_rn(acc, w);
+                if (w > mx) mx = w;
+            }
         }
         if (P.score_method == 1) acc = sqrtf(__fmul_rn(acc, inv_m));
         else if (P.score_method == 2) acc = __fmul_rn(acc, inv_m);
@@ -381,32 +409,59 @@ __global__ void __launch_bounds__(256) k_softmax_importance(const kvc_unit * __r
     }
 }
 
+// X block of the refit: X[q][j] = S[q][sel[j]], the raw scores of the kept
+// keys (the same values the scoring computed, bit for bit); one warp per row.
+__global__ void __launch_bounds__(256) k_gather_x(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                  float * __restrict__ fs, const int * __restrict__ is) {
+    const kvc_unit u = units[blockIdx.z];
+    if (!u.active) return;
+    const int h = blockIdx.y, nq = u.nq, t = u.t, C = u.C;
+    const int * sel = is + u.sel_off;
+    const float * S = fs + u.s_off + (long long)h * nq * C;
+    float * X = fs + u.x_off + (long long)h * nq * t;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int q = blockIdx.x * 8 + warp; q < nq; q += gridDim.x * 8) {
+        const float * row = S + (long long)q * C;
+        float * xr = X + (long long)q * t;
+        for (int j = lane; j < t; j += 32) xr[j] = row[sel[j]];
+    }
+    (void)P;
+}
+
 // Y_h [nq x dv] = A_h [nq x C] . V_h [C x dv]; 64x64 output tile per CTA.
 __global__ void __launch_bounds__(ST) k_pv(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                           float * __restrict__ fs) {
+                                           float * __restrict__ fs, int from_scores) {
     const kvc_unit u = units[blockIdx.z];
     const int h = blockIdx.y;
     const int dv = P.dv, ev = P.H * P.dv, nq = u.nq, C = u.C;
     const int tq = (nq + SB - 1) / SB, tn = (dv + SB - 1) / SB;
     if ((int)blockIdx.x >= tq * tn) return;
     const int q0 = (blockIdx.x / tn) * SB, n0 = (blockIdx.x % tn) * SB;
-    const float * A = fs + u.s_off + (long long)h * nq * C;
+    const float * S = fs + u.s_off + (long long)h * nq * C;    // A, or raw scores A is formed from
+    const float * rmax = fs + u.row_off + (long long)h * 2 * nq;
     const float * V = u.V + (long long)h * dv;
     float * Y = fs + u.y_off + (long long)h * nq * dv;
 
     __shared__ float As[SK][SB + 4];   // [k][row]
     __shared__ float Vs[SK][SB + 4];   // [k][col]
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int ar = tid >> 2, aq = q0 + ar;                    // the A row this thread stages
+    const bool rs = from_scores && aq < nq;
+    const float am = rs ? rmax[aq] : 0.0f, ainv = rs ? softmax_inv(rmax[nq + aq]) : 0.0f;
     float acc[4][4] = {};
     for (int k0 = 0; k0 < C; k0 += SK) {
         // A tile: 64 rows x 32 k; thread -> row tid/4, 8 consecutive k
         {
-            int r = tid >> 2, c = (tid & 3) * 8;
-            int q = q0 + r;
+            const int c = (tid & 3) * 8;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 int k = k0 + c + i;
-                As[c + i][r] = (q < nq && k < C) ? A[(long long)q * C + k] : 0.0f;
+                float a = 0.0f;
+                if (aq < nq && k < C) {
+                    a = S[(long long)aq * C + k];
+                    if (from_scores) a = softmax_entry(a, am, ainv);
+                }
+                As[c + i][ar] = a;
             }
         }
         // V tile: 32 k x 64 cols; thread -> k tid/8, 8 consecutive cols
@@ -506,6 +561,15 @@ int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_
     return KVC_OK;
 }
 
+int kvc_launch_gather_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P, float * fs,
+                        const int * is, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    const int gx = (max_nq + 7) / 8 < 16 ? (max_nq + 7) / 8 : 16;
+    k_gather_x<<<dim3(gx, P.H, n_units), 256, 0, st>>>(d_units, P, fs, is);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
 int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const kvc_params_dev & P,
                                   float * fs, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
@@ -515,11 +579,11 @@ int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const k
 }
 
 int kvc_launch_pv(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
-                  float * fs, cudaStream_t st) {
+                  float * fs, bool from_scores, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
-    if (kvc_pv_tc_ok(max_nq, P.dv)) return kvc_launch_pv_tc(d_units, n_units, P, fs, st);
+    if (kvc_pv_tc_ok(max_nq, P.dv)) return kvc_launch_pv_tc(d_units, n_units, P, fs, from_scores, st);
     int tiles = ((max_nq + SB - 1) / SB) * ((P.dv + SB - 1) / SB);
-    k_pv<<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs);
+    k_pv<<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs, from_scores ? 1 : 0);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
