@@ -159,3 +159,24 @@ def exact_cv(K, V, Q, H, d, sel, beta, units, p, q_null):
 def rel_l2(a, b):
     a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def nnls_residuals(K, Q, H, d, sel, beta, units):
+    """Per (chunk, head): the residual ||M w - b|| of the bias fit in fp64,
+    with M[q, j] = exp(S[q, sel_j] - max_q), b[q] = sum_j exp(S[q, j] - max_q)
+    over the chunk's keys and w = exp(beta) (the problem the reference's
+    Lawson-Hanson fit solves, src/kv-compact-api.cpp:812-831)."""
+    K64, Q64 = K.astype(np.float64), Q.astype(np.float64)
+    sel = np.asarray(sel)
+    out = []
+    off = 0
+    for (st, C, t, pre, cheap_chunk) in units:
+        s_loc = sel[off:off + t] - st
+        for h in range(H):
+            S = Q64[:, h * d:(h + 1) * d] @ K64[st:st + C, h * d:(h + 1) * d].T / math.sqrt(d)
+            E = np.exp(S - S.max(axis=1, keepdims=True))
+            w = np.exp(beta[h, off:off + t].astype(np.float64))
+            out.append(float(np.linalg.norm(E[:, s_loc] @ w - E.sum(axis=1))))
+        off += t
+    return np.array(out)
+

@@ -1,7 +1,9 @@
 """GPU tests at configuration shapes: the whole-model batched API against the
-drop-in C ABI, cfg1/cfg2-shaped layers against the reference CPU library
-(oracle/_ref when built, else the C oracle), the device codecs, and
-size-independent properties at the full cfg4 size."""
+drop-in C ABI, cfg1/cfg2/cfg5-shaped layers against the reference CPU library
+(oracle/_ref when built, else the C oracle), a full cfg3 layer (1M tokens)
+with reference parity on chunks the reference compacts on their own token
+ranges, the device codecs, and size-independent properties at the full cfg4
+size."""
 import ctypes
 import os
 
@@ -93,6 +95,98 @@ def test_cfg2_layer_f16(kvc, oracle, cpu_ref):
         print(f"cfg2 layer: C_v rel-L2 ours {e_ours:.2e} reference {e_ref:.2e} (vs fp64), "
               f"ours vs reference {parity.rel_l2(ours['C_v'], theirs['C_v']):.2e}")
         assert e_ours <= max(parity.CV_REL_TOL, e_ref)
+
+
+def test_cfg5_layer_beta_diversity_refine(kvc, cpu_ref):
+    """One cfg5 layer: 4 KV heads, d=128, T=32768, fp32 K/V with the cfg1
+    distributions, 256 reference queries ~N(0,1); Lawson-Hanson beta
+    (nnls_method 0), cosine-diversity 0.1, 2 rounds of worst-key refinement,
+    10% (13 chunks of 2560). Indices must equal the reference's; C_v within
+    tolerance of the fp64 solve for the beta it was fitted with (or no
+    farther than the reference's); the beta fit's residual no larger than
+    the reference's; cosine >= 0.9999 x the reference's."""
+    ref, _ = cpu_ref
+    T, H, d, nq = 32768, 4, 128, 256
+    rng = np.random.default_rng(5)
+    K = workloads.lowrank_keys(rng, T, H, d)
+    V = rng.standard_normal((T, H * d)).astype(np.float32)
+    Q = rng.standard_normal((nq, H * d)).astype(np.float32)
+    pk = dict(target_ratio=0.1, skip_beta=0, nnls_method=0, use_diversity=1, diversity_strength=0.1,
+              refine_rounds=2)
+    rc, ours = abi.run_compact(kvc, K, V, Q, nq, H, d, d, abi.make_params(kvc, **pk))
+    assert rc == 0
+    rc, theirs = abi.run_compact(ref, K, V, Q, nq, H, d, d, abi.make_params(ref, **pk))
+    assert rc == 0
+    units = parity.plan_units(T, pk)
+    assert len(units) == 13 and ours["t"] == theirs["t"] == 3276
+    np.testing.assert_array_equal(ours["indices"], theirs["indices"])
+    assert ours["stats"]["avg_cosine_sim"] >= parity.COS_RATIO * theirs["stats"]["avg_cosine_sim"] - 1e-6
+    sel = theirs["indices"]
+    r_ours = parity.nnls_residuals(K, Q, H, d, sel, ours["beta"], units)
+    r_ref = parity.nnls_residuals(K, Q, H, d, sel, theirs["beta"], units)
+    print(f"\ncfg5 layer: beta rel-L2 vs reference {parity.rel_l2(ours['beta'], theirs['beta']):.2e}; "
+          f"fit residual ours/reference max {np.max(r_ours / r_ref):.6f}")
+    assert np.all(r_ours <= r_ref * (1 + 1e-4) + 1e-9)
+    e_ours = parity.rel_l2(ours["C_v"], parity.exact_cv(K, V, Q, H, d, sel, ours["beta"], units, pk, False))
+    e_ref = parity.rel_l2(theirs["C_v"], parity.exact_cv(K, V, Q, H, d, sel, theirs["beta"], units, pk, False))
+    print(f"cfg5 layer: C_v rel-L2 ours {e_ours:.2e} reference {e_ref:.2e} (each vs the fp64 solve for its beta)")
+    assert e_ours <= max(parity.CV_REL_TOL, e_ref)
+
+
+def test_cfg3_long_context_layer(kvc, oracle, cpu_ref):
+    """cfg3: one layer of T = 1,048,576 tokens, 8 KV heads, d=128, fp16 K/V,
+    SnapKV n_q=128, 20% with the first 1024 tokens kept verbatim (shared
+    prefix), auto chunks of 1280 (820 chunks; chunk 0 keeps 1024), through
+    the drop-in kv_compact_quantized. At full size: the planned counts,
+    chunk 0 = the prefix, every chunk inside its bounds, K_out = the K rows
+    at the kept indices, finite C_v, stats in range. Against the reference:
+    chunks 0-2 and the last chunk, which it compacts on their own token
+    ranges (a chunk's result depends only on its tokens, the queries and, for
+    chunk 0, the prefix)."""
+    import torch
+    ref, _ = cpu_ref
+    T, H, d, nq = 1 << 20, 8, 128, 128
+    Kd, Vd, Qd = _model(kvc, T, H, d, 1, abi.KV_TYPE_F16, 17)
+    Kq, Vq, Q = Kd[0].cpu().numpy(), Vd[0].cpu().numpy(), Qd[0].cpu().numpy()
+    del Kd, Vd, Qd
+    torch.cuda.empty_cache()
+    krb = Kq.shape[1]
+    pk = dict(target_ratio=0.2, n_shared_prefix=1024)
+    rc, ours = abi.run_quantized(kvc, Kq, Vq, Q, 1, 1, krb, krb, T, nq, H, d, d, abi.make_params(kvc, **pk))
+    assert rc == 0
+    units = parity.plan_units(T, pk)
+    assert len(units) == 820 and units[0][2] == 1024 and units[1][2] == 256
+    assert ours["t"] == sum(u[2] for u in units) == 210483
+    sel = ours["indices"]
+    np.testing.assert_array_equal(sel[:1024], np.arange(1024))
+    assert np.all(np.diff(sel) > 0)
+    off = 0
+    for (st, C, tc, _, _) in units:
+        assert sel[off:off + tc].min() >= st and sel[off:off + tc].max() < st + C
+        off += tc
+    np.testing.assert_array_equal(ours["K_out"], Kq[sel])          # F16 rows re-encode to themselves
+    assert np.isfinite(ours["C_v"]).all() and np.isfinite(ours["beta"]).all()
+    print(f"\ncfg3 layer: t={ours['t']} stats {ours['stats']}")
+    assert 0.9 < ours["stats"]["avg_cosine_sim"] <= 1.0001
+    last = units[-1]
+    for lo, hi, o0, o1, p_sub in [(0, 3 * 1280, 0, 1024 + 2 * 256, pk),
+                                  (last[0], T, ours["t"] - last[2], ours["t"], dict(target_ratio=0.2))]:
+        n = hi - lo
+        rc, theirs = abi.run_quantized(ref, Kq[lo:hi], Vq[lo:hi], Q, 1, 1, krb, krb, n, nq, H, d, d,
+                                       abi.make_params(ref, **p_sub))
+        assert rc == 0 and theirs["t"] == o1 - o0
+        Kf, Vf = abi.dequantize_rows(kvc, Kq[lo:hi], 1, H * d), abi.dequantize_rows(kvc, Vq[lo:hi], 1, H * d)
+        imp = trace_importance(oracle, lambda: abi.run_compact(oracle, Kf, Vf, Q, nq, H, d, d,
+                                                                 abi.make_params(oracle, **p_sub)))(n)
+        mine = sel[o0:o1] - lo
+        sub_units = parity.plan_units(n, p_sub)
+        n_ties = check_indices(mine, theirs["indices"], imp, sub_units)
+        print(f"cfg3 tokens [{lo}, {hi}): {n_ties} near-tie swaps of {o1 - o0}")
+        if np.array_equal(mine, theirs["indices"]):
+            ex = parity.exact_cv(Kf, Vf, Q, H, d, mine, theirs["beta"], sub_units, p_sub, False)
+            e_ours, e_ref = parity.rel_l2(ours["C_v"][:, o0:o1], ex), parity.rel_l2(theirs["C_v"], ex)
+            print(f"cfg3 tokens [{lo}, {hi}): C_v rel-L2 ours {e_ours:.2e} reference {e_ref:.2e} (vs fp64)")
+            assert e_ours <= max(parity.CV_REL_TOL, e_ref)
 
 
 @pytest.mark.parametrize("kc,refit,chunks", [(1, 1, 1), (4, 2, 2)])
