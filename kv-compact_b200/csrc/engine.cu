@@ -414,9 +414,20 @@ static unit_sizes sizes_of(const kvc_plan_unit & u, int H, int dv, bool omp) {
 }
 
 int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, int dv,
-                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase, bool metric_partials) {
+                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase, bool metric_partials,
+                   const kvc_shared_sel * shared) {
     if (n_jobs <= 0) return KVC_OK;
     cudaStream_t st = ctx->stream;
+    const int T_sh = shared ? jobs[0].plan->T : 0;
+    if (shared) {                                // one unchunked unit per job, all over the same positions
+        if (p.use_diversity || p.use_omp) return KVC_ERR_SHAPE;
+        for (int l = 0; l < n_jobs; l++) {
+            const kvc_plan & pl = *jobs[l].plan;
+            if (jobs[l].io || pl.units.size() != 1 || pl.T != T_sh || pl.units[0].C != T_sh ||
+                pl.units[0].t != shared->t || pl.units[0].start != 0)
+                return KVC_ERR_SHAPE;
+        }
+    }
     if (p.use_sensitivity && H > 64) return KVC_ERR_SHAPE;
     if (dk > KVC_MAX_D || dv > KVC_MAX_D) return KVC_ERR_SHAPE;
 
@@ -437,9 +448,10 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     P.omp_refit_interval = p.omp_refit_interval;
 
     // ---- layer outputs table
-    if (ctx->outs_cap < (size_t)n_jobs) {
-        if (ctx->d_outs) cudaFree(ctx->d_outs);
-        ctx->outs_cap = (size_t)n_jobs * 2;
+    const size_t n_outs = (size_t)n_jobs + (shared ? 1 : 0);     // + the shared selection's own entry
+    if (ctx->outs_cap < n_outs) {
+        if (ctx->d_outs) { KVC_CUDA(cudaStreamSynchronize(st)); cudaFree(ctx->d_outs); }
+        ctx->outs_cap = n_outs * 2;
         KVC_CUDA(cudaMalloc(&ctx->d_outs, ctx->outs_cap * sizeof(kvc_layer_out)));
     }
     std::vector<kvc_layer_out> outs(n_jobs);
@@ -646,6 +658,27 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         max_gs = std::max(max_gs, bt.gs);
         B.push_back(std::move(bt));
     }
+    // shared selection: global importance, per-(job, head) sensitivities, and
+    // a unit over all T positions whose selection every job then takes
+    long long sh_gimp = 0, sh_sens = 0, sh_sel = 0;
+    kvc_unit sh_unit;
+    memset(&sh_unit, 0, sizeof(sh_unit));
+    if (shared) {
+        if (B.size() != 1) return KVC_ERR_SHAPE;
+        batch & bt = B[0];
+        sh_gimp = bt.fs; bt.fs += al32(T_sh);
+        sh_sens = bt.fs; bt.fs += al32((long long)n_jobs * H);
+        sh_sel = bt.is; bt.is += al32(shared->t);
+        sh_unit.c_off = bt.is; bt.is += al32(4LL * T_sh);
+        sh_unit.sel_off = sh_sel;
+        sh_unit.imp_off = sh_gimp - 2LL * H * T_sh;  // the select kernel reads fs + imp_off + 2*H*C
+        sh_unit.C = T_sh;
+        sh_unit.t = shared->t;
+        sh_unit.layer = n_jobs;
+        sh_unit.active = 1;
+        max_fs = std::max(max_fs, bt.fs);
+        max_is = std::max(max_is, bt.is);
+    }
     void * a0; void * a1; void * a2;
     int rc;
     if ((rc = kvc_arena(ctx, 0, (size_t)max_fs * 4, &a0))) return rc;
@@ -654,17 +687,27 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     float * F = (float *)a0;
     int * I = (int *)a1;
     double * G = (double *)a2;
-    if (ctx->units_cap < all.size()) {
+    const size_t n_table = all.size() + (shared ? 1 : 0);
+    if (ctx->units_cap < n_table) {
         if (ctx->d_units) { KVC_CUDA(cudaStreamSynchronize(st)); cudaFree(ctx->d_units); }
-        ctx->units_cap = all.size() * 2;
+        ctx->units_cap = n_table * 2;
         KVC_CUDA(cudaMalloc(&ctx->d_units, ctx->units_cap * sizeof(kvc_unit)));
     }
     {
         std::vector<kvc_unit> table;
-        table.reserve(all.size());
+        table.reserve(n_table);
         for (const batch & bt : B) table.insert(table.end(), bt.U.begin(), bt.U.end());
+        if (shared) table.push_back(sh_unit);
         KVC_CUDA(cudaMemcpyAsync(ctx->d_units, table.data(), table.size() * sizeof(kvc_unit),
                                  cudaMemcpyHostToDevice, st));
+    }
+    if (shared) {                                 // the shared unit's output entry: its selection slot
+        kvc_layer_out so;
+        memset(&so, 0, sizeof(so));
+        so.sel = I + sh_sel;
+        so.t_total = shared->t;
+        so.n_chunks = 1;
+        KVC_CUDA(cudaMemcpyAsync(ctx->d_outs + n_jobs, &so, sizeof(so), cudaMemcpyHostToDevice, st));
     }
 
     // ---- bulk uploads of a streamed job, group by group on the copy stream.
@@ -815,12 +858,30 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         }
         return KVC_OK;
     }
+    // scoring phase of the shared selection: scores and importances of every
+    // unit, then one selection for all of them
+    auto scoring_shared = [&](const batch & bt, cudaStream_t s) -> int {
+        const int nu = (int)bt.U.size();
+        const kvc_unit * du = ctx->d_units + bt.u0;
+        int e;
+        {
+            kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1, s);
+            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, I, 0, s, rows_aligned))) return e;
+        }
+        {
+            kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1, s);
+            if ((e = kvc_launch_softmax_importance(du, nu, P, F, s))) return e;
+        }
+        kvc_stage_timer tm(ctx, KVC_ST_SELECT, P.use_sensitivity ? 4 : 3, s);
+        return kvc_launch_shared_select(du, nu, ctx->d_units + all.size(), P, F, I, F + sh_gimp, F + sh_sens,
+                                        I + sh_sel, T_sh, shared->t, ctx->d_outs, s);
+    };
     for (size_t bi = 0; bi < B.size(); bi++) {
         const batch & bt = B[bi];
         if ((rc = weights(bt, st))) return rc;
         if (io && ev_k[bi] && (rc = arrive(ev_k[bi], io->k, jobs[0].K, H * dk, bt.row0, bt.row1, st))) return rc;
         if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
-        if ((rc = scoring(bt, st))) return rc;
+        if ((rc = shared ? scoring_shared(bt, st) : scoring(bt, st))) return rc;
         if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
         if (io && (rc = arrive(ev_v[bi], io->v, jobs[0].V, H * dv, bt.row0, bt.row1, st))) return rc;
         if ((rc = refit(bt, st))) return rc;

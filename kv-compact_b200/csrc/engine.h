@@ -99,8 +99,8 @@ struct kvc_ctx {
     std::vector<cudaEvent_t> sync_ev;           // cross-stream ordering events (no timing), grow-only
     size_t sync_used = 0;
     std::mutex mu;
-    void * arena[10] = {};
-    size_t arena_cap[10] = {};
+    void * arena[16] = {};          // slots: 0-2 engine scratch, 3-9 API / batched / seam, 10-13 state path
+    size_t arena_cap[16] = {};
     kvc_unit * d_units = nullptr;
     size_t units_cap = 0;
     kvc_layer_out * d_outs = nullptr;
@@ -191,8 +191,16 @@ int kvc_arena(kvc_ctx * ctx, int slot, size_t bytes, void ** out);
 // queries also get per-chunk quality-metric records (jobs[l].out.mpart, in
 // arena slot 8, valid until the next run), which kvc_engine_metrics merges
 // instead of re-reading the whole cache.
+// With `shared`, every job is one unchunked unit over the same T positions
+// and they all keep one selection: the top-t of the importance aggregated
+// over every job and head (the llama.cpp state path, kvc-state.h). All jobs
+// must fit one batch; diversity and OMP selection are not available there.
+struct kvc_shared_sel {
+    int t;                          // positions kept in every job
+};
 int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, int dv,
-                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase, bool metric_partials);
+                   kvc_layer_job * jobs, int n_jobs, kvc_phase_ms * phase, bool metric_partials,
+                   const kvc_shared_sel * shared = nullptr);
 
 // Scoring / refit milliseconds of the kvc_engine_run calls since the last
 // collection (the stream must have drained).
@@ -234,6 +242,14 @@ int kvc_launch_aggregate(const kvc_unit * d_units, int n_units, const kvc_params
                          cudaStream_t st);
 int kvc_launch_select(const kvc_unit * d_units, int n_units, int max_C, const kvc_params_dev & P, float * fs,
                       int * is, const kvc_layer_out * d_outs, cudaStream_t st);
+// One selection for every unit (each spanning positions 0..T-1): global
+// importance over all units and heads into gimp (sensitivities of each
+// (unit, head) into sens when P.use_sensitivity), top-t of it by the unit
+// d_all (one unit over gimp, its selection at is + d_all->sel_off ==
+// all_sel), then broadcast to every unit and its layer's output indices.
+int kvc_launch_shared_select(const kvc_unit * d_units, int n_units, const kvc_unit * d_all, const kvc_params_dev & P,
+                             float * fs, int * is, float * gimp, float * sens, const int * all_sel, int T, int t,
+                             const kvc_layer_out * d_outs, cudaStream_t st);
 size_t kvc_lsq_smem_bytes(int n);
 // LS refit in three launches: Gram (and primal right-hand side) products,
 // factorisation + solves, output product (dual form).

@@ -8,7 +8,8 @@
 //
 // Device layout (all row-major, resident in HBM):
 //   K, V          [T x H*d] fp32 per layer (dequantised once if stored quantised)
-//   S / A         per (unit, head) [n_q x C] scores, overwritten by softmax weights
+//   S             per (unit, head) [n_q x C] raw scores (kept: consumers of the
+//                 softmax A form it from S and the row statistics)
 //   imp           per (unit, head) [C] importance, plus [C] aggregated per unit
 //   Y             per (unit, head) [n_q x d_v] = A_h V_h
 //   X             per (unit, head) [n_q x t]   = softmax(S[:, sel] + beta)
@@ -64,8 +65,8 @@ struct kvc_unit {
     int token_base;       // chunk start within the layer (added to indices)
     int active;           // refinement: 0 once the unit stopped swapping
     int chunk;            // chunk index within its layer
-    long long s_off;      // floats: S/A scratch, H blocks of nq*C
-    long long imp_off;    // floats: (H+1) blocks of C (per head, then aggregated)
+    long long s_off;      // floats: raw scores S, H blocks of nq*C
+    long long imp_off;    // floats: 2H+1 blocks of C (per head, per-head column max, aggregated)
     long long row_off;    // floats: H blocks of nq (row max / row sum)
     long long y_off;      // floats: H blocks of nq*dv
     long long x_off;      // floats: H blocks of nq*t

@@ -20,9 +20,11 @@
 //   penalty update with the cosine between the chosen key and every unused
 //   key over the full n_embd = H*d_k row. Dot products and norms keep the
 //   reference's sequential fp32 order; norms are computed once per key.
-#include "kvc_internal.h"
+#include "engine.h"
 
 #include <math.h>
+
+#include <algorithm>
 
 namespace {
 
@@ -347,6 +349,87 @@ __global__ void __launch_bounds__(1024) k_select_diverse(const kvc_unit * __rest
     for (int i = threadIdx.x; i < n; i += blockDim.x) used[order[i]] = 1;
     __syncthreads();
     emit_selected(u, used, sel, lo, shi);
+}
+
+// ---- one selection shared by every unit of a call ---------------------------
+// (the llama.cpp state path: one unit per layer spanning all cells; the cells
+// kept must be the same in every layer, src/kv-compact.cpp:470-566)
+
+// Sensitivity of each (unit, head): max_j cmax[j] / (mean_j cmax[j] + 1e-12)
+// of the per-key maximum attention (include/kv-compact-math.h:579-594),
+// reduced as k_aggregate reduces it.
+__global__ void __launch_bounds__(256) k_unit_head_sens(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                        const float * __restrict__ fs, float * __restrict__ sens) {
+    const kvc_unit u = units[blockIdx.y];
+    const int h = blockIdx.x, C = u.C, H = P.H;
+    __shared__ float red[32];
+    const float * cm = fs + u.imp_off + (long long)(H + h) * C;
+    float mx = 0.0f, sm = 0.0f;
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+        const float v = cm[j];
+        if (v > mx) mx = v;
+        sm = __fadd_rn(sm, v);
+    }
+    mx = block_max(mx, red);
+    sm = block_sum(sm, red);
+    if (threadIdx.x == 0) sens[blockIdx.y * H + h] = __fdiv_rn(mx, __fadd_rn(__fdiv_rn(sm, (float)C), 1e-12f));
+}
+
+// Importance of every position over all units and heads: the maximum of the
+// per-head importances, or (with sensitivity weighting) the sum of s * imp
+// accumulated unit by unit, head by head, as the reference accumulates it
+// layer by layer (accumulate_weighted_importance, math.h:607-618).
+__global__ void __launch_bounds__(256) k_global_importance(const kvc_unit * __restrict__ units, int n_units,
+                                                           kvc_params_dev P, const float * __restrict__ fs,
+                                                           const float * __restrict__ sens, int T,
+                                                           float * __restrict__ gimp) {
+    extern __shared__ long long imp_base[];         // per unit: offset of its head-0 importance
+    for (int i = threadIdx.x; i < n_units; i += blockDim.x) imp_base[i] = units[i].imp_off;
+    __syncthreads();
+    const int H = P.H;
+    for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < T; j += (long long)gridDim.x * blockDim.x) {
+        float g = 0.0f;
+        for (int i = 0; i < n_units; i++)
+            for (int h = 0; h < H; h++) {
+                const float v = fs[imp_base[i] + (long long)h * T + j];
+                if (P.use_sensitivity) g = __fadd_rn(g, __fmul_rn(sens[i * H + h], v));
+                else if (v > g) g = v;
+            }
+        gimp[j] = g;
+    }
+}
+
+// The shared selection (positions 0..T-1, ascending) into every unit's
+// selection slot and its layer's output indices.
+__global__ void k_broadcast_sel(const kvc_unit * __restrict__ units, int * __restrict__ is,
+                                const int * __restrict__ sel, int t, const kvc_layer_out * __restrict__ outs) {
+    const kvc_unit u = units[blockIdx.y];
+    const kvc_layer_out lo = outs[u.layer];
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < t; j += gridDim.x * blockDim.x) {
+        is[u.sel_off + j] = sel[j];
+        lo.sel[u.out_off + j] = u.token_base + sel[j];
+    }
+}
+
+int kvc_launch_shared_select(const kvc_unit * d_units, int n_units, const kvc_unit * d_all, const kvc_params_dev & P,
+                             float * fs, int * is, float * gimp, float * sens, const int * all_sel, int T, int t,
+                             const kvc_layer_out * d_outs, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    if (P.use_sensitivity) {
+        k_unit_head_sens<<<dim3(P.H, n_units), 256, 0, st>>>(d_units, P, fs, sens);
+        KVC_CUDA(cudaGetLastError());
+    }
+    const int g = (int)std::min<long long>(((long long)T + 255) / 256, 148LL * 8);
+    k_global_importance<<<g, 256, (size_t)n_units * sizeof(long long), st>>>(d_units, n_units, P, fs, sens, T, gimp);
+    KVC_CUDA(cudaGetLastError());
+    kvc_params_dev Ps = P;                          // plain top-t over all positions
+    Ps.use_diversity = 0;
+    int rc;
+    if ((rc = kvc_launch_select(d_all, 1, T, Ps, fs, is, d_outs, st))) return rc;
+    const int gx = (t + 255) / 256 < 64 ? (t + 255) / 256 : 64;
+    k_broadcast_sel<<<dim3(gx > 0 ? gx : 1, n_units), 256, 0, st>>>(d_units, is, all_sel, t, d_outs);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
 }
 
 int kvc_launch_aggregate(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,
