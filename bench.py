@@ -185,10 +185,11 @@ def run_reference(args, cfg, name):
 # summarised in profiles/main_kernels_cfg4_q8_1layer.md. Traffic grows in
 # proportion to the layers of a launch, so a full-step launch is scaled by 12.
 NCU_TRAFFIC_PER_LAYER_HEAD = {
-    "k_score": (410.3e6 + 363.9e6) / 8,
-    "k_score_async": (410.3e6 + 363.9e6) / 8,
-    "k_pv_tc": (819.3e6 + 33.6e6) / 8,
-    "k_lsq_factor": (123.5e6 + 43.6e6) / 8,
+    "k_score": (410.2e6 + 363.1e6) / 8,
+    "k_score_async": (410.2e6 + 363.1e6) / 8,
+    "k_pv_tc": (820.0e6 + 33.7e6) / 8,
+    "k_softmax_importance": (816.1e6 + 10.2e6) / 8,
+    "k_lsq_factor": (123.2e6 + 40.4e6) / 8,
 }
 
 
@@ -240,7 +241,8 @@ def stage_rooflines(stage_times, cfg, n_steps, clocks, peaks):
                   "rounded multiply and add per term (no FMA, no tensor cores)"),
         "refit_target": ("k_pv_tc", "hbm", "GB/s", 4.0 * (nq + d) * T * H * L + 4.0 * nq * d * H * L * len(units),
                          hbm, hbm_src),
-        "softmax_importance": ("k_softmax_importance", "hbm", "GB/s", 2 * 4.0 * nq * T * H * L, hbm, hbm_src),
+        # the scores are read (once, at least) and nothing of their size is written
+        "softmax_importance": ("k_softmax_importance", "hbm", "GB/s", 4.0 * nq * T * H * L, hbm, hbm_src),
         "decode": ("k_decode_blocks", "hbm", "GB/s", (T * H * d * (kb + vb) + 8.0 * T * H * d) * L, hbm, hbm_src),
         "requant": ("k_encode_gather + k_encode_heads", "hbm", "GB/s",
                     (8.0 * t * H * d + t * H * d * (kb + vb)) * L, hbm, hbm_src),
