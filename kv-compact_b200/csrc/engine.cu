@@ -405,7 +405,8 @@ struct unit_sizes {
 static unit_sizes sizes_of(const kvc_plan_unit & u, int H, int dv, bool omp) {
     unit_sizes s;
     const int n = std::min(u.nq, u.t);
-    s.fs = al32((long long)H * u.nq * u.C) + al32((long long)(2 * H + 1) * u.C) + al32((long long)2 * H * u.nq) +
+    s.fs = al32((long long)H * u.nq * u.C) + al32((long long)H * u.nq * ((u.C + 127) / 128)) +
+           al32((long long)(2 * H + 1) * u.C) + al32((long long)2 * H * u.nq) +
            al32((long long)H * u.nq * dv) + al32((long long)H * u.nq * u.t) + al32((long long)2 * H * u.nq);
     if (omp) s.fs += al32((long long)kvc_omp_floats(u.C, u.t, u.nq, H));
     s.is = al32(u.t) + al32(4LL * u.C);
@@ -622,6 +623,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             u.active = 1;
             u.chunk = all[pos].i;
             u.s_off = bt.fs; bt.fs += al32((long long)H * pu.nq * pu.C);
+            u.pm_off = bt.fs; bt.fs += al32((long long)H * pu.nq * ((pu.C + 127) / 128));
             u.imp_off = bt.fs; bt.fs += al32((long long)(2 * H + 1) * pu.C);
             u.row_off = bt.fs; bt.fs += al32((long long)2 * H * pu.nq);
             u.y_off = bt.fs; bt.fs += al32((long long)H * pu.nq * dv);
@@ -754,7 +756,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         int e;
         {
             kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1, s);
-            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, I, 0, s, rows_aligned))) return e;
+            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, I, 2, s, rows_aligned))) return e;
         }
         if (P.use_omp) {                             // needs the raw scores: before the softmax
             kvc_stage_timer tm(ctx, KVC_ST_SELECT, 1, s);
@@ -762,7 +764,9 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         }
         {
             kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1, s);
-            if ((e = kvc_launch_softmax_importance(du, nu, P, F, s))) return e;
+            if ((e = kvc_launch_softmax_importance(du, nu, bt.max_nq, bt.max_C,
+                                                   kvc_score_tile_keys(bt.max_nq, rows_aligned), P, F, s)))
+                return e;
         }
         kvc_stage_timer tm(ctx, KVC_ST_SELECT, 2, s);
         if ((e = kvc_launch_aggregate(du, nu, P, F, s))) return e;
@@ -866,11 +870,13 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         int e;
         {
             kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1, s);
-            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, I, 0, s, rows_aligned))) return e;
+            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, I, 2, s, rows_aligned))) return e;
         }
         {
             kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1, s);
-            if ((e = kvc_launch_softmax_importance(du, nu, P, F, s))) return e;
+            if ((e = kvc_launch_softmax_importance(du, nu, bt.max_nq, bt.max_C,
+                                                   kvc_score_tile_keys(bt.max_nq, rows_aligned), P, F, s)))
+                return e;
         }
         kvc_stage_timer tm(ctx, KVC_ST_SELECT, P.use_sensitivity ? 4 : 3, s);
         return kvc_launch_shared_select(du, nu, ctx->d_units + all.size(), P, F, I, F + sh_gimp, F + sh_sens,

@@ -223,8 +223,14 @@ int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, 
 int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_cols,
                      const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st,
                      bool rows_aligned = false);
-int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const kvc_params_dev & P,
-                                  float * fs, cudaStream_t st);
+// Key tile of the scoring kernel kvc_launch_score picks (the granularity of
+// its mode-2 row maxima).
+int kvc_score_tile_keys(int max_nq, bool rows_aligned);
+// Row statistics and per-key importance. tile_keys > 0: the scores were
+// written in mode 2 with that key tile (one pass over S when the chunks are
+// small enough); 0: the kernel finds the row maxima itself.
+int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, int max_nq, int max_C, int tile_keys,
+                                  const kvc_params_dev & P, float * fs, cudaStream_t st);
 // X block of the refit: the raw scores of the kept keys, S[:, sel].
 int kvc_launch_gather_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P, float * fs,
                         const int * is, cudaStream_t st);

@@ -77,6 +77,7 @@ struct kvc_unit {
     long long c_off;      // ints/floats: C per-candidate scratch (selection)
     long long xs_off;     // floats: H blocks of 2*nq (row max, row sum of X before normalising)
     long long omp_off;    // floats: OMP selection working arrays (omp.cu), or -1
+    long long pm_off;     // floats: H blocks of nq x ceil(C/128) row maxima of the score tiles (mode 2)
 };
 
 struct kvc_layer_out {

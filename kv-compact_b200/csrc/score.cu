@@ -28,6 +28,7 @@
 #include "engine.h"
 
 #include <math.h>
+#include <stdlib.h>
 
 namespace {
 
@@ -78,7 +79,55 @@ __device__ __forceinline__ void load_rows(float (*dst)[NR + 4], const float * co
 
 }  // namespace
 
-// mode 0: all C keys of the chunk -> S block (ld C)
+// Epilogue of both scoring kernels: S = acc * (1/sqrt(d_k)) into the S block
+// (modes 0, 2) or the X block (mode 1); mode 2 also writes, per row and CTA
+// key tile, the maximum of the row's scores in the tile (exact: a maximum
+// does not depend on order), from which the importance kernel takes the row
+// maxima without a pass over S. Rows of a tile are shared by the NTX = TK/8
+// lanes with the same ty (a half-warp or a warp), reduced with shuffles.
+template <int TQ, int TK>
+__device__ __forceinline__ void store_scores(const kvc_unit & u, const kvc_params_dev & P, float * fs,
+                                             const float (&acc)[8][8], int mode, int ncols, int q0, int j0, int ty,
+                                             int tx, int h) {
+    constexpr int NTX = TK / 8;
+    const int ld = ncols;
+    float * out = fs + (mode != 1 ? u.s_off + (long long)h * u.nq * u.C : u.x_off + (long long)h * u.nq * u.t);
+    const bool vst = (ld & 3) == 0 && ((((uintptr_t)out) & 15) == 0);
+    const int ntile = (u.C + 127) / 128;
+    float * pm = fs + u.pm_off + (long long)h * u.nq * ntile;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int q = q0 + (i < 4 ? 4 * ty + i : TQ / 2 + 4 * ty + i - 4);
+        float * row = out + (long long)q * ld;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int hb = 0; hb < 2; hb++) {
+            const int c = j0 + hb * (TK / 2) + 4 * tx;
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                v[e] = __fmul_rn(acc[i][4 * hb + e], P.isd);
+                if (c + e < ncols) mx = fmaxf(mx, v[e]);
+            }
+            if (q >= u.nq) continue;
+            if (vst && c + 4 <= ncols) {
+                *reinterpret_cast<float4 *>(row + c) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    if (c + e < ncols) row[c + e] = v[e];
+            }
+        }
+        if (mode == 2) {
+#pragma unroll
+            for (int o = NTX / 2; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (tx == 0 && q < u.nq) pm[(long long)q * ntile + j0 / TK] = mx;
+        }
+    }
+}
+
+// mode 0: all C keys of the chunk -> S block (ld C); mode 2: the same plus
+// the row maxima of each key tile (store_scores)
 // mode 1: the t selected keys     -> X block (ld t), X later softmaxed in place
 // CTA tile TQ queries x TK keys (TQ*TK = 16384), 256 threads, 8x8 outputs per
 // thread: rows 4ty+{0..3} and TQ/2+4ty+{0..3}, columns 4tx+{0..3} and
@@ -93,7 +142,7 @@ __global__ void __launch_bounds__(ST, 2) k_score(const kvc_unit * __restrict__ u
     const kvc_unit u = units[blockIdx.z];
     if (!u.active) return;
     const int h = blockIdx.y;
-    const int ncols = mode == 0 ? u.C : u.t;
+    const int ncols = mode != 1 ? u.C : u.t;
     const int tq = (u.nq + TQ - 1) / TQ, tk = (ncols + TK - 1) / TK;
     if ((int)blockIdx.x >= tq * tk) return;
     const int q0 = (blockIdx.x / tk) * TQ, j0 = (blockIdx.x % tk) * TK;
@@ -112,7 +161,7 @@ __global__ void __launch_bounds__(ST, 2) k_score(const kvc_unit * __restrict__ u
         } else {
             const int j = j0 + i - TQ;
             if (j < ncols) {
-                const int key = mode == 0 ? j : sel[j];
+                const int key = mode != 1 ? j : sel[j];
                 kp[i - TQ] = u.K + (long long)key * ek + (long long)h * dk;
             } else {
                 kp[i - TQ] = nullptr;
@@ -164,29 +213,7 @@ __global__ void __launch_bounds__(ST, 2) k_score(const kvc_unit * __restrict__ u
         }
         __syncthreads();
     }
-    const int ld = ncols;
-    float * out = fs + (mode == 0 ? u.s_off + (long long)h * u.nq * u.C : u.x_off + (long long)h * u.nq * u.t);
-    const bool vst = (ld & 3) == 0 && ((((uintptr_t)out) & 15) == 0);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int q = q0 + (i < 4 ? 4 * ty + i : TQ / 2 + 4 * ty + i - 4);
-        if (q >= u.nq) continue;
-        float * row = out + (long long)q * ld;
-#pragma unroll
-        for (int hb = 0; hb < 2; hb++) {
-            const int c = j0 + hb * (TK / 2) + 4 * tx;
-            float v[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) v[e] = __fmul_rn(acc[i][4 * hb + e], P.isd);
-            if (vst && c + 4 <= ncols) {
-                *reinterpret_cast<float4 *>(row + c) = make_float4(v[0], v[1], v[2], v[3]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 4; e++)
-                    if (c + e < ncols) row[c + e] = v[e];
-            }
-        }
-    }
+    store_scores<TQ, TK>(u, P, fs, acc, mode, ncols, q0, j0, ty, tx, h);
 }
 
 // Same tile, operands staged with cp.async (requires 16-byte aligned rows:
@@ -215,7 +242,7 @@ __global__ void __launch_bounds__(ST, 2) k_score_async(const kvc_unit * __restri
     const kvc_unit u = units[blockIdx.z];
     if (!u.active) return;
     const int h = blockIdx.y;
-    const int ncols = mode == 0 ? u.C : u.t;
+    const int ncols = mode != 1 ? u.C : u.t;
     const int tq = (u.nq + TQ - 1) / TQ, tk = (ncols + TK - 1) / TK;
     if ((int)blockIdx.x >= tq * tk) return;
     const int q0 = (blockIdx.x / tk) * TQ, j0 = (blockIdx.x % tk) * TK;
@@ -236,7 +263,7 @@ __global__ void __launch_bounds__(ST, 2) k_score_async(const kvc_unit * __restri
     } else {
         const int j = j0 + tid - TQ;
         if (j < ncols) {
-            const int key = mode == 0 ? j : sel[j];
+            const int key = mode != 1 ? j : sel[j];
             kp[tid - TQ] = u.K + (long long)key * ek + (long long)h * dk;
         } else {
             kp[tid - TQ] = nullptr;
@@ -313,29 +340,7 @@ __global__ void __launch_bounds__(ST, 2) k_score_async(const kvc_unit * __restri
             }
         }
     }
-    const int ld = ncols;
-    float * out = fs + (mode == 0 ? u.s_off + (long long)h * u.nq * u.C : u.x_off + (long long)h * u.nq * u.t);
-    const bool vst = (ld & 3) == 0 && ((((uintptr_t)out) & 15) == 0);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int q = q0 + (i < 4 ? 4 * ty + i : TQ / 2 + 4 * ty + i - 4);
-        if (q >= u.nq) continue;
-        float * row = out + (long long)q * ld;
-#pragma unroll
-        for (int hb = 0; hb < 2; hb++) {
-            const int c = j0 + hb * (TK / 2) + 4 * tx;
-            float v[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) v[e] = __fmul_rn(acc[i][4 * hb + e], P.isd);
-            if (vst && c + 4 <= ncols) {
-                *reinterpret_cast<float4 *>(row + c) = make_float4(v[0], v[1], v[2], v[3]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 4; e++)
-                    if (c + e < ncols) row[c + e] = v[e];
-            }
-        }
-    }
+    store_scores<TQ, TK>(u, P, fs, acc, mode, ncols, q0, j0, ty, tx, h);
 }
 
 // A[q][j] of the row softmax, formed from the raw score s, the row max m
@@ -406,6 +411,111 @@ __global__ void __launch_bounds__(256) k_softmax_importance(const kvc_unit * __r
         else if (P.score_method == 2) acc = __fmul_rn(acc, inv_m);
         imp[j] = acc;
         cmax[j] = mx;
+    }
+}
+
+// Single pass over S for chunks of at most RI_THREADS * RI_CPT keys and
+// SMI_ROWS queries, with the row maxima from the scoring epilogue (mode 2):
+// the CTA walks the rows in blocks of RI_RB, each thread holding its
+// columns' scores of the block (the next block already loading) and turning
+// them into exponentials in place; one CTA-wide reduction per block gives
+// the rows' exp-sums, then A = e * inv (softmax_entry's arithmetic) is
+// aggregated per key in query order as k_softmax_importance aggregates it.
+// S is read once from memory and exp evaluated once per entry. Measured on
+// a cfg4 step: one row per block and 4 CTAs per SM 1.86 ms; 2 rows, 3 CTAs
+// 2.02; 2 rows, 4 CTAs 2.19; 4 rows, 2 CTAs 2.27; 1 row, 6 CTAs 2.15.
+constexpr int RI_THREADS = 256, RI_CPT = 8;
+
+template <int RI_RB, int MINB>
+__global__ void __launch_bounds__(RI_THREADS, MINB) k_row_importance(const kvc_unit * __restrict__ units,
+                                                                  kvc_params_dev P, float * __restrict__ fs,
+                                                                  int tile_keys) {
+    const kvc_unit u = units[blockIdx.y];
+    const int h = blockIdx.x, C = u.C, nq = u.nq, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const float * S = fs + u.s_off + (long long)h * nq * C;
+    const int ntile_alloc = (C + 127) / 128, ntile = (C + tile_keys - 1) / tile_keys;
+    const float * pm = fs + u.pm_off + (long long)h * nq * ntile_alloc;
+    float * rmax = fs + u.row_off + (long long)h * 2 * nq;
+    float * rsum = rmax + nq;
+    __shared__ float sm_m[SMI_ROWS];
+    __shared__ float red[2][RI_RB][RI_THREADS / 32];
+    for (int q = tid; q < nq; q += RI_THREADS) {
+        float m = pm[(long long)q * ntile_alloc];
+        for (int k = 1; k < ntile; k++) m = fmaxf(m, pm[(long long)q * ntile_alloc + k]);
+        sm_m[q] = m;
+    }
+    __syncthreads();
+    auto load_block = [&](int q0, float (&dst)[RI_RB][RI_CPT]) {
+#pragma unroll
+        for (int r = 0; r < RI_RB; r++) {
+            const float * row = S + (long long)(q0 + r) * C;
+#pragma unroll
+            for (int c = 0; c < RI_CPT; c++) {
+                const int j = tid + RI_THREADS * c;
+                dst[r][c] = (q0 + r < nq && j < C) ? row[j] : 0.0f;
+            }
+        }
+    };
+    float cur[RI_RB][RI_CPT], nxt[RI_RB][RI_CPT], acc[RI_CPT], mx[RI_CPT];
+#pragma unroll
+    for (int c = 0; c < RI_CPT; c++) { acc[c] = 0.0f; mx[c] = 0.0f; }
+    load_block(0, cur);
+    for (int q0 = 0, blk = 0; q0 < nq; q0 += RI_RB, blk ^= 1) {
+        if (q0 + RI_RB < nq) load_block(q0 + RI_RB, nxt);
+        float sl[RI_RB];
+#pragma unroll
+        for (int r = 0; r < RI_RB; r++) {
+            const float m = q0 + r < nq ? sm_m[q0 + r] : 0.0f;
+            sl[r] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < RI_CPT; c++) {
+                const int j = tid + RI_THREADS * c;
+                cur[r][c] = j < C ? expf(__fsub_rn(cur[r][c], m)) : 0.0f;
+                sl[r] = __fadd_rn(sl[r], cur[r][c]);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) sl[r] = __fadd_rn(sl[r], __shfl_xor_sync(0xffffffffu, sl[r], o));
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int r = 0; r < RI_RB; r++) red[blk][r][warp] = sl[r];
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < RI_RB; r++) {
+            const int q = q0 + r;
+            if (q >= nq) break;
+            float tot = red[blk][r][0];
+#pragma unroll
+            for (int w = 1; w < RI_THREADS / 32; w++) tot = __fadd_rn(tot, red[blk][r][w]);
+            const float inv = softmax_inv(tot);
+            if (tid == 0) { rmax[q] = sm_m[q]; rsum[q] = tot; }
+#pragma unroll
+            for (int c = 0; c < RI_CPT; c++) {       // aggregated in query order
+                const float w = __fmul_rn(cur[r][c], inv);
+                if (P.score_method == 0) { if (w > acc[c]) acc[c] = w; }
+                else if (P.score_method == 1) acc[c] = __fadd_rn(acc[c], __fmul_rn(w, w));
+                else acc[c] = __fadd_rn(acc[c], w);
+                if (w > mx[c]) mx[c] = w;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RI_RB; r++)
+#pragma unroll
+            for (int c = 0; c < RI_CPT; c++) cur[r][c] = nxt[r][c];
+    }
+    float * imp = fs + u.imp_off + (long long)h * C;
+    float * cmax = fs + u.imp_off + (long long)(P.H + h) * C;
+    const float inv_m = __fdiv_rn(1.0f, (float)nq);
+#pragma unroll
+    for (int c = 0; c < RI_CPT; c++) {
+        const int j = tid + RI_THREADS * c;
+        if (j >= C) continue;
+        float a = acc[c];
+        if (P.score_method == 1) a = sqrtf(__fmul_rn(a, inv_m));
+        else if (P.score_method == 2) a = __fmul_rn(a, inv_m);
+        imp[j] = a;
+        cmax[j] = mx[c];
     }
 }
 
@@ -570,9 +680,19 @@ int kvc_launch_gather_x(const kvc_unit * d_units, int n_units, int max_nq, const
     return KVC_OK;
 }
 
-int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, const kvc_params_dev & P,
-                                  float * fs, cudaStream_t st) {
+int kvc_score_tile_keys(int max_nq, bool rows_aligned) {
+    return (max_nq > 64) ? 128 : 256;            // k_score_async / k_score<128>: 128; k_score<64>: 256
+    (void)rows_aligned;
+}
+
+int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, int max_nq, int max_C, int tile_keys,
+                                  const kvc_params_dev & P, float * fs, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
+    if (tile_keys > 0 && max_C <= RI_THREADS * RI_CPT && max_nq <= SMI_ROWS) {
+        k_row_importance<1, 4><<<dim3(P.H, n_units), RI_THREADS, 0, st>>>(d_units, P, fs, tile_keys);
+        KVC_CUDA(cudaGetLastError());
+        return KVC_OK;
+    }
     k_softmax_importance<<<dim3(P.H, n_units), 256, 0, st>>>(d_units, P, fs);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
