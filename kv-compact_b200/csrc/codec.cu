@@ -218,20 +218,23 @@ __device__ __forceinline__ void decode_quad(const uint8_t * b, int type, int sub
     }
 }
 
+// IT: the index type of the flat quad index — 32-bit whenever the launch's
+// quads fit (the row / block split then costs a 32-bit division instead of
+// a 64-bit one, which dominated these memory-bound loops).
+template <typename IT>
 __global__ void k_decode_blocks(const uint8_t * __restrict__ src, size_t rb, int type,
                                 float * __restrict__ dst, int rows, int n) {
     const int nb = n / QK;
-    const long long total = (long long)rows * nb * 8;
+    const IT total = (IT)rows * (IT)nb * 8;
     const int bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const long long gb = i >> 3;
+    for (IT i = (IT)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (IT)gridDim.x * blockDim.x) {
+        const IT gb = i >> 3;
         const int sub = (int)(i & 7);
-        const long long r = gb / nb;
-        const int b = (int)(gb - r * nb);
+        const IT r = gb / (IT)nb;
+        const int b = (int)(gb - r * (IT)nb);
         float o[4];
-        decode_quad(src + r * rb + (size_t)b * bb, type, sub, o);
-        float * q = dst + r * (long long)n + (long long)b * QK + 4 * sub;
+        decode_quad(src + (size_t)r * rb + (size_t)b * bb, type, sub, o);
+        float * q = dst + (long long)r * n + (long long)b * QK + 4 * sub;
         if ((((uintptr_t)q) & 15) == 0) {
             *reinterpret_cast<float4 *>(q) = make_float4(o[0], o[1], o[2], o[3]);
         } else {
@@ -273,7 +276,10 @@ int kvc_launch_decode(const uint8_t * src, size_t rb, int type, float * dst, int
     if (rows <= 0 || n <= 0) return KVC_OK;
     if (is_block(type)) {
         long long work = (long long)rows * (n / QK) * 8;
-        k_decode_blocks<<<grid_for(work, 256), 256, 0, st>>>(src, rb, type, dst, rows, n);
+        if (work + (long long)148 * 64 * 256 + 64 < (1LL << 32))   // the last grid-stride step stays below 2^32
+            k_decode_blocks<uint32_t><<<grid_for(work, 256), 256, 0, st>>>(src, rb, type, dst, rows, n);
+        else
+            k_decode_blocks<unsigned long long><<<grid_for(work, 256), 256, 0, st>>>(src, rb, type, dst, rows, n);
     } else {
         long long work = (long long)rows * n;
         k_decode_elems<<<grid_for(work, 256), 256, 0, st>>>(src, rb, type, dst, rows, n);
@@ -345,20 +351,20 @@ __device__ __forceinline__ bool dev_is_block(int type) { return type == 8 || typ
 __device__ __forceinline__ long long warp_round(long long n) { return (n + 31) & ~31LL; }
 
 // K_out rows: row j = src[rows_idx[j]] (fp32, stride src_stride) re-encoded.
+template <typename IT>
 __global__ void k_encode_gather(const float * __restrict__ src, size_t stride,
                                 const int * __restrict__ idx, int rows, int n, int type,
                                 uint8_t * __restrict__ dst, size_t drb) {
     if (dev_is_block(type)) {
         const int nb = n / QK, bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
-        const long long total = (long long)rows * nb * 8;
-        for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < warp_round(total);
-             i += (long long)gridDim.x * blockDim.x) {
+        const IT total = (IT)rows * (IT)nb * 8, total_w = (total + 31) & ~(IT)31;
+        for (IT i = (IT)blockIdx.x * blockDim.x + threadIdx.x; i < total_w; i += (IT)gridDim.x * blockDim.x) {
             const bool live = i < total;
-            const long long gb = live ? (i >> 3) : 0;
+            const IT gb = live ? (i >> 3) : 0;
             const int sub = (int)(i & 7);
-            const long long r = gb / nb;
-            const int b = (int)(gb - r * nb);
-            const float * row = src + (idx ? (long long)idx[r] : r) * (long long)stride + (long long)b * QK;
+            const IT r = gb / (IT)nb;
+            const int b = (int)(gb - r * (IT)nb);
+            const float * row = src + (idx ? (long long)idx[r] : (long long)r) * (long long)stride + (long long)b * QK;
             float x[4];
             if ((((uintptr_t)(row + 4 * sub)) & 15) == 0) {
                 const float4 v = *reinterpret_cast<const float4 *>(row + 4 * sub);
@@ -368,18 +374,17 @@ __global__ void k_encode_gather(const float * __restrict__ src, size_t stride,
                 for (int k = 0; k < 4; k++) x[k] = row[4 * sub + k];
             }
             uint8_t tmp[34];
-            uint8_t * o = live ? dst + r * drb + (size_t)b * bb : tmp;
+            uint8_t * o = live ? dst + (size_t)r * drb + (size_t)b * bb : tmp;
             encode_quad(x, row[0], type, sub, o);
         }
         return;
     }
-    const long long total = (long long)rows * n;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const long long r = i / n;
-        const int e = (int)(i - r * n);
-        const float v = src[(idx ? (long long)idx[r] : r) * (long long)stride + e];
-        uint8_t * o = dst + r * drb;
+    const IT total = (IT)rows * (IT)n;
+    for (IT i = (IT)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (IT)gridDim.x * blockDim.x) {
+        const IT r = i / (IT)n;
+        const int e = (int)(i - r * (IT)n);
+        const float v = src[(idx ? (long long)idx[r] : (long long)r) * (long long)stride + e];
+        uint8_t * o = dst + (size_t)r * drb;
         if (type == 1) st16(o + 2 * e, kvc_f2h_trunc(v));
         else memcpy(o + 4 * e, &v, 4);
     }
@@ -387,19 +392,19 @@ __global__ void k_encode_gather(const float * __restrict__ src, size_t stride,
 
 // V_out rows: row j (of `rows`), element e = h*dv + k comes from
 // cv[h][j][k], heads `t` rows apart.
+template <typename IT>
 __global__ void k_encode_heads(const float * __restrict__ cv, int H, int t, int rows, int dv, int type,
                                uint8_t * __restrict__ dst, size_t drb) {
     const int n = H * dv;
     if (dev_is_block(type)) {
         const int nb = n / QK, bb = (type == 8) ? 34 : (type == 2 ? 18 : 20);
-        const long long total = (long long)rows * nb * 8;
-        for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < warp_round(total);
-             i += (long long)gridDim.x * blockDim.x) {
+        const IT total = (IT)rows * (IT)nb * 8, total_w = (total + 31) & ~(IT)31;
+        for (IT i = (IT)blockIdx.x * blockDim.x + threadIdx.x; i < total_w; i += (IT)gridDim.x * blockDim.x) {
             const bool live = i < total;
-            const long long gb = live ? (i >> 3) : 0;
+            const IT gb = live ? (i >> 3) : 0;
             const int sub = (int)(i & 7);
-            const long long j = gb / nb;
-            const int b = (int)(gb - j * nb);
+            const IT j = gb / (IT)nb;
+            const int b = (int)(gb - j * (IT)nb);
             float x[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
@@ -410,16 +415,15 @@ __global__ void k_encode_heads(const float * __restrict__ cv, int H, int t, int 
             const int e0 = b * QK, h0 = e0 / dv;
             const float x0 = cv[((long long)h0 * t + j) * dv + (e0 - h0 * dv)];
             uint8_t tmp[34];
-            uint8_t * o = live ? dst + j * drb + (size_t)b * bb : tmp;
+            uint8_t * o = live ? dst + (size_t)j * drb + (size_t)b * bb : tmp;
             encode_quad(x, x0, type, sub, o);
         }
         return;
     }
-    const long long total = (long long)rows * n;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const long long j = i / n;
-        const int b = (int)(i - j * n);
+    const IT total = (IT)rows * (IT)n;
+    for (IT i = (IT)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (IT)gridDim.x * blockDim.x) {
+        const IT j = i / (IT)n;
+        const int b = (int)(i - j * (IT)n);
         const int h = b / dv, c = b - h * dv;
         const float v = cv[((long long)h * t + j) * dv + c];
         uint8_t * o = dst + j * drb;
@@ -432,7 +436,11 @@ int kvc_launch_encode_gather(const float * src, size_t stride, const int * idx, 
                              int type, uint8_t * dst, size_t drb, cudaStream_t st) {
     if (rows <= 0) return KVC_OK;
     long long work = (long long)rows * (is_block(type) ? (n / QK) * 8 : n);
-    k_encode_gather<<<grid_for(work, 256), 256, 0, st>>>(src, stride, idx, rows, n, type, dst, drb);
+    if (work + (long long)148 * 64 * 256 + 64 < (1LL << 32))   // the last grid-stride step stays below 2^32
+        k_encode_gather<uint32_t><<<grid_for(work, 256), 256, 0, st>>>(src, stride, idx, rows, n, type, dst, drb);
+    else
+        k_encode_gather<unsigned long long><<<grid_for(work, 256), 256, 0, st>>>(src, stride, idx, rows, n, type, dst,
+                                                                              drb);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
@@ -441,7 +449,10 @@ int kvc_launch_encode_heads(const float * cv, int H, int t, int rows, int dv, in
                             size_t drb, cudaStream_t st) {
     if (rows <= 0) return KVC_OK;
     long long work = (long long)rows * (is_block(type) ? ((H * dv) / QK) * 8 : H * dv);
-    k_encode_heads<<<grid_for(work, 256), 256, 0, st>>>(cv, H, t, rows, dv, type, dst, drb);
+    if (work + (long long)148 * 64 * 256 + 64 < (1LL << 32))   // the last grid-stride step stays below 2^32
+        k_encode_heads<uint32_t><<<grid_for(work, 256), 256, 0, st>>>(cv, H, t, rows, dv, type, dst, drb);
+    else
+        k_encode_heads<unsigned long long><<<grid_for(work, 256), 256, 0, st>>>(cv, H, t, rows, dv, type, dst, drb);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }

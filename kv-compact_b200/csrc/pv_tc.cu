@@ -94,9 +94,12 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
         if (!live) return 0.0f;
         return from_scores ? __fmul_rn(__expf(__fsub_rn(sv, am[it])), ainv[it]) : sv;
     };
-    float4 ra[4];
-    float rb[NPB][4];
-    auto load = [&](int s) {
+    // two register sets: the stages s+1 and s+2 are in flight while stage s
+    // is converted into shared memory (one stage of loads per thread alone
+    // leaves too few bytes in flight to keep HBM busy)
+    float4 ra[2][4];
+    float rb[2][NPB][4];
+    auto load = [&](int s, int p) {
         const int k0 = s * PV_KS;
 #pragma unroll
         for (int it = 0; it < 4; it++) {               // A rows: a quarter-warp covers 8 rows of one k-quad
@@ -115,7 +118,7 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
                     if (k + 3 < C) v.w = p[3];
                 }
             }
-            ra[it] = v;
+            ra[p][it] = v;
         }
 #pragma unroll
         for (int pb = 0; pb < NPB; pb++) {             // V: lanes run along d_v (coalesced rows)
@@ -123,10 +126,10 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
             const int n = idx % DV, kq = idx / DV;
             const int k = k0 + 4 * kq;
 #pragma unroll
-            for (int e = 0; e < 4; e++) rb[pb][e] = (k + e < C) ? V[(long long)(k + e) * ev + n] : 0.0f;
+            for (int e = 0; e < 4; e++) rb[p][pb][e] = (k + e < C) ? V[(long long)(k + e) * ev + n] : 0.0f;
         }
     };
-    auto store = [&](int b, int s) {
+    auto store = [&](int b, int s, int p) {
         uint8_t * base = smem + b * STAGE;
 #pragma unroll
         for (int it = 0; it < 4; it++) {
@@ -135,8 +138,8 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
             const int k = s * PV_KS + 4 * kq;
             const uint32_t off = (r >> 3) * PV_SBO + kq * PV_LBO + (r & 7) * 16;
             const bool rl = r < nq;
-            const float a0 = a_entry(ra[it].x, it, rl && k + 0 < C), a1 = a_entry(ra[it].y, it, rl && k + 1 < C);
-            const float a2 = a_entry(ra[it].z, it, rl && k + 2 < C), a3 = a_entry(ra[it].w, it, rl && k + 3 < C);
+            const float a0 = a_entry(ra[p][it].x, it, rl && k + 0 < C), a1 = a_entry(ra[p][it].y, it, rl && k + 1 < C);
+            const float a2 = a_entry(ra[p][it].z, it, rl && k + 2 < C), a3 = a_entry(ra[p][it].w, it, rl && k + 3 < C);
             float4 hi, lo;
             tf32_split(a0, hi.x, lo.x);
             tf32_split(a1, hi.y, lo.y);
@@ -151,23 +154,29 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
             const int n = idx % DV, kq = idx / DV;
             const uint32_t off = (n >> 3) * PV_SBO + kq * PV_LBO + (n & 7) * 16;
             float4 hi, lo;
-            tf32_split(rb[pb][0], hi.x, lo.x);
-            tf32_split(rb[pb][1], hi.y, lo.y);
-            tf32_split(rb[pb][2], hi.z, lo.z);
-            tf32_split(rb[pb][3], hi.w, lo.w);
+            tf32_split(rb[p][pb][0], hi.x, lo.x);
+            tf32_split(rb[p][pb][1], hi.y, lo.y);
+            tf32_split(rb[p][pb][2], hi.z, lo.z);
+            tf32_split(rb[p][pb][3], hi.w, lo.w);
             *reinterpret_cast<float4 *>(base + 2 * A_BYTES + off) = hi;
             *reinterpret_cast<float4 *>(base + 2 * A_BYTES + B_BYTES + off) = lo;
         }
     };
 
-    load(0);
+    load(0, 0);
+    if (nst > 1) load(1, 1);
     int s = 0, err = 0;
     for (; s < nst; s++) {
-        const int b = s & 1;
+        const int b = s & 1;                      // stage buffer = register set
         bool ok = true;
         if (s >= 2) ok = mbar_wait(&mbar[b], (uint32_t)(((s - 2) >> 1) & 1), PV_POLLS);
-        store(b, s);
-        if (s + 1 < nst) load(s + 1);
+        if (b == 0) {
+            store(0, s, 0);
+            if (s + 2 < nst) load(s + 2, 0);
+        } else {
+            store(1, s, 1);
+            if (s + 2 < nst) load(s + 2, 1);
+        }
         fence_smem_to_async();
         if (__syncthreads_or(!ok)) {          // every thread takes the same decision
             err = 1;
