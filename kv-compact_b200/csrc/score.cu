@@ -496,7 +496,7 @@ __global__ void __launch_bounds__(RI_THREADS, MINB) k_row_importance(const kvc_u
                 if (P.score_method == 0) { if (w > acc[c]) acc[c] = w; }
                 else if (P.score_method == 1) acc[c] = __fadd_rn(acc[c], __fmul_rn(w, w));
                 else acc[c] = __fadd_rn(acc[c], w);
-                if (w > mx[c]) mx[c] = w;
+                if (P.use_sensitivity && w > mx[c]) mx[c] = w;     // read only by sensitivity weighting
             }
         }
 #pragma unroll
@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(RI_THREADS, MINB) k_row_importance(const kvc_u
         if (P.score_method == 1) a = sqrtf(__fmul_rn(a, inv_m));
         else if (P.score_method == 2) a = __fmul_rn(a, inv_m);
         imp[j] = a;
-        cmax[j] = mx[c];
+        if (P.use_sensitivity) cmax[j] = mx[c];
     }
 }
 
