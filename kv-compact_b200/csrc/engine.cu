@@ -789,15 +789,18 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
                 kvc_stage_timer tm(ctx, KVC_ST_REFINE, 1, s);
                 if ((e = kvc_launch_refine(du, nu, P, F, I, ctx->d_outs, s))) return e;
             }
-            {
-                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s);     // raw S[:, sel], gathered from S
-                if ((e = kvc_launch_gather_x(du, nu, max_nq, P, F, I, s))) return e;
-            }
-            if (!p.skip_beta) {
-                kvc_stage_timer tm(ctx, KVC_ST_BETA, 2, s);
-                if ((e = kvc_launch_beta(du, nu, max_nq, max_t, P, F, I, G, ctx->d_outs, s))) return e;
-            }
-            {
+            if (p.skip_beta) {
+                kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s);     // X = softmax(S[:, sel]), one pass
+                if ((e = kvc_launch_gather_softmax_x(du, nu, max_nq, P, F, I, s))) return e;
+            } else {
+                {
+                    kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s); // raw S[:, sel], gathered from S
+                    if ((e = kvc_launch_gather_x(du, nu, max_nq, P, F, I, s))) return e;
+                }
+                {
+                    kvc_stage_timer tm(ctx, KVC_ST_BETA, 2, s);
+                    if ((e = kvc_launch_beta(du, nu, max_nq, max_t, P, F, I, G, ctx->d_outs, s))) return e;
+                }
                 kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s);     // X = softmax(S[:, sel] + beta)
                 if ((e = kvc_launch_softmax_x(du, nu, max_nq, P, F, ctx->d_outs, s))) return e;
             }

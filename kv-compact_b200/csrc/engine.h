@@ -234,6 +234,9 @@ int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, int max
 // X block of the refit: the raw scores of the kept keys, S[:, sel].
 int kvc_launch_gather_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P, float * fs,
                         const int * is, cudaStream_t st);
+// X = softmax(S[:, sel]) in one pass (no beta).
+int kvc_launch_gather_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
+                                float * fs, const int * is, cudaStream_t st);
 // Y = A V per (unit, head). from_scores: the S region holds raw scores and A
 // is formed from them and the row statistics (the engine); else it holds A.
 int kvc_launch_pv(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,

@@ -651,6 +651,58 @@ __global__ void __launch_bounds__(256) k_softmax_x(const kvc_unit * __restrict__
     (void)beta_all;
 }
 
+// X = softmax(S[:, sel]) without a bias (skip_beta): the gather of
+// k_gather_x and the row softmax of k_softmax_x in one pass, one warp per
+// row (the raw row block is never written to memory and read back). Adding a
+// zero beta changes no exponential, so X is bit for bit that of the two
+// kernels.
+__global__ void __launch_bounds__(256) k_gather_softmax_x(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                          float * __restrict__ fs, const int * __restrict__ is) {
+    const kvc_unit u = units[blockIdx.z];
+    if (!u.active) return;
+    const int h = blockIdx.y, nq = u.nq, t = u.t, C = u.C;
+    const int * sel = is + u.sel_off;
+    const float * S = fs + u.s_off + (long long)h * nq * C;
+    float * X = fs + u.x_off + (long long)h * nq * t;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int q = blockIdx.x * 8 + warp; q < nq; q += gridDim.x * 8) {
+        const float * src = S + (long long)q * C;
+        float * row = X + (long long)q * t;
+        float m = -INFINITY;
+        bool first = true;
+        for (int j = lane; j < t; j += 32) {
+            const float v = src[sel[j]];
+            row[j] = v;
+            if (first || v > m) { m = v; first = false; }
+        }
+        for (int o = 16; o; o >>= 1) { float v = __shfl_xor_sync(0xffffffffu, m, o); if (v > m) m = v; }
+        float sm = 0.0f;
+        for (int j = lane; j < t; j += 32) {
+            const float e = expf(__fsub_rn(row[j], m));
+            row[j] = e;
+            sm = __fadd_rn(sm, e);
+        }
+        for (int o = 16; o; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+        const float inv = __fdiv_rn(1.0f, __fadd_rn(sm, 1e-12f));
+        for (int j = lane; j < t; j += 32) row[j] = __fmul_rn(row[j], inv);
+        if (lane == 0 && u.xs_off > 0) {     // kept for the chunk-merged quality metrics
+            float * xs = fs + u.xs_off + (long long)h * 2 * nq;
+            xs[q] = m;
+            xs[nq + q] = sm;
+        }
+    }
+    (void)P;
+}
+
+int kvc_launch_gather_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
+                                float * fs, const int * is, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    const int gx = (max_nq + 7) / 8 < 16 ? (max_nq + 7) / 8 : 16;
+    k_gather_softmax_x<<<dim3(gx, P.H, n_units), 256, 0, st>>>(d_units, P, fs, is);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
 int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_cols,
                      const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st,
                      bool rows_aligned) {
