@@ -35,6 +35,47 @@ constexpr int FN = 128;   // max unknowns of the shared-memory path (k_lsq_facto
 }
 
 enum { DG_GRAM = 0, DG_RHS = 1, DG_OUT = 2 };
+
+// In-place inverse of a 4x4 block by its adjugate (cofactor expansion over
+// the 2x2 minors of the top and bottom row pairs) divided by the
+// determinant. Returns false, leaving `a` unchanged, unless the block is
+// positive definite by Sylvester's criterion (leading minors > 0) with a
+// finite determinant.
+__device__ __forceinline__ bool inverse4_spd(double (&a)[4][4]) {
+    const double s0 = a[0][0] * a[1][1] - a[1][0] * a[0][1], s1 = a[0][0] * a[1][2] - a[1][0] * a[0][2];
+    const double s2 = a[0][0] * a[1][3] - a[1][0] * a[0][3], s3 = a[0][1] * a[1][2] - a[1][1] * a[0][2];
+    const double s4 = a[0][1] * a[1][3] - a[1][1] * a[0][3], s5 = a[0][2] * a[1][3] - a[1][2] * a[0][3];
+    const double c5 = a[2][2] * a[3][3] - a[3][2] * a[2][3], c4 = a[2][1] * a[3][3] - a[3][1] * a[2][3];
+    const double c3 = a[2][1] * a[3][2] - a[3][1] * a[2][2], c2 = a[2][0] * a[3][3] - a[3][0] * a[2][3];
+    const double c1 = a[2][0] * a[3][2] - a[3][0] * a[2][2], c0 = a[2][0] * a[3][1] - a[3][0] * a[2][1];
+    const double det = s0 * c5 - s1 * c4 + s2 * c3 + s3 * c2 - s4 * c1 + s5 * c0;
+    const double m3 = a[0][0] * (a[1][1] * a[2][2] - a[1][2] * a[2][1]) - a[0][1] * (a[1][0] * a[2][2] - a[1][2] * a[2][0]) +
+                      a[0][2] * (a[1][0] * a[2][1] - a[1][1] * a[2][0]);
+    if (!(a[0][0] > 0.0 && s0 > 0.0 && m3 > 0.0 && det > 0.0 && isfinite(det))) return false;
+    const double id = 1.0 / det;
+    double b[4][4];
+    b[0][0] = (a[1][1] * c5 - a[1][2] * c4 + a[1][3] * c3) * id;
+    b[0][1] = (-a[0][1] * c5 + a[0][2] * c4 - a[0][3] * c3) * id;
+    b[0][2] = (a[3][1] * s5 - a[3][2] * s4 + a[3][3] * s3) * id;
+    b[0][3] = (-a[2][1] * s5 + a[2][2] * s4 - a[2][3] * s3) * id;
+    b[1][0] = (-a[1][0] * c5 + a[1][2] * c2 - a[1][3] * c1) * id;
+    b[1][1] = (a[0][0] * c5 - a[0][2] * c2 + a[0][3] * c1) * id;
+    b[1][2] = (-a[3][0] * s5 + a[3][2] * s2 - a[3][3] * s1) * id;
+    b[1][3] = (a[2][0] * s5 - a[2][2] * s2 + a[2][3] * s1) * id;
+    b[2][0] = (a[1][0] * c4 - a[1][1] * c2 + a[1][3] * c0) * id;
+    b[2][1] = (-a[0][0] * c4 + a[0][1] * c2 - a[0][3] * c0) * id;
+    b[2][2] = (a[3][0] * s4 - a[3][1] * s2 + a[3][3] * s0) * id;
+    b[2][3] = (-a[2][0] * s4 + a[2][1] * s2 - a[2][3] * s0) * id;
+    b[3][0] = (-a[1][0] * c3 + a[1][1] * c1 - a[1][2] * c0) * id;
+    b[3][1] = (a[0][0] * c3 - a[0][1] * c1 + a[0][2] * c0) * id;
+    b[3][2] = (-a[3][0] * s3 + a[3][1] * s1 - a[3][2] * s0) * id;
+    b[3][3] = (a[2][0] * s3 - a[2][1] * s1 + a[2][2] * s0) * id;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) a[i][j] = b[i][j];
+    return true;
+}
 constexpr int DT = 64, DK = 16, DLD = 72;   // CTA tile, k slab, shared row stride (doubles)
 
 // D (8x8) += A (8x4) B (4x8) on the fp64 tensor cores (warp-wide). Lane l
@@ -551,13 +592,17 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
         const int prt = (k >> 3) & 3, pr0 = k & 7;
         // ---- A1: P^-1 and the new pivot rows of G (warps 0-3); multipliers; old pivot rows of R
         if (tid < 128) {
-            // in-place Gauss-Jordan inversion of the pivot block; a skipped
+            // inverse of the pivot block: the adjugate over the determinant
+            // (one division, a short dependency chain) when the block is
+            // positive definite, which every pivot block of G + ridge I is;
+            // otherwise in-place Gauss-Jordan inversion, where a skipped
             // (non-positive) pivot leaves its row and column to be zeroed
             double T[4][4];
 #pragma unroll
             for (int q = 0; q < 4; q++)
 #pragma unroll
                 for (int c = 0; c < 4; c++) T[q][c] = G[(k + q) * GLD + k + c];
+            if (!inverse4_spd(T)) {
             bool skip[4];
 #pragma unroll
             for (int q = 0; q < 4; q++) {
@@ -582,6 +627,7 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
                 if (skip[q])
 #pragma unroll
                     for (int c = 0; c < 4; c++) T[q][c] = T[c][q] = 0.0;
+            }
             if (tid == 0)
 #pragma unroll
                 for (int q = 0; q < 16; q++) Ts[q] = T[q >> 2][q & 3];
