@@ -55,7 +55,7 @@ int scores(const float * Q, const float * K, float ** out, int nq, int T, int H,
     u.s_off = (long long)(dS - dQ);
     if (put_unit(ctx, u)) return -1;
     kvc_params_dev P = seam_params(H, dk, dk, scale);
-    if (kvc_launch_score(ctx->d_units, 1, nq, T, P, dQ, nullptr, 0, st)) return -1;
+    if (kvc_launch_score(ctx->d_units, 1, nq, T, P, dQ, 0, st)) return -1;
     ctx->launches += 1;
     for (int h = 0; h < H; h++)
         if (cudaMemcpyAsync(out[h], dS + (size_t)h * nq * T, (size_t)nq * T * 4, cudaMemcpyDeviceToHost, st) !=

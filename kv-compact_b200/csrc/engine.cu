@@ -756,7 +756,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         int e;
         {
             kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1, s);
-            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, I, 2, s, rows_aligned))) return e;
+            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, 2, s, rows_aligned))) return e;
         }
         if (P.use_omp) {                             // needs the raw scores: before the softmax
             kvc_stage_timer tm(ctx, KVC_ST_SELECT, 1, s);
@@ -873,7 +873,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         int e;
         {
             kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1, s);
-            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, I, 2, s, rows_aligned))) return e;
+            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, 2, s, rows_aligned))) return e;
         }
         {
             kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1, s);

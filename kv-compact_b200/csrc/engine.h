@@ -220,8 +220,10 @@ int kvc_engine_metrics(kvc_ctx * ctx, const kvc_layer_job & job, int H, int dk, 
 // rows_aligned: every K / Q row the units read starts on a 16-byte boundary
 // (H*d_k and d_k multiples of 4, 16-byte aligned bases) — enables the
 // asynchronous-copy variant.
+// S = Q K^T / sqrt(d_k) of every (unit, head); mode 2 also writes the row
+// maxima of each key tile (for the one-pass importance kernel).
 int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_cols,
-                     const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st,
+                     const kvc_params_dev & P, float * fs, int mode, cudaStream_t st,
                      bool rows_aligned = false);
 // Key tile of the scoring kernel kvc_launch_score picks (the granularity of
 // its mode-2 row maxima).

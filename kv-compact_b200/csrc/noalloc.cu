@@ -93,7 +93,7 @@ extern "C" KVC_EXPORT int kv_compact_cuda_score_all_heads_noalloc(const float * 
     P.dk = d_k;
     P.dv = d_k;
     P.isd = scale;
-    if (kvc_launch_score(g_unit[dev], 1, n_q, T, P, base, nullptr, 0, st) != KVC_OK) return -1;
+    if (kvc_launch_score(g_unit[dev], 1, n_q, T, P, base, 0, st) != KVC_OK) return -1;
     for (int h = 0; h < H; h++)
         if (cudaMemcpyAsync(scores_out[h], dS + (size_t)h * n_q * T, (size_t)n_q * T * 4, cudaMemcpyDeviceToHost,
                             st) != cudaSuccess)

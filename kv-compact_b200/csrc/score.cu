@@ -10,8 +10,8 @@
 //   order with explicitly rounded multiply and add: S is bit-identical to the
 //   reference's. The kernel is a 128x128 (or 64x256) tile SIMT GEMM whose
 //   inner loop runs over d in order for 64 independent accumulators per thread.
-//   The kernel can also score only the kept keys (mode 1, S[:, sel]); the
-//   engine gathers those from S instead (k_gather_x).
+//   The refit's S[:, sel] is gathered from S afterwards (k_gather_x,
+//   k_gather_softmax_x), bit for bit these scores.
 //
 // Stage 2, k_softmax_importance: row softmax statistics with max shift and
 //   1/(sum + 1e-12) (math.h:201-248), kept for the beta fit and the metrics;
@@ -79,8 +79,8 @@ __device__ __forceinline__ void load_rows(float (*dst)[NR + 4], const float * co
 
 }  // namespace
 
-// Epilogue of both scoring kernels: S = acc * (1/sqrt(d_k)) into the S block
-// (modes 0, 2) or the X block (mode 1); mode 2 also writes, per row and CTA
+// Epilogue of both scoring kernels: S = acc * (1/sqrt(d_k)) into the S block;
+// mode 2 also writes, per row and CTA
 // key tile, the maximum of the row's scores in the tile (exact: a maximum
 // does not depend on order), from which the importance kernel takes the row
 // maxima without a pass over S. Rows of a tile are shared by the NTX = TK/8
@@ -91,7 +91,7 @@ __device__ __forceinline__ void store_scores(const kvc_unit & u, const kvc_param
                                              int tx, int h) {
     constexpr int NTX = TK / 8;
     const int ld = ncols;
-    float * out = fs + (mode != 1 ? u.s_off + (long long)h * u.nq * u.C : u.x_off + (long long)h * u.nq * u.t);
+    float * out = fs + u.s_off + (long long)h * u.nq * u.C;
     const bool vst = (ld & 3) == 0 && ((((uintptr_t)out) & 15) == 0);
     const int ntile = (u.C + 127) / 128;
     float * pm = fs + u.pm_off + (long long)h * u.nq * ntile;
@@ -128,7 +128,6 @@ __device__ __forceinline__ void store_scores(const kvc_unit & u, const kvc_param
 
 // mode 0: all C keys of the chunk -> S block (ld C); mode 2: the same plus
 // the row maxima of each key tile (store_scores)
-// mode 1: the t selected keys     -> X block (ld t), X later softmaxed in place
 // CTA tile TQ queries x TK keys (TQ*TK = 16384), 256 threads, 8x8 outputs per
 // thread: rows 4ty+{0..3} and TQ/2+4ty+{0..3}, columns 4tx+{0..3} and
 // TK/2+4tx+{0..3}, so both operand reads per d are two conflict-free
@@ -136,18 +135,17 @@ __device__ __forceinline__ void store_scores(const kvc_unit & u, const kvc_param
 // updated in d order: acc = fl(acc + fl(q*k)).
 template <int TQ>
 __global__ void __launch_bounds__(ST, 2) k_score(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                                 float * __restrict__ fs, const int * __restrict__ is, int mode) {
+                                                 float * __restrict__ fs, int mode) {
     constexpr int TK = 16384 / TQ;
     constexpr int NTX = TK / 8;               // threads along keys
     const kvc_unit u = units[blockIdx.z];
     if (!u.active) return;
     const int h = blockIdx.y;
-    const int ncols = mode != 1 ? u.C : u.t;
+    const int ncols = u.C;
     const int tq = (u.nq + TQ - 1) / TQ, tk = (ncols + TK - 1) / TK;
     if ((int)blockIdx.x >= tq * tk) return;
     const int q0 = (blockIdx.x / tk) * TQ, j0 = (blockIdx.x % tk) * TK;
     const int ek = P.H * P.dk, dk = P.dk;
-    const int * sel = is + u.sel_off;
 
     __shared__ __align__(16) float Qs[SK][TQ + 4];
     __shared__ __align__(16) float Ks[SK][TK + 4];
@@ -161,7 +159,7 @@ __global__ void __launch_bounds__(ST, 2) k_score(const kvc_unit * __restrict__ u
         } else {
             const int j = j0 + i - TQ;
             if (j < ncols) {
-                const int key = mode != 1 ? j : sel[j];
+                const int key = j;
                 kp[i - TQ] = u.K + (long long)key * ek + (long long)h * dk;
             } else {
                 kp[i - TQ] = nullptr;
@@ -236,18 +234,16 @@ size_t kvc_score_async_smem() {
 }
 
 __global__ void __launch_bounds__(ST, 2) k_score_async(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                                       float * __restrict__ fs, const int * __restrict__ is,
-                                                       int mode) {
+                                                       float * __restrict__ fs, int mode) {
     constexpr int TQ = 128, TK = 128, NTX = TK / 8;
     const kvc_unit u = units[blockIdx.z];
     if (!u.active) return;
     const int h = blockIdx.y;
-    const int ncols = mode != 1 ? u.C : u.t;
+    const int ncols = u.C;
     const int tq = (u.nq + TQ - 1) / TQ, tk = (ncols + TK - 1) / TK;
     if ((int)blockIdx.x >= tq * tk) return;
     const int q0 = (blockIdx.x / tk) * TQ, j0 = (blockIdx.x % tk) * TK;
     const int ek = P.H * P.dk, dk = P.dk;
-    const int * sel = is + u.sel_off;
 
     extern __shared__ __align__(16) float dsm[];
     float * Sq = dsm;                                   // [2][TQ][AS_LD] staged Q rows
@@ -263,7 +259,7 @@ __global__ void __launch_bounds__(ST, 2) k_score_async(const kvc_unit * __restri
     } else {
         const int j = j0 + tid - TQ;
         if (j < ncols) {
-            const int key = mode != 1 ? j : sel[j];
+            const int key = j;
             kp[tid - TQ] = u.K + (long long)key * ek + (long long)h * dk;
         } else {
             kp[tid - TQ] = nullptr;
@@ -704,20 +700,20 @@ int kvc_launch_gather_softmax_x(const kvc_unit * d_units, int n_units, int max_n
 }
 
 int kvc_launch_score(const kvc_unit * d_units, int n_units, int max_nq, int max_cols,
-                     const kvc_params_dev & P, float * fs, const int * is, int mode, cudaStream_t st,
+                     const kvc_params_dev & P, float * fs, int mode, cudaStream_t st,
                      bool rows_aligned) {
     if (n_units <= 0) return KVC_OK;
     if (max_nq > 64 && rows_aligned) {
         const int tiles = ((max_nq + 127) / 128) * ((max_cols + 127) / 128);
         const size_t sm = kvc_score_async_smem();
         KVC_CUDA(cudaFuncSetAttribute(k_score_async, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        k_score_async<<<dim3(tiles, P.H, n_units), ST, sm, st>>>(d_units, P, fs, is, mode);
+        k_score_async<<<dim3(tiles, P.H, n_units), ST, sm, st>>>(d_units, P, fs, mode);
     } else if (max_nq > 64) {
         const int tiles = ((max_nq + 127) / 128) * ((max_cols + 127) / 128);
-        k_score<128><<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs, is, mode);
+        k_score<128><<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs, mode);
     } else {
         const int tiles = ((max_nq + 63) / 64) * ((max_cols + 255) / 256);
-        k_score<64><<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs, is, mode);
+        k_score<64><<<dim3(tiles, P.H, n_units), ST, 0, st>>>(d_units, P, fs, mode);
     }
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
