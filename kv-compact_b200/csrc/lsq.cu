@@ -569,9 +569,22 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int fr = lane >> 2, fq = lane & 3;     // MMA fragment row / k index of this lane
     const int wr = warp >> 2, wc = warp & 3;     // this warp's quarter-block of R
-    for (int e = tid; e < n8 * n8; e += 512) {
-        const int i = e / n8, j = e - i * n8;
-        G[i * GLD + j] = (i < n && j < n) ? Gg[(long long)i * n + j] : (i == j ? 1.0 : 0.0);
+    if (n == n8 && (n & 1) == 0 && ((((uintptr_t)Gg) & 15) == 0)) {
+        // rows of G straight into shared memory, 16 bytes per asynchronous
+        // copy, all in flight at once (one CTA per SM: nothing else hides
+        // this load); the copies complete before the first barrier
+        const int per_row = n >> 1;
+        for (int e = tid; e < n * per_row; e += 512) {
+            const int i = e / per_row, c = (e - i * per_row) * 2;
+            const uint32_t sa = (uint32_t)__cvta_generic_to_shared(G + i * GLD + c);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(sa), "l"(Gg + (long long)i * n + c) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    } else {
+        for (int e = tid; e < n8 * n8; e += 512) {
+            const int i = e / n8, j = e - i * n8;
+            G[i * GLD + j] = (i < n && j < n) ? Gg[(long long)i * n + j] : (i == j ? 1.0 : 0.0);
+        }
     }
     double acc[4][4][2];
 #pragma unroll
@@ -585,6 +598,7 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
                 if (row < n && col < dv) x = dual ? (double)Y[(long long)row * dv + col] : Zg[(long long)row * dv + col];
                 acc[rt][ct][v] = x;
             }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
 
     for (int k = 0; k < n8; k += 4) {
