@@ -686,33 +686,38 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
                 for (int q = 0; q < 4; q++) G[(k + q) * GLD + j] = PR[q * PLD + j];
         }
         __syncthreads();
-        // ---- B: rank-4 updates (pivot rows have zero multipliers)
-        if (8 * warp < n8) {                     // G: row tile `warp`, column tiles from jt0, two at a time
-            const double am = -M[(8 * warp + fr) * 4 + fq];
-            const int nct = n8 >> 3;
-            for (int ct0 = jt0; ct0 < nct; ct0 += 2) {
-                const int ct1 = min(ct0 + 1, nct - 1);
-                double2 * cp0 = reinterpret_cast<double2 *>(G + (8 * warp + fr) * GLD + 8 * ct0 + 2 * fq);
-                double2 * cp1 = reinterpret_cast<double2 *>(G + (8 * warp + fr) * GLD + 8 * ct1 + 2 * fq);
-                const double b0 = PR[fq * PLD + 8 * ct0 + fr], b1 = PR[fq * PLD + 8 * ct1 + fr];
-                const double2 c0 = *cp0, c1 = *cp1;
-                double cc0[2] = {c0.x, c0.y}, cc1[2] = {c1.x, c1.y};
-                dmma(cc0, am, b0);
-                dmma(cc1, am, b1);
-                *cp0 = make_double2(cc0[0], cc0[1]);
-                if (ct0 + 1 < nct) *cp1 = make_double2(cc1[0], cc1[1]);
-            }
-        }
-        {                                        // R: this warp's 4x4 tiles
+        // ---- B: rank-4 updates (pivot rows have zero multipliers). The 16
+        // independent MMAs of this warp's R tiles are interleaved, two at a
+        // time, with the load -> MMA -> store chains of its G tiles (row
+        // tile `warp`, column tiles from jt0, two at a time), so the tensor
+        // pipe works on R while a G chain waits.
+        {
             double am[4], bb[4];
 #pragma unroll
             for (int rt = 0; rt < 4; rt++) am[rt] = -M[(32 * wr + 8 * rt + fr) * 4 + fq];
 #pragma unroll
             for (int ct = 0; ct < 4; ct++) bb[ct] = RR[fq * PLD + 32 * wc + 8 * ct + fr];
+            const bool grow = 8 * warp < n8;
+            const double amg = grow ? -M[(8 * warp + fr) * 4 + fq] : 0.0;
+            const int nct = n8 >> 3;
 #pragma unroll
-            for (int rt = 0; rt < 4; rt++)
-#pragma unroll
-                for (int ct = 0; ct < 4; ct++) dmma(acc[rt][ct], am[rt], bb[ct]);
+            for (int it = 0; it < 8; it++) {
+                const int ct0 = jt0 + 2 * it;
+                if (grow && ct0 < nct) {
+                    const int ct1 = min(ct0 + 1, nct - 1);
+                    double2 * cp0 = reinterpret_cast<double2 *>(G + (8 * warp + fr) * GLD + 8 * ct0 + 2 * fq);
+                    double2 * cp1 = reinterpret_cast<double2 *>(G + (8 * warp + fr) * GLD + 8 * ct1 + 2 * fq);
+                    const double b0 = PR[fq * PLD + 8 * ct0 + fr], b1 = PR[fq * PLD + 8 * ct1 + fr];
+                    const double2 c0 = *cp0, c1 = *cp1;
+                    double cc0[2] = {c0.x, c0.y}, cc1[2] = {c1.x, c1.y};
+                    dmma(cc0, amg, b0);
+                    dmma(cc1, amg, b1);
+                    *cp0 = make_double2(cc0[0], cc0[1]);
+                    if (ct0 + 1 < nct) *cp1 = make_double2(cc1[0], cc1[1]);
+                }
+                dmma(acc[(2 * it) >> 2][(2 * it) & 3], am[(2 * it) >> 2], bb[(2 * it) & 3]);
+                dmma(acc[(2 * it + 1) >> 2][(2 * it + 1) & 3], am[(2 * it + 1) >> 2], bb[(2 * it + 1) & 3]);
+            }
             if (wr == (k >> 5) && fr >= pr0 && fr < pr0 + 4) {
 #pragma unroll
                 for (int rt = 0; rt < 4; rt++)
