@@ -39,26 +39,26 @@ template <int DV>
 constexpr uint32_t pv_tmem_cols() { return DV <= 32 ? 32 : (DV <= 64 ? 64 : (DV <= 128 ? 128 : 256)); }
 }  // namespace
 
-template <int DV>
-__global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                               float * __restrict__ fs, int from_scores) {
+// One (unit, head) tile. FULL: every query row exists (n_q = 128), every
+// stage holds 16 keys and the score rows are 16-byte aligned, so the loads
+// and conversions run without per-element bounds predicates (measured on a
+// cfg4 batch: 2.67 ms against 3.49 ms with the predicates).
+template <int DV, bool FULL>
+__device__ __forceinline__ void pv_tile(const kvc_unit & u, const int h, const kvc_params_dev & P,
+                                        float * __restrict__ fs, const int from_scores, uint8_t * smem,
+                                        uint64_t * mbar, uint32_t * tmem_slot_p) {
     using namespace kvc_tc;
     constexpr int NPB = DV / 32;                       // (row, k-quad) pairs of V per thread and stage
     constexpr uint32_t A_BYTES = (PV_M / 8) * PV_SBO;  // one A tile (hi or lo)
     constexpr uint32_t B_BYTES = (DV / 8) * PV_SBO;    // one B tile
     constexpr uint32_t STAGE = pv_stage_bytes<DV>();
     constexpr uint32_t NCOLS = pv_tmem_cols<DV>();
-    const kvc_unit u = units[blockIdx.x];
-    const int h = blockIdx.y;
     const int ev = P.H * DV, nq = u.nq, C = u.C;
     const float * A = fs + u.s_off + (long long)h * nq * C;     // A, or raw scores A is formed from
     const float * rmax = fs + u.row_off + (long long)h * 2 * nq;
     const float * V = u.V + (long long)h * DV;
     float * Y = fs + u.y_off + (long long)h * nq * DV;
-
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t mbar[2];
-    __shared__ uint32_t tmem_slot;
+    uint32_t & tmem_slot = *tmem_slot_p;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (warp == 0) tmem_alloc(&tmem_slot, NCOLS);
@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
     // near 1e-6, like the 3xTF32 products); else the given weights; zero
     // outside the tile
     auto a_entry = [&](float sv, int it, bool live) {
-        if (!live) return 0.0f;
+        if (!FULL && !live) return 0.0f;
         return from_scores ? __fmul_rn(__expf(__fsub_rn(sv, am[it])), ainv[it]) : sv;
     };
     // two register sets: the stages s+1 and s+2 are in flight while stage s
@@ -107,7 +107,9 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
             const int r = ((idx >> 5) << 3) | (idx & 7), kq = (idx >> 3) & 3;
             const int k = k0 + 4 * kq;
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (r < nq) {
+            if (FULL) {
+                v = *reinterpret_cast<const float4 *>(A + (long long)r * C + k);
+            } else if (r < nq) {
                 const float * p = A + (long long)r * C + k;
                 if (avec && k + 4 <= C) {
                     v = *reinterpret_cast<const float4 *>(p);
@@ -126,7 +128,7 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
             const int n = idx % DV, kq = idx / DV;
             const int k = k0 + 4 * kq;
 #pragma unroll
-            for (int e = 0; e < 4; e++) rb[p][pb][e] = (k + e < C) ? V[(long long)(k + e) * ev + n] : 0.0f;
+            for (int e = 0; e < 4; e++) rb[p][pb][e] = (FULL || k + e < C) ? V[(long long)(k + e) * ev + n] : 0.0f;
         }
     };
     auto store = [&](int b, int s, int p) {
@@ -223,6 +225,20 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
     fence_before_sync();
     __syncthreads();
     if (warp == 0) tmem_free(tmem, NCOLS);
+}
+
+template <int DV>
+__global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                               float * __restrict__ fs, int from_scores) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t mbar[2];
+    __shared__ uint32_t tmem_slot;
+    const kvc_unit u = units[blockIdx.x];
+    const int h = blockIdx.y;
+    const float * A = fs + u.s_off + (long long)h * u.nq * u.C;
+    const bool full = u.nq == PV_M && (u.C % PV_KS) == 0 && ((((uintptr_t)A) & 15) == 0);
+    if (full) pv_tile<DV, true>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+    else pv_tile<DV, false>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
 }
 
 // Whether k_pv_tc handles this shape (else the SIMT k_pv does).

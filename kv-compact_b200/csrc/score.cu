@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(256) k_softmax_importance(const kvc_unit * __r
     }
 }
 
-// Single pass over S for chunks of at most RI_THREADS * RI_CPT keys and
+// Single pass over S for chunks of at most RI_THREADS * RI_MAX_CPT keys and
 // SMI_ROWS queries, with the row maxima from the scoring epilogue (mode 2):
 // the CTA walks the rows in blocks of RI_RB, each thread holding its
 // columns' scores of the block (the next block already loading) and turning
@@ -420,9 +420,11 @@ __global__ void __launch_bounds__(256) k_softmax_importance(const kvc_unit * __r
 // S is read once from memory and exp evaluated once per entry. Measured on
 // a cfg4 step: one row per block and 4 CTAs per SM 1.86 ms; 2 rows, 3 CTAs
 // 2.02; 2 rows, 4 CTAs 2.19; 4 rows, 2 CTAs 2.27; 1 row, 6 CTAs 2.15.
-constexpr int RI_THREADS = 256, RI_CPT = 8;
+// RI_CPT columns per thread, the smallest instantiation that covers the
+// chunk (a 1,280-key chunk takes 5: no thread evaluates dead columns).
+constexpr int RI_THREADS = 256, RI_MAX_CPT = 8;
 
-template <int RI_RB, int MINB>
+template <int RI_RB, int MINB, int RI_CPT>
 __global__ void __launch_bounds__(RI_THREADS, MINB) k_row_importance(const kvc_unit * __restrict__ units,
                                                                   kvc_params_dev P, float * __restrict__ fs,
                                                                   int tile_keys) {
@@ -736,8 +738,13 @@ int kvc_score_tile_keys(int max_nq, bool rows_aligned) {
 int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, int max_nq, int max_C, int tile_keys,
                                   const kvc_params_dev & P, float * fs, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
-    if (tile_keys > 0 && max_C <= RI_THREADS * RI_CPT && max_nq <= SMI_ROWS) {
-        k_row_importance<1, 4><<<dim3(P.H, n_units), RI_THREADS, 0, st>>>(d_units, P, fs, tile_keys);
+    if (tile_keys > 0 && max_C <= RI_THREADS * RI_MAX_CPT && max_nq <= SMI_ROWS) {
+        const dim3 grid(P.H, n_units);
+        const int cpt = (max_C + RI_THREADS - 1) / RI_THREADS;
+        if (cpt <= 2) k_row_importance<1, 4, 2><<<grid, RI_THREADS, 0, st>>>(d_units, P, fs, tile_keys);
+        else if (cpt <= 4) k_row_importance<1, 4, 4><<<grid, RI_THREADS, 0, st>>>(d_units, P, fs, tile_keys);
+        else if (cpt <= 5) k_row_importance<1, 4, 5><<<grid, RI_THREADS, 0, st>>>(d_units, P, fs, tile_keys);
+        else k_row_importance<1, 4, 8><<<grid, RI_THREADS, 0, st>>>(d_units, P, fs, tile_keys);
         KVC_CUDA(cudaGetLastError());
         return KVC_OK;
     }
