@@ -129,13 +129,16 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
         float * dK = F + (size_t)i * (nk + nv);
         float * dV = dK + nk;
         {
-            kvc_stage_timer tm(ctx, KVC_ST_DECODE, 2);
+            kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1);
             if ((rc = kvc_launch_decode((const uint8_t *)L[l].K, m->k_row_bytes, m->k_type, dK, T, ek, st))) return rc;
-            if ((rc = kvc_launch_decode((const uint8_t *)L[l].V, m->v_row_bytes, m->v_type, dV, T, ev, st))) return rc;
         }
         kvc_layer_job & J = jobs[i];
         J.K = dK;
-        J.V = dV;
+        J.V = dV;                  // decoded by the engine unless it reads V in its block format
+        J.Vq = (const uint8_t *)L[l].V;
+        J.v_row_bytes = m->v_row_bytes;
+        J.v_type = m->v_type;
+        J.v_decoded = false;
         if (plans[i].top_cheap) {
             float * q = io_p;
             io_p += (((size_t)plans[i].nq_top * ek) + 31) & ~31ULL;

@@ -497,7 +497,43 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         if (jobs[l].io) {
             if (n_jobs > 1) return KVC_ERR_SHAPE;   // host-resident inputs: single-job calls only
             io = jobs[l].io;
+            jobs[l].v_decoded = io->v.type < 0;     // fp32 rows land in V as they are
         }
+    // V stays in its block format when every job has it in one format and
+    // the tensor-core refit-target kernel takes every unit: that kernel
+    // decodes the values it reads, and no fp32 copy of V is written (the
+    // direct quality metrics decode V on their own when they run).
+    // KVC_DECODE_V=1 decodes V first instead.
+    {
+        int max_nq_all = 1, ty = -1;
+        size_t rb = 0;
+        bool ok = !shared && getenv("KVC_DECODE_V") == nullptr;
+        for (int l = 0; l < n_jobs && ok; l++) {
+            for (const kvc_plan_unit & pu : jobs[l].plan->units) max_nq_all = std::max(max_nq_all, pu.nq);
+            const bool streamed = jobs[l].io != nullptr;
+            const int t_l = streamed ? jobs[l].io->v.type : jobs[l].v_type;
+            const size_t rb_l = streamed ? jobs[l].io->v.row_bytes : jobs[l].v_row_bytes;
+            const bool src = streamed ? jobs[l].io->v.stage != nullptr : jobs[l].Vq != nullptr;
+            ok = src && (t_l == 8 || t_l == 2 || t_l == 3) && (l == 0 || (t_l == ty && rb_l == rb));
+            ty = t_l;
+            rb = rb_l;
+        }
+        ok = ok && kvc_pv_tc_ok(max_nq_all, dv);
+        P.v_type = ok ? ty : -1;
+        P.v_rb = ok ? (long long)rb : 0;
+    }
+    const bool v_blocks = P.v_type >= 0;
+    if (io && !v_blocks) jobs[0].v_decoded = true;  // arrive() decodes every group's rows
+    for (int l = 0; l < n_jobs && !v_blocks; l++) {
+        kvc_layer_job & J = jobs[l];
+        if (J.io || J.v_decoded) continue;
+        if (!J.Vq || !J.V) return KVC_ERR_NULL;
+        kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1);
+        int rcd;
+        if ((rcd = kvc_launch_decode(J.Vq, J.v_row_bytes, J.v_type, const_cast<float *>(J.V), J.plan->T, H * dv, st)))
+            return rcd;
+        J.v_decoded = true;
+    }
     // a streamed job is cut into at most io->max_groups groups of consecutive
     // units whose sizes shrink by io->size_ratio from one to the next (each
     // at least one unit); group_end[g] is one past the last unit of group g
@@ -612,7 +648,10 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             kvc_unit u;
             memset(&u, 0, sizeof(u));
             u.K = J.K + (long long)pu.start * ek;
-            u.V = J.V + (long long)pu.start * ev;
+            if (v_blocks)
+                u.Vq = (J.io ? J.io->v.stage : J.Vq) + (long long)pu.start * P.v_rb;
+            else
+                u.V = J.V + (long long)pu.start * ev;
             u.Q = J.Q;
             u.C = pu.C; u.t = pu.t; u.prefix = pu.prefix; u.nq = pu.nq; u.qmode = pu.qmode;
             u.layer = all[pos].l;
@@ -743,7 +782,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     auto arrive = [&](cudaEvent_t e, const kvc_stream_io::input & in, const float * dst, int ncols, int r0,
                       int r1, cudaStream_t s) -> int {
         KVC_CUDA(cudaStreamWaitEvent(s, e, 0));
-        if (in.type < 0) return KVC_OK;
+        if (in.type < 0 || (v_blocks && &in == &io->v)) return KVC_OK;     // used as they are
         kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1, s);
         return kvc_launch_decode(in.stage + (size_t)r0 * in.row_bytes, in.row_bytes, in.type,
                                  const_cast<float *>(dst) + (size_t)r0 * ncols, r1 - r0, ncols, s);
@@ -908,6 +947,15 @@ int kvc_engine_metrics_launch(kvc_ctx * ctx, const kvc_layer_job & job, int H, i
     kvc_stage_timer tm(ctx, KVC_ST_METRICS, job.out.mpart ? 1 : 4);
     if (job.out.mpart)              // merge the per-chunk records of the last run
         return kvc_launch_metric_merge(job.out.mpart, job.out.n_chunks, H, pl.nq_top, dv, d_res, ctx->stream);
+    if (!job.v_decoded) {           // the run read V in its block format: decode it for the direct metrics
+        const bool streamed = job.io != nullptr;
+        const uint8_t * src = streamed ? job.io->v.stage : job.Vq;
+        if (!src || !job.V) return KVC_ERR_NULL;
+        if ((rc = kvc_launch_decode(src, streamed ? job.io->v.row_bytes : job.v_row_bytes,
+                                    streamed ? job.io->v.type : job.v_type, const_cast<float *>(job.V), pl.T,
+                                    H * dv, ctx->stream)))
+            return rc;
+    }
     const size_t nf = kvc_metric_scratch_floats(H, pl.nq_top, pl.T, t, dv);
     void * a4;
     if ((rc = kvc_arena(ctx, 4, nf * 4, &a4))) return rc;

@@ -75,7 +75,11 @@ struct kvc_stream_io {
 // Device-side job for one layer: fp32 caches resident on the device.
 struct kvc_layer_job {
     const float * K = nullptr;      // [T x H*dk]
-    const float * V = nullptr;      // [T x H*dv]
+    const float * V = nullptr;      // [T x H*dv] (holds the decoded rows once v_decoded)
+    const uint8_t * Vq = nullptr;   // or V's rows in their block format [T x v_row_bytes] (device)
+    size_t v_row_bytes = 0;
+    int v_type = -1;
+    bool v_decoded = true;          // false: V is only in Vq (or the io stage) so far
     const float * Q = nullptr;      // [nq_top x H*dk] top-level queries
     const float * rkv_w = nullptr;  // [T] device R-KV weights or null
     const kvc_plan * plan = nullptr;

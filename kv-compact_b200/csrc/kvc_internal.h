@@ -55,6 +55,7 @@ struct kvc_unit {
     const float * K;      // first row of the chunk, row stride ek = H*d_k
     const float * V;      // first row of the chunk, row stride ev = H*d_v
     const float * Q;      // first reference-query row (qmode 0), row stride ek
+    const uint8_t * Vq;   // or null: first V row in its block format (kvc_params_dev::v_type, v_rb), V unused
     int C;                // tokens in the chunk
     int t;                // keys kept
     int prefix;           // positions 0..prefix-1 always kept (prefix <= t)
@@ -104,6 +105,8 @@ struct kvc_params_dev {
     int use_omp;
     int omp_k_choice;
     int omp_refit_interval;
+    int v_type;           // block format of the units' Vq rows (8 Q8_0, 2 Q4_0, 3 Q4_1)
+    long long v_rb;       // bytes per Vq row
 };
 
 // f32 arithmetic that is never contracted into FMA, on host and device.

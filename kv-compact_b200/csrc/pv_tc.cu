@@ -24,6 +24,8 @@
 #include "engine.h"
 #include "tc_sm100.h"
 
+#include <cuda_fp16.h>
+
 namespace {
 constexpr int PV_M = 128;                    // tile rows (queries)
 constexpr int PV_KS = 16;                    // keys per stage
@@ -39,11 +41,34 @@ template <int DV>
 constexpr uint32_t pv_tmem_cols() { return DV <= 32 ? 32 : (DV <= 64 ? 64 : (DV <= 128 ? 128 : 256)); }
 }  // namespace
 
+// Value n of row `row` of a V matrix kept in its block format (VT: 8 Q8_0,
+// 2 Q4_0, 3 Q4_1; head h's values start at block h * DV / 32), with the
+// arithmetic of the codec's decode (separately rounded multiply and add):
+// the same fp32 value a decoded V row holds.
+template <int VT, int DV>
+__device__ __forceinline__ float vq_value(const uint8_t * __restrict__ row, int h, int n) {
+    constexpr int BB = VT == 8 ? 34 : (VT == 2 ? 18 : 20);
+    const uint8_t * blk = row + (h * (DV / 32) + (n >> 5)) * BB;
+    const int i = n & 31;
+    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(blk)));
+    if (VT == 8) return __fmul_rn(d, (float)(int8_t)blk[2 + i]);
+    if (VT == 2) {
+        const uint8_t q = blk[2 + (i >> 1)];
+        return __fmul_rn(d, __fsub_rn((float)((i & 1) ? q >> 4 : q & 0xF), 8.0f));
+    }
+    const float m = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(blk + 2)));
+    const uint8_t q = blk[4 + (i >> 1)];
+    return __fadd_rn(__fmul_rn(d, (float)((i & 1) ? q >> 4 : q & 0xF)), m);
+}
+
 // One (unit, head) tile. FULL: every query row exists (n_q = 128), every
 // stage holds 16 keys and the score rows are 16-byte aligned, so the loads
 // and conversions run without per-element bounds predicates (measured on a
-// cfg4 batch: 2.67 ms against 3.49 ms with the predicates).
-template <int DV, bool FULL>
+// cfg4 batch: 2.67 ms against 3.49 ms with the predicates). VT: 0 when V is
+// an fp32 matrix (u.V), else the block format of u.Vq's rows, decoded here
+// (no fp32 copy of V is written or read: on the cfg4 batch 2.92 ms, against
+// 2.66 ms plus about 1.3 ms for decoding V first).
+template <int DV, bool FULL, int VT>
 __device__ __forceinline__ void pv_tile(const kvc_unit & u, const int h, const kvc_params_dev & P,
                                         float * __restrict__ fs, const int from_scores, uint8_t * smem,
                                         uint64_t * mbar, uint32_t * tmem_slot_p) {
@@ -56,7 +81,7 @@ __device__ __forceinline__ void pv_tile(const kvc_unit & u, const int h, const k
     const int ev = P.H * DV, nq = u.nq, C = u.C;
     const float * A = fs + u.s_off + (long long)h * nq * C;     // A, or raw scores A is formed from
     const float * rmax = fs + u.row_off + (long long)h * 2 * nq;
-    const float * V = u.V + (long long)h * DV;
+    const float * V = VT ? nullptr : u.V + (long long)h * DV;
     float * Y = fs + u.y_off + (long long)h * nq * DV;
     uint32_t & tmem_slot = *tmem_slot_p;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -128,7 +153,11 @@ __device__ __forceinline__ void pv_tile(const kvc_unit & u, const int h, const k
             const int n = idx % DV, kq = idx / DV;
             const int k = k0 + 4 * kq;
 #pragma unroll
-            for (int e = 0; e < 4; e++) rb[p][pb][e] = (FULL || k + e < C) ? V[(long long)(k + e) * ev + n] : 0.0f;
+            for (int e = 0; e < 4; e++) {
+                if (!FULL && k + e >= C) rb[p][pb][e] = 0.0f;
+                else if (VT) rb[p][pb][e] = vq_value<VT, DV>(u.Vq + (long long)(k + e) * P.v_rb, h, n);
+                else rb[p][pb][e] = V[(long long)(k + e) * ev + n];
+            }
         }
     };
     auto store = [&](int b, int s, int p) {
@@ -237,8 +266,19 @@ __global__ void __launch_bounds__(128) k_pv_tc(const kvc_unit * __restrict__ uni
     const int h = blockIdx.y;
     const float * A = fs + u.s_off + (long long)h * u.nq * u.C;
     const bool full = u.nq == PV_M && (u.C % PV_KS) == 0 && ((((uintptr_t)A) & 15) == 0);
-    if (full) pv_tile<DV, true>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
-    else pv_tile<DV, false>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+    if (!u.Vq) {
+        if (full) pv_tile<DV, true, 0>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+        else pv_tile<DV, false, 0>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+    } else if (P.v_type == 8) {
+        if (full) pv_tile<DV, true, 8>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+        else pv_tile<DV, false, 8>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+    } else if (P.v_type == 2) {
+        if (full) pv_tile<DV, true, 2>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+        else pv_tile<DV, false, 2>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+    } else {
+        if (full) pv_tile<DV, true, 3>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+        else pv_tile<DV, false, 3>(u, h, P, fs, from_scores, smem, mbar, &tmem_slot);
+    }
 }
 
 // Whether k_pv_tc handles this shape (else the SIMT k_pv does).
