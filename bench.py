@@ -224,6 +224,10 @@ def stage_rooflines(stage_times, cfg, n_steps, clocks, peaks):
     fp64_src = "derived: 148 SMs x 64 FP64 lanes x 2 flop x max SM clock (no measured FP64 figure)"
     bpe = {abi.KV_TYPE_Q8_0: 34 / 32, abi.KV_TYPE_Q4_0: 18 / 32, abi.KV_TYPE_Q4_1: 20 / 32, abi.KV_TYPE_F16: 2.0}
     kb, vb = bpe[cfg["ktype"]], bpe[cfg["vtype"]]
+    # a block-format V (Q8_0/Q4_0/Q4_1) is read as it is by the refit-target
+    # kernel and never decoded; an F16 V is decoded to fp32 first
+    v_blocks = cfg["vtype"] != abi.KV_TYPE_F16
+    v_read = vb if v_blocks else 4.0
     # fp64 FMA of the LS refit per (unit, head): n = min(n_q, t_u) unknowns;
     # Gram n(n+1)/2 x k (k = t_u in the dual form, n_q in the primal), Cholesky n^3/3,
     # two triangular solves n^2 d, output t_u x d x n (dual) or right-hand side t_u x d x n_q (primal)
@@ -239,11 +243,12 @@ def stage_rooflines(stage_times, cfg, n_steps, clocks, peaks):
         "score": ("k_score_async", "fp32_issue", "T instr/s", 2.0 * nq * d * T * H * L, fp32_issue,
                   "derived: 148 SMs x 128 FP32 lanes x max SM clock; bit-exact scores need a separate "
                   "rounded multiply and add per term (no FMA, no tensor cores)"),
-        "refit_target": ("k_pv_tc", "hbm", "GB/s", 4.0 * (nq + d) * T * H * L + 4.0 * nq * d * H * L * len(units),
-                         hbm, hbm_src),
+        "refit_target": ("k_pv_tc", "hbm", "GB/s",
+                         (4.0 * nq + v_read * d) * T * H * L + 4.0 * nq * d * H * L * len(units), hbm, hbm_src),
         # the scores are read (once, at least) and nothing of their size is written
-        "softmax_importance": ("k_softmax_importance", "hbm", "GB/s", 4.0 * nq * T * H * L, hbm, hbm_src),
-        "decode": ("k_decode_blocks", "hbm", "GB/s", (T * H * d * (kb + vb) + 8.0 * T * H * d) * L, hbm, hbm_src),
+        "softmax_importance": ("k_row_importance", "hbm", "GB/s", 4.0 * nq * T * H * L, hbm, hbm_src),
+        "decode": ("k_decode_span", "hbm", "GB/s",
+                   (T * H * d * (kb + 4.0) + (0.0 if v_blocks else T * H * d * (vb + 4.0))) * L, hbm, hbm_src),
         "requant": ("k_encode_gather + k_encode_heads", "hbm", "GB/s",
                     (8.0 * t * H * d + t * H * d * (kb + vb)) * L, hbm, hbm_src),
         "ls_gram": ("k_dgemm (Gram)", "fp64", "TFLOP/s", 2.0 * per_lh(gram), fp64, fp64_src),
