@@ -529,15 +529,15 @@ __global__ void __launch_bounds__(256) k_chol_solve(const kvc_unit * __restrict_
 // four unknowns per step, on the fp64 tensor cores. G is symmetric positive
 // definite (Gram matrix + ridge), for which elimination in diagonal order is
 // stable.
-// Step k (unknowns k..k+3): P = G[k..k+3][k..k+3] is inverted by Gauss-Jordan
-// in registers; a pivot that is not positive and finite marks its unknown
+// Step k (unknowns k..k+3): P = G[k..k+3][k..k+3] is inverted in registers
+// (adjugate, or Gauss-Jordan when P is not positive definite); a pivot that is not positive and finite marks its unknown
 // singular (its row of P^-1 is zeroed, so it drops out and ends at zero — the
 // reference skips pivots below 1e-12). The pivot rows become P^-1 (pivot rows
 // of G and R); every other row i loses M[i] x (the new pivot rows), with
 // M[i] = G[i][k..k+3]. That rank-4 update is an m8n8k4 MMA per 8x8 tile: G's
 // tiles right of the block (read from and written back to shared memory) and
 // all of R (held in MMA accumulator fragments, warp w owning a 32x32 quarter-
-// block). Three barriers per step; no triangular dependency chains. n is
+// block). Two barriers per step; no triangular dependency chains. n is
 // padded to a multiple of 8 with identity rows, which stay untouched.
 // After the last step R holds G^-1 R: Z (dual, consumed by the OUT product) or
 // C_v (primal) is written to global memory.
@@ -565,7 +565,6 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
     double * RR = PR + 4 * PLD;                  // [4][PLD] new pivot rows of R
     double * RP = RR + 4 * PLD;                  // [4][PLD] old pivot rows of R
     double * M = RP + 4 * PLD;                   // [FN][4]  multipliers (0 on pivot rows)
-    double * Ts = M + 4 * FN;                    // [16]     P^-1
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int fr = lane >> 2, fq = lane & 3;     // MMA fragment row / k index of this lane
     const int wr = warp >> 2, wc = warp & 3;     // this warp's quarter-block of R
@@ -598,24 +597,44 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
                 if (row < n && col < dv) x = dual ? (double)Y[(long long)row * dv + col] : Zg[(long long)row * dv + col];
                 acc[rt][ct][v] = x;
             }
+    // rows kk .. kk+3 of R (held in this warp's fragments) into RP: the old
+    // pivot rows of R for step kk, taken as soon as the previous step is done
+    auto extract_rp = [&](int kk) {
+        if (kk >= n8 || wr != (kk >> 5)) return;
+        const int prt_ = (kk >> 3) & 3, pr0_ = kk & 7;
+        if (fr < pr0_ || fr >= pr0_ + 4) return;
+#pragma unroll
+        for (int rt = 0; rt < 4; rt++)
+            if (rt == prt_)
+#pragma unroll
+                for (int ct = 0; ct < 4; ct++)
+#pragma unroll
+                    for (int v = 0; v < 2; v++) RP[(fr - pr0_) * PLD + 32 * wc + 8 * ct + 2 * fq + v] = acc[rt][ct][v];
+    };
+    extract_rp(0);
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
 
     for (int k = 0; k < n8; k += 4) {
         const int jt0 = (k + 4) >> 3;            // first column tile of G still needed
         const int prt = (k >> 3) & 3, pr0 = k & 7;
-        // ---- A1: P^-1 and the new pivot rows of G (warps 0-3); multipliers; old pivot rows of R
+        // ---- A (one barrier): warps 0-3 invert the pivot block P and write the
+        // new pivot rows of G (P^-1 G[k..k+3][j], into PR and into G itself) and
+        // of R (P^-1 RP, into RR), one column per thread; warps 4-7 meanwhile
+        // copy the multipliers M. A step costs 4.3k cycles without the overlap
+        // (A 1.7k, of which 0.4k the multipliers; a second barrier 0.4k).
         if (tid < 128) {
-            // inverse of the pivot block: the adjugate over the determinant
-            // (one division, a short dependency chain) when the block is
-            // positive definite, which every pivot block of G + ridge I is;
-            // otherwise in-place Gauss-Jordan inversion, where a skipped
-            // (non-positive) pivot leaves its row and column to be zeroed
             double T[4][4];
 #pragma unroll
             for (int q = 0; q < 4; q++)
 #pragma unroll
                 for (int c = 0; c < 4; c++) T[q][c] = G[(k + q) * GLD + k + c];
+            asm volatile("bar.sync 1, 128;" ::: "memory");   // P read before its columns are rewritten
+            // inverse of the pivot block: the adjugate over the determinant
+            // (one division, a short dependency chain) when the block is
+            // positive definite, which every pivot block of G + ridge I is;
+            // otherwise in-place Gauss-Jordan inversion, where a skipped
+            // (non-positive) pivot leaves its row and column to be zeroed
             if (!inverse4_spd(T)) {
             bool skip[4];
 #pragma unroll
@@ -642,48 +661,29 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
 #pragma unroll
                     for (int c = 0; c < 4; c++) T[q][c] = T[c][q] = 0.0;
             }
-            if (tid == 0)
-#pragma unroll
-                for (int q = 0; q < 16; q++) Ts[q] = T[q >> 2][q & 3];
             const int j = 8 * jt0 + tid;
             if (j < n8) {
                 double g[4];
 #pragma unroll
                 for (int q = 0; q < 4; q++) g[q] = G[(k + q) * GLD + j];
 #pragma unroll
-                for (int q = 0; q < 4; q++)
-                    PR[q * PLD + j] = fma(T[q][0], g[0], fma(T[q][1], g[1], fma(T[q][2], g[2], T[q][3] * g[3])));
+                for (int q = 0; q < 4; q++) {
+                    const double x = fma(T[q][0], g[0], fma(T[q][1], g[1], fma(T[q][2], g[2], T[q][3] * g[3])));
+                    PR[q * PLD + j] = x;
+                    G[(k + q) * GLD + j] = x;
+                }
             }
-        }
-        if (tid < FN) {                          // rows past n8 get zero multipliers too
-            const bool zero = (tid >= k && tid < k + 4) || tid >= n8;
-#pragma unroll
-            for (int q = 0; q < 4; q++) M[tid * 4 + q] = zero ? 0.0 : G[tid * GLD + k + q];
-        }
-        if (wr == (k >> 5) && fr >= pr0 && fr < pr0 + 4) {
-#pragma unroll
-            for (int rt = 0; rt < 4; rt++)
-                if (rt == prt)
-#pragma unroll
-                    for (int ct = 0; ct < 4; ct++)
-#pragma unroll
-                        for (int v = 0; v < 2; v++) RP[(fr - pr0) * PLD + 32 * wc + 8 * ct + 2 * fq + v] = acc[rt][ct][v];
-        }
-        __syncthreads();
-        // ---- A2: new pivot rows of R; pivot rows of G take their new values
-        if (tid < 128) {
-            const int c = tid;
             double rp[4];
 #pragma unroll
-            for (int q = 0; q < 4; q++) rp[q] = RP[q * PLD + c];
+            for (int q = 0; q < 4; q++) rp[q] = RP[q * PLD + tid];
 #pragma unroll
             for (int q = 0; q < 4; q++)
-                RR[q * PLD + c] = fma(Ts[4 * q], rp[0], fma(Ts[4 * q + 1], rp[1], fma(Ts[4 * q + 2], rp[2], Ts[4 * q + 3] * rp[3])));
-        } else if (tid < 256) {
-            const int j = 8 * jt0 + (tid - 128);
-            if (j < n8)
+                RR[q * PLD + tid] = fma(T[q][0], rp[0], fma(T[q][1], rp[1], fma(T[q][2], rp[2], T[q][3] * rp[3])));
+        } else if (tid < 256) {                  // rows past n8 get zero multipliers too
+            const int r = tid - 128;
+            const bool zero = (r >= k && r < k + 4) || r >= n8;
 #pragma unroll
-                for (int q = 0; q < 4; q++) G[(k + q) * GLD + j] = PR[q * PLD + j];
+            for (int q = 0; q < 4; q++) M[r * 4 + q] = zero ? 0.0 : G[r * GLD + k + q];
         }
         __syncthreads();
         // ---- B: rank-4 updates (pivot rows have zero multipliers). The 16
@@ -728,6 +728,7 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
                             for (int v = 0; v < 2; v++)
                                 acc[rt][ct][v] = RR[(fr - pr0) * PLD + 32 * wc + 8 * ct + 2 * fq + v];
             }
+            extract_rp(k + 4);
         }
         __syncthreads();
     }
