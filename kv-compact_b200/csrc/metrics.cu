@@ -269,9 +269,13 @@ __host__ __device__ inline int metric_rec(int dv) { return 4 + 2 * dv; }
 // grid (units, min(H,4)): per-chunk terms of the first min(n_q,32) queries.
 // Runs for every unit of a layer that has a record buffer, active or not
 // (a unit that stopped refining keeps the X and C_v of its last solve).
-__global__ void __launch_bounds__(256) k_metric_partial(const kvc_unit * __restrict__ units, kvc_params_dev P,
+// HI: d_v > 128, each thread also owns columns 128 + 4 cg .. +3 (otherwise
+// those accumulators would only ever add products of zero).
+template <bool HI>
+__global__ void __launch_bounds__(256, HI ? 2 : 4) k_metric_partial(const kvc_unit * __restrict__ units, kvc_params_dev P,
                                                         const float * __restrict__ fs,
                                                         const kvc_layer_out * __restrict__ outs) {
+    constexpr int NC = HI ? 8 : 4;
     const kvc_unit u = units[blockIdx.x];
     const kvc_layer_out lo = outs[u.layer];
     if (lo.mpart == nullptr || u.qmode != 0) return;
@@ -299,12 +303,11 @@ __global__ void __launch_bounds__(256) k_metric_partial(const kvc_unit * __restr
     __shared__ __align__(16) float Ws[PK][MQ];
     __shared__ __align__(16) float Vs[PK][KVC_MAX_D];
     const int qg = tid >> 5, cg = tid & 31;
-    const bool hi = dv > 128;
-    float acc[4][8];
+    float acc[4][NC];
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int c = 0; c < 8; c++) acc[i][c] = 0.0f;
+        for (int c = 0; c < NC; c++) acc[i][c] = 0.0f;
     for (int j0 = 0; j0 < t; j0 += PK) {
         for (int e = tid; e < MQ * PK; e += 256) {
             const int qq = e / PK, jj = e % PK;
@@ -316,26 +319,29 @@ __global__ void __launch_bounds__(256) k_metric_partial(const kvc_unit * __restr
         }
         __syncthreads();
         const int jn = min(PK, t - j0);
+#pragma unroll 4
         for (int jj = 0; jj < jn; jj++) {
             const float4 w4 = *reinterpret_cast<const float4 *>(&Ws[jj][4 * qg]);
             const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-            float vv[8];
+            float vv[NC];
             if (4 * cg < dv) {
                 const float4 v4 = *reinterpret_cast<const float4 *>(&Vs[jj][4 * cg]);
                 vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
             } else {
                 vv[0] = vv[1] = vv[2] = vv[3] = 0.0f;
             }
-            if (hi && 128 + 4 * cg < dv) {
-                const float4 v4 = *reinterpret_cast<const float4 *>(&Vs[jj][128 + 4 * cg]);
-                vv[4] = v4.x; vv[5] = v4.y; vv[6] = v4.z; vv[7] = v4.w;
-            } else {
-                vv[4] = vv[5] = vv[6] = vv[7] = 0.0f;
+            if (HI) {
+                if (128 + 4 * cg < dv) {
+                    const float4 v4 = *reinterpret_cast<const float4 *>(&Vs[jj][128 + 4 * cg]);
+                    vv[NC - 4] = v4.x; vv[NC - 3] = v4.y; vv[NC - 2] = v4.z; vv[NC - 1] = v4.w;
+                } else {
+                    vv[NC - 4] = vv[NC - 3] = vv[NC - 2] = vv[NC - 1] = 0.0f;
+                }
             }
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int c = 0; c < 8; c++) acc[i][c] = fmaf(wv[i], vv[c], acc[i][c]);
+                for (int c = 0; c < NC; c++) acc[i][c] = fmaf(wv[i], vv[c], acc[i][c]);
         }
         __syncthreads();
     }
@@ -344,9 +350,9 @@ __global__ void __launch_bounds__(256) k_metric_partial(const kvc_unit * __restr
         const int q = 4 * qg + i;
         if (q >= mq) continue;
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
+        for (int c = 0; c < NC; c++) {
             const int col = (c < 4) ? 4 * cg + c : 128 + 4 * cg + (c - 4);
-            if (col < dv && (c < 4 || hi)) out[(long long)q * rec + 4 + dv + col] = acc[i][c];
+            if (col < dv) out[(long long)q * rec + 4 + dv + col] = acc[i][c];
         }
     }
 }
@@ -472,7 +478,8 @@ int kvc_launch_metric_partial(const kvc_unit * d_units, int n_units, const kvc_p
                               const kvc_layer_out * d_outs, cudaStream_t st) {
     const int mh = P.H < 4 ? P.H : 4;
     if (n_units <= 0 || mh <= 0) return KVC_OK;
-    k_metric_partial<<<dim3(n_units, mh), 256, 0, st>>>(d_units, P, fs, d_outs);
+    if (P.dv > 128) k_metric_partial<true><<<dim3(n_units, mh), 256, 0, st>>>(d_units, P, fs, d_outs);
+    else k_metric_partial<false><<<dim3(n_units, mh), 256, 0, st>>>(d_units, P, fs, d_outs);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
