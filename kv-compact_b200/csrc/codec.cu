@@ -491,9 +491,141 @@ __global__ void k_encode_heads(const float * __restrict__ cv, int H, int t, int 
     }
 }
 
+// Encode 8 values (part `part` of 4) of a block held by the 4 lanes of an
+// aligned lane group, into the block's bytes at o: the arithmetic of
+// encode_quad / encode_block, with the block statistics combined by
+// shuffles inside the group (maxima and minima do not depend on order).
+template <int TYPE>
+__device__ __forceinline__ void encode_oct(const float (&x)[8], float x0, int part, uint8_t * o) {
+    auto st = [](uint8_t * q, uint16_t v) { *reinterpret_cast<uint16_t *>(q) = v; };
+    if (TYPE == 8 || TYPE == 2) {
+        float amax = 0.0f;                               // NaN never wins: skipped as in encode_block
+#pragma unroll
+        for (int i = 0; i < 8; i++) { const float a = fabsf(x[i]); if (a > amax) amax = a; }
+#pragma unroll
+        for (int off = 2; off; off >>= 1) {
+            const float b = __shfl_xor_sync(0xffffffffu, amax, off, 4);
+            if (b > amax) amax = b;
+        }
+        const float lim = (TYPE == 8) ? 127.0f : 7.0f;
+        const float d = kvc_div(amax, lim);
+        if (part == 0) st(o, kvc_f2h_trunc(d));
+        const float id = (d != 0.0f) ? kvc_div(lim, amax) : 0.0f;
+        if (TYPE == 8) {
+            uint8_t q[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) q[i] = (uint8_t)(int8_t)kvc_roundf(kvc_clamp(kvc_mul(x[i], id), -128.0f, 127.0f));
+#pragma unroll
+            for (int i = 0; i < 4; i++) st(o + 2 + 8 * part + 2 * i, (uint16_t)(q[2 * i] | (q[2 * i + 1] << 8)));
+        } else {
+            uint8_t q[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) q[i] = (uint8_t)kvc_clamp(kvc_roundf(kvc_add(kvc_mul(x[i], id), 8.0f)), 0.0f, 15.0f);
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+                st(o + 2 + 4 * part + 2 * i,
+                   (uint16_t)((q[4 * i] | (q[4 * i + 1] << 4)) | ((q[4 * i + 2] | (q[4 * i + 3] << 4)) << 8)));
+        }
+    } else {
+        float lo = x0, hi = x0;                          // a NaN first value poisons both, as in encode_block
+#pragma unroll
+        for (int i = 0; i < 8; i++) { if (x[i] < lo) lo = x[i]; if (x[i] > hi) hi = x[i]; }
+#pragma unroll
+        for (int off = 2; off; off >>= 1) {
+            const float a = __shfl_xor_sync(0xffffffffu, lo, off, 4);
+            const float b = __shfl_xor_sync(0xffffffffu, hi, off, 4);
+            if (a < lo) lo = a;
+            if (b > hi) hi = b;
+        }
+        const float rng = kvc_sub(hi, lo);
+        const float d = kvc_div(rng, 15.0f);
+        if (part == 0) {
+            st(o, kvc_f2h_trunc(d));
+            st(o + 2, kvc_f2h_trunc(lo));
+        }
+        const float id = (d != 0.0f) ? kvc_div(15.0f, rng) : 0.0f;
+        uint8_t q[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) q[i] = (uint8_t)kvc_clamp(kvc_roundf(kvc_mul(kvc_sub(x[i], lo), id)), 0.0f, 15.0f);
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+            st(o + 4 + 4 * part + 2 * i,
+               (uint16_t)((q[4 * i] | (q[4 * i + 1] << 4)) | ((q[4 * i + 2] | (q[4 * i + 3] << 4)) << 8)));
+    }
+}
+
+// Packed block rows out (row bytes = blocks x block bytes, 16-byte aligned
+// destination): a CTA encodes 64 blocks at a time, 4 threads a block and 8
+// values a thread read as two float4, into shared memory, and writes the
+// span's bytes out as 16-byte stores (one thread per 16 bytes) instead of the
+// 2-byte stores of k_encode_gather / k_encode_heads. HEADS = 0: block b of
+// output row r holds values 32b.. of source row idx[r] (or r); HEADS = 1:
+// output row r is row r of every head of cv ([H][t][dv], d_v a multiple of
+// 32, so a block lies within one head).
+template <int TYPE, int HEADS>
+__global__ void __launch_bounds__(256) k_encode_span(const float * __restrict__ src, size_t stride,
+                                                     const int * __restrict__ idx, int t, int dv, int nb,
+                                                     long long nblocks, uint8_t * __restrict__ dst) {
+    constexpr int BB = TYPE == 8 ? 34 : (TYPE == 2 ? 18 : 20);
+    constexpr int SPB = 64, SB = SPB * BB, NV = SB / 16;
+    static_assert(SB % 16 == 0, "a span is whole 16-byte pieces");
+    __shared__ __align__(16) uint8_t sb[SB + BB + 14];   // + a block that lanes past the end write, never read
+    const int blk = threadIdx.x >> 2, part = threadIdx.x & 3;
+    for (long long sp = blockIdx.x; sp * SPB < nblocks; sp += gridDim.x) {
+        const long long b0 = sp * SPB;
+        const int nbk = (int)min((long long)SPB, nblocks - b0);
+        const bool live = blk < nbk;
+        float x[8];
+        if (live) {
+            const long long gb = b0 + blk, r = gb / nb;
+            const int b = (int)(gb - r * nb);
+            const float * p;
+            if (HEADS) {
+                const int e0 = b * QK, h = e0 / dv;
+                p = src + ((long long)h * t + r) * dv + (e0 - h * dv) + 8 * part;
+            } else {
+                p = src + (idx ? (long long)idx[r] : r) * (long long)stride + (long long)b * QK + 8 * part;
+            }
+            const float4 u0 = *reinterpret_cast<const float4 *>(p), u1 = *reinterpret_cast<const float4 *>(p + 4);
+            x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
+            x[4] = u1.x; x[5] = u1.y; x[6] = u1.z; x[7] = u1.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) x[i] = 0.0f;
+        }
+        const float x0 = __shfl_sync(0xffffffffu, x[0], threadIdx.x & 28);   // the block's first value
+        encode_oct<TYPE>(x, x0, part, sb + (live ? blk * BB : SB));
+        __syncthreads();
+        const int nbytes = nbk * BB;
+        uint8_t * d = dst + b0 * BB;
+        if (threadIdx.x < NV) {
+            const int o = threadIdx.x * 16;
+            if (o + 16 <= nbytes) *reinterpret_cast<uint4 *>(d + o) = *reinterpret_cast<const uint4 *>(sb + o);
+            else
+                for (int i = o; i < nbytes && i < o + 16; i++) d[i] = sb[i];
+        }
+        __syncthreads();
+    }
+}
+
+template <int HEADS>
+static void launch_encode_span(int type, const float * src, size_t stride, const int * idx, int t, int dv, int nb,
+                               long long nblocks, uint8_t * dst, cudaStream_t st) {
+    const int grid = (int)std::min<long long>((nblocks + 63) / 64, 148LL * 32);
+    if (type == 8) k_encode_span<8, HEADS><<<grid, 256, 0, st>>>(src, stride, idx, t, dv, nb, nblocks, dst);
+    else if (type == 2) k_encode_span<2, HEADS><<<grid, 256, 0, st>>>(src, stride, idx, t, dv, nb, nblocks, dst);
+    else k_encode_span<3, HEADS><<<grid, 256, 0, st>>>(src, stride, idx, t, dv, nb, nblocks, dst);
+}
+
 int kvc_launch_encode_gather(const float * src, size_t stride, const int * idx, int rows, int n,
                              int type, uint8_t * dst, size_t drb, cudaStream_t st) {
     if (rows <= 0) return KVC_OK;
+    if (is_block(type) && n >= QK && n % QK == 0 && drb == (size_t)(n / QK) * (size_t)kvc_block_bytes(type) &&
+        stride % 4 == 0 && (((uintptr_t)src) & 15) == 0 && (((uintptr_t)dst) & 15) == 0) {
+        launch_encode_span<0>(type, src, stride, idx, 0, 0, n / QK, (long long)rows * (n / QK), dst, st);
+        KVC_CUDA(cudaGetLastError());
+        return KVC_OK;
+    }
     long long work = (long long)rows * (is_block(type) ? (n / QK) * 8 : n);
     if (work + (long long)148 * 64 * 256 + 64 < (1LL << 32))   // the last grid-stride step stays below 2^32
         k_encode_gather<uint32_t><<<grid_for(work, 256), 256, 0, st>>>(src, stride, idx, rows, n, type, dst, drb);
@@ -507,6 +639,12 @@ int kvc_launch_encode_gather(const float * src, size_t stride, const int * idx, 
 int kvc_launch_encode_heads(const float * cv, int H, int t, int rows, int dv, int type, uint8_t * dst,
                             size_t drb, cudaStream_t st) {
     if (rows <= 0) return KVC_OK;
+    if (is_block(type) && dv % QK == 0 && drb == (size_t)((H * dv) / QK) * (size_t)kvc_block_bytes(type) &&
+        (((uintptr_t)cv) & 15) == 0 && (((uintptr_t)dst) & 15) == 0) {
+        launch_encode_span<1>(type, cv, 0, nullptr, t, dv, (H * dv) / QK, (long long)rows * ((H * dv) / QK), dst, st);
+        KVC_CUDA(cudaGetLastError());
+        return KVC_OK;
+    }
     long long work = (long long)rows * (is_block(type) ? ((H * dv) / QK) * 8 : H * dv);
     if (work + (long long)148 * 64 * 256 + 64 < (1LL << 32))   // the last grid-stride step stays below 2^32
         k_encode_heads<uint32_t><<<grid_for(work, 256), 256, 0, st>>>(cv, H, t, rows, dv, type, dst, drb);
