@@ -830,7 +830,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             }
             if (p.skip_beta) {
                 kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s);     // X = softmax(S[:, sel]), one pass
-                if ((e = kvc_launch_gather_softmax_x(du, nu, max_nq, P, F, I, s))) return e;
+                if ((e = kvc_launch_gather_softmax_x(du, nu, max_nq, max_t, P, F, I, s))) return e;
             } else {
                 {
                     kvc_stage_timer tm(ctx, KVC_ST_XBUILD, 1, s); // raw S[:, sel], gathered from S

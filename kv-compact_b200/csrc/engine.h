@@ -241,7 +241,7 @@ int kvc_launch_softmax_importance(const kvc_unit * d_units, int n_units, int max
 int kvc_launch_gather_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P, float * fs,
                         const int * is, cudaStream_t st);
 // X = softmax(S[:, sel]) in one pass (no beta).
-int kvc_launch_gather_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
+int kvc_launch_gather_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, int max_t, const kvc_params_dev & P,
                                 float * fs, const int * is, cudaStream_t st);
 // Y = A V per (unit, head). from_scores: the S region holds raw scores and A
 // is formed from them and the row statistics (the engine); else it holds A.

@@ -692,11 +692,64 @@ __global__ void __launch_bounds__(256) k_gather_softmax_x(const kvc_unit * __res
     (void)P;
 }
 
-int kvc_launch_gather_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
+// k_gather_softmax_x with the row in registers (t <= 32 R): each lane
+// gathers its R values of S[q][sel[j]] (j = lane, lane + 32, ...) at once,
+// with sel staged in shared memory for all the CTA's rows, and X is written
+// once. Same order of every operation as k_gather_softmax_x (bit-identical).
+template <int R>
+__global__ void __launch_bounds__(256) k_gather_softmax_x_reg(const kvc_unit * __restrict__ units,
+                                                              float * __restrict__ fs, const int * __restrict__ is) {
+    const kvc_unit u = units[blockIdx.z];
+    if (!u.active) return;
+    const int h = blockIdx.y, nq = u.nq, t = u.t, C = u.C;
+    __shared__ int ssel[32 * R];
+    for (int j = threadIdx.x; j < t; j += 256) ssel[j] = is[u.sel_off + j];
+    __syncthreads();
+    const float * S = fs + u.s_off + (long long)h * nq * C;
+    float * X = fs + u.x_off + (long long)h * nq * t;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int q = blockIdx.x * 8 + warp; q < nq; q += gridDim.x * 8) {
+        const float * src = S + (long long)q * C;
+        float v[R];
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            const int j = lane + 32 * i;
+            v[i] = j < t ? src[ssel[j]] : 0.0f;
+        }
+        float m = -INFINITY;
+        bool first = true;
+#pragma unroll
+        for (int i = 0; i < R; i++)
+            if (lane + 32 * i < t && (first || v[i] > m)) { m = v[i]; first = false; }
+        for (int o = 16; o; o >>= 1) { float w = __shfl_xor_sync(0xffffffffu, m, o); if (w > m) m = w; }
+        float sm = 0.0f;
+#pragma unroll
+        for (int i = 0; i < R; i++)
+            if (lane + 32 * i < t) {
+                v[i] = expf(__fsub_rn(v[i], m));
+                sm = __fadd_rn(sm, v[i]);
+            }
+        for (int o = 16; o; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+        const float inv = __fdiv_rn(1.0f, __fadd_rn(sm, 1e-12f));
+        float * row = X + (long long)q * t;
+#pragma unroll
+        for (int i = 0; i < R; i++)
+            if (lane + 32 * i < t) row[lane + 32 * i] = __fmul_rn(v[i], inv);
+        if (lane == 0 && u.xs_off > 0) {     // kept for the chunk-merged quality metrics
+            float * xs = fs + u.xs_off + (long long)h * 2 * nq;
+            xs[q] = m;
+            xs[nq + q] = sm;
+        }
+    }
+}
+
+int kvc_launch_gather_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, int max_t, const kvc_params_dev & P,
                                 float * fs, const int * is, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
     const int gx = (max_nq + 7) / 8 < 16 ? (max_nq + 7) / 8 : 16;
-    k_gather_softmax_x<<<dim3(gx, P.H, n_units), 256, 0, st>>>(d_units, P, fs, is);
+    if (max_t <= 256) k_gather_softmax_x_reg<8><<<dim3(gx, P.H, n_units), 256, 0, st>>>(d_units, fs, is);
+    else if (max_t <= 512) k_gather_softmax_x_reg<16><<<dim3(gx, P.H, n_units), 256, 0, st>>>(d_units, fs, is);
+    else k_gather_softmax_x<<<dim3(gx, P.H, n_units), 256, 0, st>>>(d_units, P, fs, is);
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
