@@ -168,6 +168,9 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
         if ((rc = kvc_arena(ctx, 9, ((size_t)pair_off[n] * 3 + 64) * 4, &a9))) return rc;
         d_res = (float *)a9;
     }
+    std::vector<const float *> m_parts;
+    std::vector<int> m_chunks;
+    std::vector<float *> m_res;
     for (int i = 0; i < n; i++) {
         const int l = on[i];
         const int t = plans[i].t_total;
@@ -184,7 +187,19 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
                 return rc;
         }
         memset(&R[l].stats, 0, sizeof(R[l].stats));
-        if (want_stats && (rc = kvc_engine_metrics_launch(ctx, jobs[i], H, dk, dv, d_res + (size_t)pair_off[i] * 3)))
+        if (!want_stats) continue;
+        if (jobs[i].out.mpart && plans[i].nq_top == plans[0].nq_top) {   // merged below, all layers at once
+            m_parts.push_back(jobs[i].out.mpart);
+            m_chunks.push_back(jobs[i].out.n_chunks);
+            m_res.push_back(d_res + (size_t)pair_off[i] * 3);
+        } else if ((rc = kvc_engine_metrics_launch(ctx, jobs[i], H, dk, dv, d_res + (size_t)pair_off[i] * 3))) {
+            return rc;
+        }
+    }
+    if (!m_parts.empty()) {
+        kvc_stage_timer tm(ctx, KVC_ST_METRICS, 1);
+        if ((rc = kvc_launch_metric_merge_batch(m_parts.data(), m_chunks.data(), m_res.data(), (int)m_parts.size(), H,
+                                                plans[0].nq_top, dv, st)))
             return rc;
     }
     if ((rc = kvc_wait(ctx))) return rc;

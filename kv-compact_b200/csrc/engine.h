@@ -289,6 +289,9 @@ size_t kvc_metric_partial_floats(int n_chunks, int H, int nq, int dv);
 int kvc_launch_metric_partial(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, const float * fs,
                               const kvc_layer_out * d_outs, cudaStream_t st);
 int kvc_launch_metric_merge(const float * mpart, int n_chunks, int H, int nq, int dv, float * res, cudaStream_t st);
+// The merges of n layers (all with H heads, nq_top queries, d_v) in as few launches as possible.
+int kvc_launch_metric_merge_batch(const float * const * mparts, const int * n_chunks, float * const * res, int n,
+                                  int H, int nq, int dv, cudaStream_t st);
 size_t kvc_omp_floats(int C, int t, int nq, int H);
 int kvc_launch_omp_exp(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, cudaStream_t st);
 int kvc_launch_omp_select(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, int * is,

@@ -364,9 +364,8 @@ __global__ void __launch_bounds__(256, HI ? 2 : 4) k_metric_partial(const kvc_un
 // are recomputed per column).
 constexpr int MERGE_SMEM_CHUNKS = 2048;
 
-__global__ void __launch_bounds__(256) k_metric_merge(const float * __restrict__ mpart, int n_chunks, int mh,
-                                                      int mq, int dv, float * __restrict__ res) {
-    const int pair = blockIdx.x;
+__device__ __forceinline__ void metric_merge_pair(const float * __restrict__ mpart, int n_chunks, int mh, int mq,
+                                                  int dv, float * __restrict__ res, const int pair) {
     const int h = pair / mq, q = pair % mq;
     const int rec = metric_rec(dv);
     const long long cstride = (long long)mh * mq * rec;
@@ -431,6 +430,58 @@ __global__ void __launch_bounds__(256) k_metric_merge(const float * __restrict__
     }
     __syncthreads();
     if (threadIdx.x == 0) metric_triple(oo, co, dv, res + pair * 3);
+}
+
+__global__ void __launch_bounds__(256) k_metric_merge(const float * __restrict__ mpart, int n_chunks, int mh,
+                                                      int mq, int dv, float * __restrict__ res) {
+    metric_merge_pair(mpart, n_chunks, mh, mq, dv, res, blockIdx.x);
+}
+
+// Several layers' merges in one launch (grid.y = layer): the per-layer
+// launches each ran one short wave of min(H,4) x min(n_q,32) CTAs.
+constexpr int MERGE_BATCH = 32;
+struct kvc_merge_batch {
+    const float * mpart[MERGE_BATCH];
+    float * res[MERGE_BATCH];
+    int n_chunks[MERGE_BATCH];
+};
+
+__global__ void __launch_bounds__(256) k_metric_merge_batch(const kvc_merge_batch b, int mh, int mq, int dv) {
+    const int l = blockIdx.y;
+    metric_merge_pair(b.mpart[l], b.n_chunks[l], mh, mq, dv, b.res[l], blockIdx.x);
+}
+
+int kvc_launch_metric_merge(const float * mpart, int n_chunks, int H, int nq, int dv, float * res, cudaStream_t st);
+
+int kvc_launch_metric_merge_batch(const float * const * mparts, const int * n_chunks, float * const * res, int n,
+                                  int H, int nq, int dv, cudaStream_t st) {
+    const int mh = H < 4 ? H : 4, mq = nq < 32 ? nq : 32;
+    if (mh * mq <= 0) return KVC_OK;
+    for (int l = 0; l < n; l++)
+        if (n_chunks[l] > MERGE_SMEM_CHUNKS) {        // uncached weights: one launch per layer
+            for (int i = 0; i < n; i++) {
+                int rc = kvc_launch_metric_merge(mparts[i], n_chunks[i], H, nq, dv, res[i], st);
+                if (rc) return rc;
+            }
+            return KVC_OK;
+        }
+    for (int l0 = 0; l0 < n; l0 += MERGE_BATCH) {
+        kvc_merge_batch b;
+        memset(&b, 0, sizeof(b));
+        const int nl = n - l0 < MERGE_BATCH ? n - l0 : MERGE_BATCH;
+        int max_chunks = 1;
+        for (int i = 0; i < nl; i++) {
+            b.mpart[i] = mparts[l0 + i];
+            b.res[i] = res[l0 + i];
+            b.n_chunks[i] = n_chunks[l0 + i];
+            if (n_chunks[l0 + i] <= 0) return KVC_ERR_SHAPE;
+            if (n_chunks[l0 + i] > max_chunks) max_chunks = n_chunks[l0 + i];
+        }
+        const size_t sm = 2 * (size_t)max_chunks * sizeof(double);     // every layer's weights cached
+        k_metric_merge_batch<<<dim3(mh * mq, nl), 256, sm, st>>>(b, mh, mq, dv);
+        KVC_CUDA(cudaGetLastError());
+    }
+    return KVC_OK;
 }
 
 int kvc_metric_pairs(int H, int nq) { return (H < 4 ? H : 4) * (nq < 32 ? nq : 32); }
