@@ -185,11 +185,12 @@ def run_reference(args, cfg, name):
 # summarised in profiles/main_kernels_cfg4_q8_1layer.md. Traffic grows in
 # proportion to the layers of a launch, so a full-step launch is scaled by 12.
 NCU_TRAFFIC_PER_LAYER_HEAD = {
-    "k_score": (410.2e6 + 363.1e6) / 8,
-    "k_score_async": (410.2e6 + 363.1e6) / 8,
-    "k_pv_tc": (820.0e6 + 33.7e6) / 8,
-    "k_softmax_importance": (816.1e6 + 10.2e6) / 8,
-    "k_lsq_factor": (123.2e6 + 40.4e6) / 8,
+    "k_score": (410.2e6 + 366.6e6) / 8,
+    "k_score_async": (410.2e6 + 366.6e6) / 8,
+    "k_pv_tc": (538.6e6 + 33.5e6) / 8,
+    "k_row_importance": (412.8e6 + 4.7e6) / 8,
+    "k_lsq_factor": (123.3e6 + 41.9e6) / 8,
+    "k_decode_span": (109.7e6 + 352.3e6) / 8,
 }
 
 
