@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Compaction throughput of the kv-compact hot path on B200.
 
-Metric (BASELINE.json): compaction input tokens/s over all filtered layers x
+Metric: compaction input tokens/s over all filtered layers x
 KV heads, 100k context, 5x compression (20% retention). Default workload is
 configuration 4: 48 layers x 8 KV heads x d=128, T=100,000, every 4th layer
 compacted (12 layers), K/V stored Q8_0, SnapKV window W=32 over 32 query
@@ -114,24 +114,42 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_sample(cfg, Kq_h, Vq_h, Q_h, max_seconds=30.0):
-    """Time the reference CPU library (or the oracle port) on one filtered
-    layer; returns (tokens/s of the whole model extrapolated, details)."""
-    T, H, d = cfg["T"], cfg["H"], cfg["d"]
+def host_cores():
+    """Host threads this process may run on."""
+    return len(os.sched_getaffinity(0))
+
+
+def cpu_library():
+    """(bound functions, kind): the reference library built from its sources
+    (oracle/_ref) when present, else the C restatement of its CPU path."""
     if os.path.exists(REF_PATH):
-        fns = abi.bind(ctypes.CDLL(REF_PATH, mode=ctypes.RTLD_LOCAL))
-        kind, cores = "reference", len(os.sched_getaffinity(0))
-        tokens = T
-    else:
-        fns = abi.bind(ctypes.CDLL(ORACLE_PATH, mode=ctypes.RTLD_LOCAL), prefix="oracle_")
-        kind, cores = "port", 1
-        tokens = min(T, 20 * 1280)   # the single-threaded port: a 20-chunk prefix
+        return abi.bind(ctypes.CDLL(REF_PATH, mode=ctypes.RTLD_LOCAL)), "reference"
+    return abi.bind(ctypes.CDLL(ORACLE_PATH, mode=ctypes.RTLD_LOCAL), prefix="oracle_"), "port"
+
+
+def cpu_sample_tokens(cfg, kind, cores):
+    """Tokens of the bounded CPU sample: whole chunks of one filtered layer,
+    two per host thread for the multi-threaded reference (every thread gets the
+    same number of chunks, so the sample is not slowed by an idle tail), a
+    4-chunk prefix for the single-threaded port."""
+    cs = chunk_plan(cfg)[0][0]
+    n = 2 * cores if kind == "reference" else 4
+    return min(cfg["T"], n * cs)
+
+
+def cpu_sample(fns, kind, cores, cfg, Kq_h, Vq_h, Q_h):
+    """Time one kv_compact_quantized call of the reference CPU library (or the
+    oracle port) on the first len(Kq_h) tokens of one filtered layer with
+    `cores` OpenMP threads (params.n_threads set explicitly: under torchrun
+    OMP_NUM_THREADS=1 would otherwise make the reference single-threaded).
+    Returns (tokens/s of the whole model, details, seconds)."""
+    H, d = cfg["H"], cfg["d"]
+    tokens = Kq_h.shape[0]
     krb, vrb = Kq_h.shape[1], Vq_h.shape[1]
-    p = abi.make_params(fns, target_ratio=cfg["ratio"])
+    p = abi.make_params(fns, target_ratio=cfg["ratio"], n_threads=cores if kind == "reference" else 1)
     r = abi.QuantResult()
     t0 = time.perf_counter()
-    rc = fns["kv_compact_quantized"](abi.u8ptr(np.ascontiguousarray(Kq_h[:tokens])),
-                                     abi.u8ptr(np.ascontiguousarray(Vq_h[:tokens])), abi.fptr(Q_h),
+    rc = fns["kv_compact_quantized"](abi.u8ptr(Kq_h), abi.u8ptr(Vq_h), abi.fptr(Q_h),
                                      cfg["ktype"], cfg["vtype"], krb, vrb, tokens, Q_h.shape[0], H, d, d,
                                      ctypes.byref(p), ctypes.byref(r))
     dt = time.perf_counter() - t0
@@ -139,29 +157,40 @@ def cpu_sample(cfg, Kq_h, Vq_h, Q_h, max_seconds=30.0):
     fns["quant_result_free"](ctypes.byref(r))
     n_layers = len(filtered_layers(cfg))
     value = tokens / (n_layers * dt)   # T tokens need n_layers layer-compactions
-    sample = (f"1 of {n_layers} filtered layers, {tokens} tokens x {H} heads, {TYPE_NAME[cfg['ktype']]}, "
-              f"{dt:.2f} s; model throughput = tokens / ({n_layers} x layer time)")
+    n_chunks = -(-tokens // chunk_plan(cfg)[0][0])
+    sample = (f"{tokens} tokens ({n_chunks} chunks) of 1 of {n_layers} filtered layers x {H} heads, "
+              f"{TYPE_NAME[cfg['ktype']]}, {dt:.2f} s on {cores} threads; "
+              f"model throughput = tokens / ({n_layers} x sample time)")
     return value, {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}, dt
 
 
+def reference_inputs(fns, cfg, tokens, seed):
+    """One layer's first `tokens` rows with the workload's distributions,
+    generated on the host (numpy) and quantised by `fns`' own kv_quantize_row."""
+    rng = np.random.default_rng(seed)
+    H, d = cfg["H"], cfg["d"]
+    K = workloads.rope_keys(rng, tokens, H, d)
+    V = rng.standard_normal((tokens, H * d)).astype(np.float32)
+    Q = workloads.snapkv_queries(rng, H, d, cfg["window"], cfg["group"])
+    return (abi.quantize_rows(fns, K, cfg["ktype"]), abi.quantize_rows(fns, V, cfg["vtype"]),
+            np.ascontiguousarray(Q))
+
+
 def run_reference(args, cfg, name):
+    """The reference's own CPU library on the host cores: nothing of this
+    repository's CUDA library is loaded in this process (inputs are generated
+    with numpy and quantised by the reference's kv_quantize_row)."""
     rank, _, _ = kdist.env_ranks()
     if rank != 0:
         return
-    import torch
-    device = "cuda:0" if torch.cuda.is_available() else "cpu"
-    from kvc_b200 import lib
-    fns = lib.load()
-    if device == "cpu":
-        print(json.dumps({"impl": "reference", "unavailable": "data generation needs the CUDA device"}))
-        return
-    Kq, Vq, Q = make_layers(cfg, 1000, device, fns)
-    Kh, Vh, Qh = Kq[0].cpu().numpy(), Vq[0].cpu().numpy(), Q[0].cpu().numpy()
-    del Kq, Vq, Q
-    torch.cuda.empty_cache()
+    cores = host_cores()
+    os.environ["OMP_NUM_THREADS"] = str(cores)     # before the OpenMP runtime loads
+    fns, kind = cpu_library()
+    tokens = cpu_sample_tokens(cfg, kind, cores)
+    Kh, Vh, Qh = reference_inputs(fns, cfg, tokens, 1000)
     times, vals, base = [], [], None
     for i in range(args.warmup + args.steps):
-        v, base, dt = cpu_sample(cfg, Kh, Vh, Qh)
+        v, base, dt = cpu_sample(fns, kind, cores, cfg, Kh, Vh, Qh)
         if i >= args.warmup:
             times.append(dt)
             vals.append(v)
@@ -170,9 +199,11 @@ def run_reference(args, cfg, name):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(times) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic (seeded; cfg2 distributions quantised)",
-        "config": {"workload": workload_desc(name, cfg), "sample": base["sample"]},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded numpy; cfg2 distributions quantised by the reference's kv_quantize_row)",
+        "config": {"workload": workload_desc(name, cfg), "sample": base["sample"],
+                   "threads": cores, "library": os.path.relpath(REF_PATH if kind == "reference" else ORACLE_PATH,
+                                                                REPO)},
         "cpu_baseline": base,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -370,7 +401,11 @@ def run_kvc(args, cfg, name):
     # ---- CPU baseline on the host cores (rank 0, N=1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        _, cpu, _ = cpu_sample(cfg, Kq[0].cpu().numpy(), Vq[0].cpu().numpy(), Q[0].cpu().numpy())
+        cfns, kind = cpu_library()
+        cores = host_cores() if kind == "reference" else 1
+        n = cpu_sample_tokens(cfg, kind, cores)
+        _, cpu, _ = cpu_sample(cfns, kind, cores, cfg, np.ascontiguousarray(Kq[0][:n].cpu().numpy()),
+                               np.ascontiguousarray(Vq[0][:n].cpu().numpy()), Q[0].cpu().numpy())
 
     peaks = {}
     try:

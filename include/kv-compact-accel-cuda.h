@@ -10,7 +10,9 @@
  * CPU-path values bit for bit (sequential fp32 dot products, then the scale).
  *
  * A build of the reference that defines the HIP seam can link against
- * libkvc.so by mapping the names.
+ * libkvc.so by mapping each kv_compact_hip_* name onto the kv_compact_cuda_*
+ * entry point of the same arguments (a macro or a one-line forwarding
+ * function per name).
  */
 #pragma once
 
@@ -48,7 +50,7 @@ void kv_compact_cuda_pool_free(void);
  * the library (held by every GPU that loads it), so it needs
  * n_q*H*d_k + T*H*d_k + H*n_q*T floats (each part rounded up to 64) <=
  * 4,194,304 and returns -13 with a message beyond that; -1 on bad arguments
- * or no sm_100 device. The first call on a device looks up the array's
+ * (d_k > 256 among them) or no sm_100 device. The first call on a device looks up the array's
  * address (make it before any stream capture). Calls share the array: calls
  * from this process are serialised, calls overlapping on the GPU race. */
 int kv_compact_cuda_score_all_heads_noalloc(const float * Q_ref, const float * K_all,

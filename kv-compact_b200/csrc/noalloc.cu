@@ -21,6 +21,8 @@
 // at zero. Calls made from this process are serialised by a mutex; calls that
 // overlap on the GPU from elsewhere (another thread bypassing it, or another
 // stream still reading a previous result) race on the array.
+#include <limits.h>
+
 #include <mutex>
 
 #include "engine.h"
@@ -48,8 +50,12 @@ extern "C" KVC_EXPORT int kv_compact_cuda_score_all_heads_noalloc(const float * 
         cudaGetLastError();
         return -1;
     }
+    // every product in size_t, and the head width bounded before it is used
+    // as an int, so absurd arguments cannot wrap into a size that passes
+    if (d_k > KVC_MAX_D || (size_t)n_head_kv * (size_t)d_k > (size_t)INT_MAX) return -1;
     const int H = n_head_kv, ek = H * d_k;
-    const size_t nQ = up64((size_t)n_q * ek), nK = up64((size_t)T * ek), nS = up64((size_t)H * n_q * T);
+    const size_t nQ = up64((size_t)n_q * (size_t)ek), nK = up64((size_t)T * (size_t)ek);
+    const size_t nS = up64((size_t)H * (size_t)n_q * (size_t)T);
     if (nQ + nK + nS > KVC_NOALLOC_SCRATCH_FLOATS) {
         fprintf(stderr,
                 "[kvc] kv_compact_cuda_score_all_heads_noalloc: n_q=%d T=%d heads=%d d_k=%d needs %zu floats of "
@@ -75,8 +81,16 @@ extern "C" KVC_EXPORT int kv_compact_cuda_score_all_heads_noalloc(const float * 
     float * dK = dQ + nQ;
     float * dS = dK + nK;
     cudaStream_t st = cudaStreamPerThread;
-    if (cudaMemcpyAsync(dQ, Q_ref, (size_t)n_q * ek * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) return -1;
-    if (cudaMemcpyAsync(dK, K_all, (size_t)T * ek * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) return -1;
+    // An error after copies were queued waits for the stream first: the
+    // copies read the caller's host buffers, which the caller may release
+    // as soon as this call returns.
+    auto fail = [st]() {
+        cudaStreamSynchronize(st);
+        cudaGetLastError();
+        return -1;
+    };
+    if (cudaMemcpyAsync(dQ, Q_ref, (size_t)n_q * ek * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) return fail();
+    if (cudaMemcpyAsync(dK, K_all, (size_t)T * ek * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) return fail();
     kvc_unit u;
     memset(&u, 0, sizeof(u));
     u.K = dK;
@@ -86,18 +100,18 @@ extern "C" KVC_EXPORT int kv_compact_cuda_score_all_heads_noalloc(const float * 
     u.nq = n_q;
     u.active = 1;
     u.s_off = (long long)(dS - base);
-    if (cudaMemcpyAsync(g_unit[dev], &u, sizeof(u), cudaMemcpyHostToDevice, st) != cudaSuccess) return -1;
+    if (cudaMemcpyAsync(g_unit[dev], &u, sizeof(u), cudaMemcpyHostToDevice, st) != cudaSuccess) return fail();
     kvc_params_dev P;
     memset(&P, 0, sizeof(P));
     P.H = H;
     P.dk = d_k;
     P.dv = d_k;
     P.isd = scale;
-    if (kvc_launch_score(g_unit[dev], 1, n_q, T, P, base, 0, st) != KVC_OK) return -1;
+    if (kvc_launch_score(g_unit[dev], 1, n_q, T, P, base, 0, st) != KVC_OK) return fail();
     for (int h = 0; h < H; h++)
         if (cudaMemcpyAsync(scores_out[h], dS + (size_t)h * n_q * T, (size_t)n_q * T * 4, cudaMemcpyDeviceToHost,
                             st) != cudaSuccess)
-            return -1;
+            return fail();
     if (cudaStreamSynchronize(st) != cudaSuccess) return -1;
     return 0;
 }

@@ -30,7 +30,9 @@ def _scores(fn, Q, K, nq, T, H, d, scale):
 def test_noalloc_scores_match_allocating_entry_point_twice(kvc):
     lib = kvc["_lib"]
     rng = np.random.default_rng(2024)
-    shapes = [(64, 1000, 4, 128), (37, 777, 3, 48)]     # two calls in a row, different shapes
+    # calls in a row on different shapes; n_q > 64 takes the scoring kernel's
+    # 128-query tile, n_q <= 64 its 64-query tile
+    shapes = [(64, 1000, 4, 128), (37, 777, 3, 48), (128, 1000, 4, 128)]
     for nq, T, H, d in shapes:
         Q = rng.standard_normal((nq, H * d)).astype(np.float32)
         K = rng.standard_normal((T, H * d)).astype(np.float32)
