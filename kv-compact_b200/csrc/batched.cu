@@ -134,6 +134,9 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
         }
         kvc_layer_job & J = jobs[i];
         J.K = dK;
+        J.Kq = (const uint8_t *)L[l].K;     // scored from its block bytes where the format allows
+        J.k_row_bytes = m->k_row_bytes;
+        J.k_type = m->k_type;
         J.V = dV;                  // decoded by the engine unless it reads V in its block format
         J.Vq = (const uint8_t *)L[l].V;
         J.v_row_bytes = m->v_row_bytes;

@@ -197,7 +197,8 @@ int kvc_wait(kvc_ctx * ctx) {
     while ((e = cudaEventQuery(ctx->ev[0])) == cudaErrorNotReady) {
     }
     KVC_CUDA(e);
-    const int te = kvc_tc_take_error(ctx->stream);
+    int te = kvc_tc_take_error(ctx->stream);
+    if (!te) te = kvc_score_tc_take_error(ctx->stream);
     if (te) {
         fprintf(stderr, "[kvc] tensor-core kernel reported error %d (bounded wait ran out)\n", te);
         return KVC_ERR_CUDA;
@@ -523,6 +524,42 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         P.v_rb = ok ? (long long)rb : 0;
     }
     const bool v_blocks = P.v_type >= 0;
+    // Scores on the tensor cores, read from K's stored block bytes
+    // (score_tc.cu), when every job has them on the device in one supported
+    // format; else the bit-exact SIMT kernels over the fp32 K.
+    kvc_score_tc_geom tcg;
+    bool tc_score = !shared;
+    {
+        int max_nq_all = 1;
+        for (int l = 0; l < n_jobs; l++)
+            for (const kvc_plan_unit & pu : jobs[l].plan->units) max_nq_all = std::max(max_nq_all, pu.nq);
+        for (int l = 0; l < n_jobs && tc_score; l++) {
+            const bool streamed = jobs[l].io != nullptr;
+            const uint8_t * kb = streamed ? jobs[l].io->k.stage : jobs[l].Kq;
+            const int kt = streamed ? jobs[l].io->k.type : jobs[l].k_type;
+            const size_t krb = streamed ? jobs[l].io->k.row_bytes : jobs[l].k_row_bytes;
+            kvc_score_tc_geom g;
+            tc_score = kb != nullptr && kvc_score_tc_ok(kt, krb, kb, H, dk, max_nq_all, &g) &&
+                       (l == 0 || (g.k_type == tcg.k_type && g.seg == tcg.seg && g.raww == tcg.raww));
+            if (l == 0) tcg = g;
+        }
+    }
+    void * d_maps = nullptr;
+    if (tc_score) {                               // one TMA map per job (layer): its K rows as bytes x rows
+        const size_t mb = kvc_score_tc_map_bytes();
+        std::vector<uint64_t> maps((size_t)n_jobs * mb / 8);
+        for (int l = 0; l < n_jobs; l++) {
+            const bool streamed = jobs[l].io != nullptr;
+            const uint8_t * kb = streamed ? jobs[l].io->k.stage : jobs[l].Kq;
+            const size_t krb = streamed ? jobs[l].io->k.row_bytes : jobs[l].k_row_bytes;
+            int rcm;
+            if ((rcm = kvc_score_tc_make_map(maps.data() + (size_t)l * mb / 8, kb, krb, jobs[l].plan->T, tcg.raww)))
+                return rcm;
+        }
+        int rcm;
+        if ((rcm = kvc_arena(ctx, 14, (size_t)n_jobs * mb, &d_maps))) return rcm;
+        KVC_CUDA(cudaMemcpyAsync(d_maps, maps.data(), (size_t)n_jobs * mb, cudaMemcpyHostToDevice, st));
+    }
     if (io && !v_blocks) jobs[0].v_decoded = true;  // arrive() decodes every group's rows
     for (int l = 0; l < n_jobs && !v_blocks; l++) {
         kvc_layer_job & J = jobs[l];
@@ -795,17 +832,19 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         int e;
         {
             kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1, s);
-            if ((e = kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, 2, s, rows_aligned))) return e;
+            e = tc_score ? kvc_launch_score_tc(du, nu, P, F, d_maps, tcg, 2, s)
+                         : kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, 2, s, rows_aligned);
+            if (e) return e;
         }
         if (P.use_omp) {                             // needs the raw scores: before the softmax
             kvc_stage_timer tm(ctx, KVC_ST_SELECT, 1, s);
             if ((e = kvc_launch_omp_exp(du, nu, P, F, s))) return e;
         }
         {
+            // the tensor-core scoring leaves each row's maximum over the whole chunk
             kvc_stage_timer tm(ctx, KVC_ST_SOFTMAX, 1, s);
-            if ((e = kvc_launch_softmax_importance(du, nu, bt.max_nq, bt.max_C,
-                                                   kvc_score_tile_keys(bt.max_nq, rows_aligned), P, F, s)))
-                return e;
+            const int tile_keys = tc_score ? bt.max_C : kvc_score_tile_keys(bt.max_nq, rows_aligned);
+            if ((e = kvc_launch_softmax_importance(du, nu, bt.max_nq, bt.max_C, tile_keys, P, F, s))) return e;
         }
         kvc_stage_timer tm(ctx, KVC_ST_SELECT, 2, s);
         if ((e = kvc_launch_aggregate(du, nu, P, F, s))) return e;

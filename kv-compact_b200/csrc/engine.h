@@ -75,6 +75,9 @@ struct kvc_stream_io {
 // Device-side job for one layer: fp32 caches resident on the device.
 struct kvc_layer_job {
     const float * K = nullptr;      // [T x H*dk]
+    const uint8_t * Kq = nullptr;   // or K's rows in their block format [T x k_row_bytes] (device), if kept
+    size_t k_row_bytes = 0;
+    int k_type = -1;
     const float * V = nullptr;      // [T x H*dv] (holds the decoded rows once v_decoded)
     const uint8_t * Vq = nullptr;   // or V's rows in their block format [T x v_row_bytes] (device)
     size_t v_row_bytes = 0;
@@ -251,6 +254,26 @@ bool kvc_pv_tc_ok(int max_nq, int dv);
 int kvc_launch_pv_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, bool from_scores,
                      cudaStream_t st);
 int kvc_tc_take_error(cudaStream_t st);
+
+// Scoring on the tcgen05 tensor cores from K's stored block bytes
+// (score_tc.cu). kvc_score_tc_ok: whether the format, row layout, head
+// dimension and query count take that path (KVC_EXACT_SCORES=1 keeps the
+// bit-exact SIMT kernels); fills the geometry the launch needs.
+struct kvc_score_tc_geom {
+    int k_type = -1;      // 8 Q8_0, 2 Q4_0, 1 F16
+    int seg = 0;          // bytes of one head in a K row
+    int raww = 0;         // TMA box width in bytes
+};
+bool kvc_score_tc_ok(int k_type, size_t k_row_bytes, const void * k_base, int H, int dk, int max_nq,
+                     kvc_score_tc_geom * g);
+size_t kvc_score_tc_map_bytes();
+// Encode the TMA map of one layer's K rows into `map` (kvc_score_tc_map_bytes() bytes, 64-byte aligned).
+int kvc_score_tc_make_map(void * map, const uint8_t * k_base, size_t k_row_bytes, int rows, int raww);
+// S (and, mode 2, each row's maximum in pm slot 0) of every (unit, head);
+// d_maps[layer] = the TMA map of the layer's K rows.
+int kvc_launch_score_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,
+                        const void * d_maps, const kvc_score_tc_geom & g, int mode, cudaStream_t st);
+int kvc_score_tc_take_error(cudaStream_t st);
 int kvc_launch_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
                          float * fs, const kvc_layer_out * d_outs, cudaStream_t st);
 int kvc_launch_aggregate(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,

@@ -111,6 +111,52 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * mbar, uint32_t parity, uint
     return false;
 }
 
+// Instruction descriptor of kind::f16 with f16 operands: fp32 accumulate,
+// A and B both F16 and K-major, M x N tile (A/B format 0 = F16).
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4)                      // D format F32
+         | ((uint32_t)(N >> 3) << 17)
+         | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T in kind::f16, issued by one thread.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+        :: "r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane, without waiting:
+// several loads can be in flight before one tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t * r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Arm the mbarrier for one arrival (this thread's) plus `bytes` of
+// asynchronous-copy transactions.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * mbar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 :: "r"(smem_u32(mbar)), "r"(bytes) : "memory");
+}
+
+// 2-D tiled TMA load of one box of the tensor map at `tmap` (a global-memory
+// CUtensorMap) into shared memory, completing on `mbar`. x is the innermost
+// coordinate (its byte offset must be a multiple of 16), y the row. No
+// multicast: the box lands in this CTA's shared memory only.
+__device__ __forceinline__ void tma_load_2d(void * dst, const void * tmap, int x, int y, uint64_t * mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(mbar)) : "memory");
+}
+
 // Round an fp32 value to the nearest TF32 value (10 explicit mantissa bits,
 // ties away from zero), returned as fp32 with the 13 low bits clear — the
 // tensor core then reads it exactly.

@@ -155,7 +155,7 @@ def test_cfg4_full_layer_matches_reference(kvc, reference, oracle_traced, typ):
 
 
 def abi_name(typ):
-    return {abi.KV_TYPE_Q8_0: "Q8_0", abi.KV_TYPE_Q4_0: "Q4_0"}.get(typ, str(typ))
+    return {abi.KV_TYPE_Q8_0: "Q8_0", abi.KV_TYPE_Q4_0: "Q4_0", abi.KV_TYPE_F16: "F16"}.get(typ, str(typ))
 
 
 def test_reference_api_suite_on_libkvc():
@@ -168,3 +168,39 @@ def test_reference_api_suite_on_libkvc():
     print(f"\n{tail}")
     assert p.returncode == 0, f"rc {p.returncode}\n{tail}\n{p.stderr[-2000:]}"
     assert "All tests passed!" in p.stdout
+
+
+@pytest.mark.parametrize("typ", [abi.KV_TYPE_Q8_0, abi.KV_TYPE_Q4_0, abi.KV_TYPE_F16], ids=["q8_0", "q4_0", "f16"])
+def test_tensor_core_scores_match_exact_mode(kvc, reference, oracle_traced, monkeypatch, typ):
+    """Scores from K's block bytes on the tensor cores (the default) against
+    the bit-exact SIMT scoring (KVC_EXACT_SCORES=1): the exact mode still
+    selects the reference's keys bit for bit, and the tensor-core mode selects
+    them too, except near-ties (< parity.NEAR_TIE_REL relative importance gap)."""
+    T, H, d, nq = 12_800, 8, 128, 128
+    K, V, Q = workloads.small_case(300 + typ, T, nq, H, d, "rope")
+    Kq, Vq = abi.quantize_rows(kvc, K, typ), abi.quantize_rows(kvc, V, typ)
+    pk = dict(target_ratio=0.2)
+    args = (Kq, Vq, Q, typ, typ, Kq.shape[1], Vq.shape[1], T, nq, H, d, d)
+    rc, theirs = abi.run_quantized(reference, *args, abi.make_params(reference, **pk))
+    assert rc == 0
+    rc, tc = abi.run_quantized(kvc, *args, abi.make_params(kvc, **pk))
+    assert rc == 0
+    monkeypatch.setenv("KVC_EXACT_SCORES", "1")
+    rc, exact = abi.run_quantized(kvc, *args, abi.make_params(kvc, **pk))
+    assert rc == 0
+    monkeypatch.delenv("KVC_EXACT_SCORES")
+    np.testing.assert_array_equal(exact["indices"], theirs["indices"])
+    np.testing.assert_array_equal(exact["K_out"], theirs["K_out"])
+    units = parity.plan_units(T, pk)
+    Kf = abi.dequantize_rows(kvc, Kq, typ, H * d)
+    Vf = abi.dequantize_rows(kvc, Vq, typ, H * d)
+    imp = np.zeros(T, np.float32)
+    oracle_traced["_trace"](imp.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), T)
+    rc, _ = abi.run_compact(oracle_traced, Kf, Vf, Q, nq, H, d, d, abi.make_params(oracle_traced, **pk))
+    oracle_traced["_trace"](None, 0)
+    assert rc == 0
+    mism, ties, worst = parity.classify_indices(tc["indices"], theirs["indices"], imp, units)
+    print(f"\n{abi_name(typ)}: tensor-core scoring {mism} index differences ({ties} near-ties) of {tc['t']}; "
+          f"C_v tensor-core vs exact mode rel-L2 {parity.rel_l2(tc['C_v'], exact['C_v']):.2e}")
+    assert mism == ties, f"{mism} index mismatches, {ties} near-ties, worst gap {worst:.3e}"
+    assert tc["stats"]["avg_cosine_sim"] >= parity.COS_RATIO * theirs["stats"]["avg_cosine_sim"] - 1e-6
