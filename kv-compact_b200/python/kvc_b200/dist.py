@@ -1,9 +1,10 @@
 """Multi-process plumbing of the benchmark: one process per GPU.
 
 The compaction path has no exchange step: every (layer, chunk) unit is
-independent, so N ranks each compact their own cache (weak scaling) and the
-only collectives are a barrier before timing and the maximum of the per-rank
-step times afterwards. These helpers hold that logic so it can be exercised on
+independent. N ranks either share one model's units (kvc_b200.shard: a
+partition plus a final gather of the compacted rows to rank 0) or each
+compact their own cache (weak scaling); the other collectives are a barrier
+before timing and the maximum of the per-rank step times afterwards. These helpers hold that logic so it can be exercised on
 CPU with the gloo backend (tests/test_dist_cpu.py) and on GPUs with NCCL
 (bench.py under torchrun).
 """
@@ -44,6 +45,16 @@ def max_over_ranks(value, world, device="cpu"):
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value, world, device="cpu"):
+    """The sum of a per-rank number over all ranks."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
 
 

@@ -1,0 +1,112 @@
+"""Partition of one model across ranks and the merge of the slice results on
+rank 0 (kvc_b200.shard), on CPU: the partition covers every (layer, chunk)
+unit exactly once in order, balanced by tokens; the slices' output rows are
+the chunks' kept counts as the reference plans them; and the gather over two
+and three gloo ranks rebuilds the whole-model arrays exactly as one rank
+holding every slice would."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+import parity
+from kvc_b200 import shard
+
+
+def test_partition_covers_every_unit_once_in_order():
+    for n_layers, T, ratio, world in [(12, 100_000, 0.2, 8), (12, 100_000, 0.2, 3), (32, 16_384, 0.2, 4),
+                                      (1, 4096, 0.5, 2), (2, 3000, 0.2, 8), (12, 100_000, 0.2, 1)]:
+        plan = shard.partition(n_layers, T, ratio, world)
+        assert len(plan) == world
+        chunks = shard.chunk_table(T, ratio)
+        ref_units = parity.plan_units(T, dict(target_ratio=ratio))
+        assert [(c[0], c[1], c[2]) for c in chunks] == [(u[0], u[1], u[2]) for u in ref_units]
+        seen = []
+        for sl in plan:
+            for s in sl:
+                assert s.tok0 == chunks[s.c0][0] and s.tok1 == chunks[s.c1 - 1][0] + chunks[s.c1 - 1][1]
+                assert s.kept == sum(c[2] for c in chunks[s.c0:s.c1])
+                seen += [(s.layer, c) for c in range(s.c0, s.c1)]
+        assert seen == [(l, c) for l in range(n_layers) for c in range(len(chunks))]
+        loads = [sum(s.tokens for s in sl) for sl in plan]
+        assert sum(loads) == n_layers * T
+        if n_layers * len(chunks) >= world:
+            assert max(loads) - min(loads) <= 2 * max(c[1] for c in chunks)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _whole(n_layers, T, ratio, H, kb, vb):
+    """Deterministic stand-ins of whole-layer results (indices in layer positions)."""
+    out = []
+    for l in range(n_layers):
+        chunks = shard.chunk_table(T, ratio)
+        sel = np.concatenate([st + np.arange(t) * 3 % C for st, C, t in chunks]).astype(np.int32)
+        t = len(sel)
+        rng = np.random.default_rng(l)
+        out.append({"sel": sel, "beta": rng.standard_normal(H * t).astype(np.float32),
+                    "kout": rng.integers(0, 255, t * kb, dtype=np.uint8),
+                    "vout": rng.integers(0, 255, t * vb, dtype=np.uint8)})
+    return out
+
+
+def _worker(rank, world, port, q, n_layers, T, ratio, H, kb, vb):
+    os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
+                       "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
+    import torch
+    import torch.distributed as dist
+    from kvc_b200 import dist as kdist
+    try:
+        kdist.init("gloo", timeout_s=60)
+        plan = shard.partition(n_layers, T, ratio, world)
+        whole = _whole(n_layers, T, ratio, H, kb, vb)
+        local = []
+        for s in plan[rank]:                       # this rank's slice outputs, indices slice-relative
+            w = whole[s.layer]
+            t = len(w["sel"])
+            local.append({"sel": torch.from_numpy(w["sel"][s.out0:s.out1] - s.tok0),
+                          "beta": torch.from_numpy(w["beta"].reshape(H, t)[:, s.out0:s.out1].copy()).reshape(-1),
+                          "kout": torch.from_numpy(w["kout"][s.out0 * kb:s.out1 * kb].copy()),
+                          "vout": torch.from_numpy(w["vout"][s.out0 * vb:s.out1 * vb].copy())})
+        finals = None
+        if rank == 0:
+            t = shard.layer_kept(T, ratio)
+            finals = [{"sel": torch.full((t,), -1, dtype=torch.int32), "beta": torch.full((H * t,), np.nan),
+                       "kout": torch.zeros(t * kb, dtype=torch.uint8), "vout": torch.zeros(t * vb, dtype=torch.uint8)}
+                      for _ in range(n_layers)]
+        shard.gather_to_root(dist, rank, world, plan, local, finals, H)
+        ok = True
+        if rank == 0:
+            for l in range(n_layers):
+                for k in ("sel", "beta", "kout", "vout"):
+                    ok = ok and np.array_equal(finals[l][k].numpy(), whole[l][k])
+        kdist.finish(world)
+        q.put((rank, ok, None))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_rebuilds_whole_model_arrays(world):
+    args = (3, 5000, 0.2, 2, 34, 18)           # 3 layers x 4 chunks, 2 heads, row bytes 34 / 18
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q) + args) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, ok, err = q.get(timeout=120)
+        assert err is None, err
+        res[rank] = ok
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0]
