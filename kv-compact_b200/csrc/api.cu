@@ -618,6 +618,9 @@ KVC_EXPORT int kv_compact_quantized(const uint8_t * K_quant, const uint8_t * V_q
         if ((rc = kvc_launch_decode(qK, k_row_bytes, k_type, dK, T, ek, st))) return rc;
         io.k_resident = true;
     }
+    // K stays in its block format when nothing needs it decoded (tensor-core
+    // scoring, K_out re-encoded from the stored rows)
+    io.k_blocks_only = !io.k_resident && kvc_k_blocks_only(p, d.plan, k_type, k_row_bytes, qK, H, d_k);
     if ((rc = stage_call(ctx, dK, hQ, T, H, d_k, d_v, p, &d))) return rc;
     memset(result, 0, sizeof(*result));
     host_outputs outs;
@@ -649,9 +652,12 @@ KVC_EXPORT int kv_compact_quantized(const uint8_t * K_quant, const uint8_t * V_q
         int e;
         {
             kvc_stage_timer tm(ctx, KVC_ST_REQUANT, 2, s);
-            if ((e = kvc_launch_encode_gather(dK, (size_t)ek, d.sel + r0, r1 - r0, ek, k_type,
-                                              oK + (size_t)r0 * k_row_bytes, k_row_bytes, s)))
-                return e;
+            e = io.k_blocks_only
+                    ? kvc_launch_transcode_gather(qK, k_row_bytes, d.sel + r0, r1 - r0, ek, k_type,
+                                                  oK + (size_t)r0 * k_row_bytes, k_row_bytes, s)
+                    : kvc_launch_encode_gather(dK, (size_t)ek, d.sel + r0, r1 - r0, ek, k_type,
+                                               oK + (size_t)r0 * k_row_bytes, k_row_bytes, s);
+            if (e) return e;
             if ((e = kvc_launch_encode_heads(d.cv + (size_t)r0 * d_v, H, t, r1 - r0, d_v, v_type,
                                              oV + (size_t)r0 * v_row_bytes, v_row_bytes, s)))
                 return e;

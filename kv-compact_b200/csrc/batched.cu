@@ -123,12 +123,17 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
         io_p += ((size_t)T + 31) & ~31ULL;
         KVC_CUDA(cudaMemcpyAsync(dW, w.data(), (size_t)T * 4, cudaMemcpyHostToDevice, st));
     }
+    // K is decoded to fp32 unless every layer reads it only in its block
+    // format (then K_out is re-encoded from the stored rows)
+    bool k_blocks = true;
+    for (int i = 0; i < n && k_blocks; i++)
+        k_blocks = kvc_k_blocks_only(p, plans[i], m->k_type, m->k_row_bytes, L[on[i]].K, H, dk);
     std::vector<kvc_layer_job> jobs(n);
     for (int i = 0; i < n; i++) {
         const int l = on[i];
         float * dK = F + (size_t)i * (nk + nv);
         float * dV = dK + nk;
-        {
+        if (!k_blocks) {
             kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1);
             if ((rc = kvc_launch_decode((const uint8_t *)L[l].K, m->k_row_bytes, m->k_type, dK, T, ek, st))) return rc;
         }
@@ -180,9 +185,12 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
         R[l].t = t;
         if (R[l].K_out) {
             kvc_stage_timer tm(ctx, KVC_ST_REQUANT, 1);
-            if ((rc = kvc_launch_encode_gather(jobs[i].K, (size_t)ek, R[l].selected_indices, t, ek, m->k_type,
-                                               R[l].K_out, m->k_row_bytes, st)))
-                return rc;
+            rc = k_blocks ? kvc_launch_transcode_gather((const uint8_t *)L[l].K, m->k_row_bytes,
+                                                        R[l].selected_indices, t, ek, m->k_type, R[l].K_out,
+                                                        m->k_row_bytes, st)
+                          : kvc_launch_encode_gather(jobs[i].K, (size_t)ek, R[l].selected_indices, t, ek,
+                                                     m->k_type, R[l].K_out, m->k_row_bytes, st);
+            if (rc) return rc;
         }
         if (R[l].V_out) {
             kvc_stage_timer tm(ctx, KVC_ST_REQUANT, 1);

@@ -653,3 +653,82 @@ int kvc_launch_encode_heads(const float * cv, int H, int t, int rows, int dv, in
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
+
+// Rows re-encoded straight from their stored bytes: output row r =
+// encode(decode(source row idx[r])) block by block with decode_block /
+// encode_block, the same arithmetic the decode and encode kernels use, so the
+// bytes equal those of decoding every row to fp32 first and re-encoding the
+// kept ones. One thread per 32-value block (a warp covers consecutive blocks
+// of a row: contiguous bytes in and out); F16 / F32 rows per value.
+__global__ void __launch_bounds__(256) k_transcode_gather(const uint8_t * __restrict__ src, size_t srb,
+                                                          const int * __restrict__ idx, int rows, int nb, int type,
+                                                          uint8_t * __restrict__ dst, size_t drb) {
+    const long long total = (long long)rows * nb;
+    const int bb = type == 8 ? 34 : (type == 2 ? 18 : (type == 3 ? 20 : (type == 1 ? 2 : 4)));
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / nb;
+        const int b = (int)(i - r * nb);
+        const uint8_t * s = src + (size_t)idx[r] * srb + (size_t)b * bb;
+        uint8_t * o = dst + (size_t)r * drb + (size_t)b * bb;
+        if (type == 1) {
+            st16(o, kvc_f2h_trunc(kvc_h2f(ld16(s))));
+        } else if (type == 0) {
+            o[0] = s[0]; o[1] = s[1]; o[2] = s[2]; o[3] = s[3];
+        } else {
+            float x[QK];
+            decode_block(s, type, x);
+            encode_block(x, type, o);
+        }
+    }
+}
+
+// The same for block formats with 16-byte multiple rows: one warp per output
+// row. The source row's bytes come into shared memory by 16-byte loads, each
+// lane re-encodes whole blocks there (decode_block / encode_block over
+// shared memory), and the row goes out by 16-byte stores.
+constexpr int TR_WARPS = 8, TR_MAX_RB = 2176;        // rows up to 2,176 bytes (e.g. 64 Q8_0 blocks)
+template <int TYPE>
+__global__ void __launch_bounds__(TR_WARPS * 32) k_transcode_rows(const uint8_t * __restrict__ src, size_t rb,
+                                                                  const int * __restrict__ idx, int rows, int nb,
+                                                                  uint8_t * __restrict__ dst) {
+    constexpr int BB = TYPE == 8 ? 34 : (TYPE == 2 ? 18 : 20);
+    __shared__ __align__(16) uint8_t sin[TR_WARPS][TR_MAX_RB], sout[TR_WARPS][TR_MAX_RB];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nv = (int)(rb / 16);
+    for (long long r = (long long)blockIdx.x * TR_WARPS + warp; r < rows; r += (long long)gridDim.x * TR_WARPS) {
+        const uint4 * s = reinterpret_cast<const uint4 *>(src + (size_t)idx[r] * rb);
+        for (int i = lane; i < nv; i += 32) reinterpret_cast<uint4 *>(sin[warp])[i] = s[i];
+        __syncwarp();
+        for (int b = lane; b < nb; b += 32) {
+            float x[QK];
+            decode_block(sin[warp] + b * BB, TYPE, x);
+            encode_block(x, TYPE, sout[warp] + b * BB);
+        }
+        __syncwarp();
+        uint4 * o = reinterpret_cast<uint4 *>(dst + (size_t)r * rb);
+        for (int i = lane; i < nv; i += 32) o[i] = reinterpret_cast<const uint4 *>(sout[warp])[i];
+        __syncwarp();
+    }
+}
+
+int kvc_launch_transcode_gather(const uint8_t * src, size_t src_rb, const int * idx, int rows, int n, int type,
+                                uint8_t * dst, size_t dst_rb, cudaStream_t st) {
+    if (rows <= 0) return KVC_OK;
+    if (is_block(type) && src_rb == dst_rb && src_rb % 16 == 0 && src_rb <= (size_t)TR_MAX_RB &&
+        src_rb == (size_t)(n / QK) * (size_t)kvc_block_bytes(type) && (((uintptr_t)src) & 15) == 0 &&
+        (((uintptr_t)dst) & 15) == 0) {
+        const int grid = (int)std::min<long long>(((long long)rows + TR_WARPS - 1) / TR_WARPS, 148LL * 8);
+        if (type == 8) k_transcode_rows<8><<<grid, TR_WARPS * 32, 0, st>>>(src, src_rb, idx, rows, n / QK, dst);
+        else if (type == 2) k_transcode_rows<2><<<grid, TR_WARPS * 32, 0, st>>>(src, src_rb, idx, rows, n / QK, dst);
+        else k_transcode_rows<3><<<grid, TR_WARPS * 32, 0, st>>>(src, src_rb, idx, rows, n / QK, dst);
+        KVC_CUDA(cudaGetLastError());
+        return KVC_OK;
+    }
+    const int nb = is_block(type) ? n / QK : n;
+    const long long work = (long long)rows * nb;
+    const int grid = (int)std::min<long long>((work + 255) / 256, 148LL * 16);
+    k_transcode_gather<<<grid, 256, 0, st>>>(src, src_rb, idx, rows, nb, type, dst, dst_rb);
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}

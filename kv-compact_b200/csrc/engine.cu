@@ -12,6 +12,7 @@
 #include <math.h>
 #include <limits.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 #include <thread>
@@ -43,6 +44,17 @@ static int size_t_for(int T, const kv_compact_params & p) {   // :396-409
 static int clamp_prefix(int prefix, int t) {
     if (prefix <= 0) return 0;
     return prefix < t ? prefix : t;
+}
+
+bool kvc_k_blocks_only(const kv_compact_params & p, const kvc_plan & pl, int k_type, size_t k_row_bytes,
+                       const void * k_base, int H, int dk) {
+    if (p.use_diversity || pl.top_cheap || pl.units.empty()) return false;
+    int max_nq = 1;
+    for (const kvc_plan_unit & u : pl.units) {
+        if (u.qmode != 0 || u.nq != pl.nq_top) return false;
+        max_nq = std::max(max_nq, u.nq);
+    }
+    return kvc_score_tc_ok(k_type, k_row_bytes, k_base, H, dk, max_nq, nullptr);
 }
 
 int kvc_make_plan(int T, int n_q, bool q_null, int H, int dk, int dv, const kv_compact_params & p,
@@ -123,8 +135,21 @@ int kvc_make_plan(int T, int n_q, bool q_null, int H, int dk, int dv, const kv_c
 static std::mutex g_ctx_mu;
 static kvc_ctx * g_ctx[64];
 
+// Host-side failure injection for tests: KVC_FAULT_INJECT=alloc makes every
+// scratch request fail as an exhausted device would (-11), =nodev makes the
+// library see no usable device (-10). Read on every call, so a test can turn
+// it on and off around single calls; nothing is injected on the GPU.
+static bool fault_injected(const char * what) {
+    const char * e = getenv("KVC_FAULT_INJECT");
+    return e && strcmp(e, what) == 0;
+}
+
 kvc_ctx * kvc_get_ctx(int * rc) {
     int dev = -1, n = 0;
+    if (fault_injected("nodev")) {
+        if (rc) *rc = KVC_ERR_NODEV;
+        return nullptr;
+    }
     if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
         cudaGetLastError();
         if (rc) *rc = KVC_ERR_NODEV;
@@ -175,6 +200,10 @@ kvc_ctx * kvc_get_ctx(int * rc) {
 }
 
 int kvc_arena(kvc_ctx * ctx, int slot, size_t bytes, void ** out) {
+    if (fault_injected("alloc")) {
+        fprintf(stderr, "[kvc] injected allocation failure (KVC_FAULT_INJECT=alloc)\n");
+        return KVC_ERR_OOM;
+    }
     if (bytes == 0) bytes = 256;
     if (ctx->arena_cap[slot] < bytes) {
         if (ctx->arena[slot]) {
@@ -544,6 +573,26 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             if (l == 0) tcg = g;
         }
     }
+    for (int l = 0; l < n_jobs; l++)             // undecoded K needs the tensor-core scoring
+        if (jobs[l].io && jobs[l].io->k_blocks_only && !tc_score) return KVC_ERR_SHAPE;
+    // The refit target Y = softmax(S) V in the scoring pass itself when V's
+    // rows are in one block format the fused kernel reads (score_tc.cu)
+    kvc_score_tc_geom vg;
+    bool fused_pv = tc_score && v_blocks && !P.use_omp;
+    {
+        int max_nq_all = 1;
+        for (int l = 0; l < n_jobs; l++)
+            for (const kvc_plan_unit & pu : jobs[l].plan->units) max_nq_all = std::max(max_nq_all, pu.nq);
+        for (int l = 0; l < n_jobs && fused_pv; l++) {
+            const bool streamed = jobs[l].io != nullptr;
+            const uint8_t * vb = streamed ? jobs[l].io->v.stage : jobs[l].Vq;
+            kvc_score_tc_geom g;
+            fused_pv = vb != nullptr &&
+                       kvc_score_pv_tc_ok(dk, dv, max_nq_all, tcg, (int)P.v_type, (size_t)P.v_rb, vb, H, &g) &&
+                       (l == 0 || (g.seg == vg.seg && g.raww == vg.raww));
+            if (l == 0) vg = g;
+        }
+    }
     void * d_maps = nullptr;
     if (tc_score) {                               // one TMA map per job (layer): its K rows as bytes x rows
         const size_t mb = kvc_score_tc_map_bytes();
@@ -553,13 +602,28 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             const uint8_t * kb = streamed ? jobs[l].io->k.stage : jobs[l].Kq;
             const size_t krb = streamed ? jobs[l].io->k.row_bytes : jobs[l].k_row_bytes;
             int rcm;
-            if ((rcm = kvc_score_tc_make_map(maps.data() + (size_t)l * mb / 8, kb, krb, jobs[l].plan->T, tcg.raww)))
+            if ((rcm = kvc_score_tc_make_map(maps.data() + (size_t)l * mb / 8, kb, krb, jobs[l].plan->T, tcg.raww,
+                                             fused_pv)))
                 return rcm;
         }
+        if (fused_pv) {                           // then one per job for V's rows
+            maps.resize((size_t)2 * n_jobs * mb / 8);
+            for (int l = 0; l < n_jobs; l++) {
+                const bool streamed = jobs[l].io != nullptr;
+                const uint8_t * vb = streamed ? jobs[l].io->v.stage : jobs[l].Vq;
+                int rcm;
+                if ((rcm = kvc_score_tc_make_map(maps.data() + (size_t)(n_jobs + l) * mb / 8, vb, (size_t)P.v_rb,
+                                                 jobs[l].plan->T, vg.raww, true)))
+                    return rcm;
+            }
+        }
+        const size_t nmaps = fused_pv ? 2 * (size_t)n_jobs : (size_t)n_jobs;
         int rcm;
-        if ((rcm = kvc_arena(ctx, 14, (size_t)n_jobs * mb, &d_maps))) return rcm;
-        KVC_CUDA(cudaMemcpyAsync(d_maps, maps.data(), (size_t)n_jobs * mb, cudaMemcpyHostToDevice, st));
+        if ((rcm = kvc_arena(ctx, 14, nmaps * mb, &d_maps))) return rcm;
+        KVC_CUDA(cudaMemcpyAsync(d_maps, maps.data(), nmaps * mb, cudaMemcpyHostToDevice, st));
     }
+    const void * d_vmaps = fused_pv ? (const void *)((const uint8_t *)d_maps + (size_t)n_jobs * kvc_score_tc_map_bytes())
+                                    : nullptr;
     if (io && !v_blocks) jobs[0].v_decoded = true;  // arrive() decodes every group's rows
     for (int l = 0; l < n_jobs && !v_blocks; l++) {
         kvc_layer_job & J = jobs[l];
@@ -711,7 +775,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             u.sel_off = bt.is; bt.is += al32(pu.t);
             u.c_off = bt.is; bt.is += al32(4LL * pu.C);
             const int n = std::min(pu.nq, pu.t);
-            if (n > 3072) return KVC_ERR_SHAPE;
+            if (n > ((p.skip_beta && !p.use_omp) ? KVC_LSQ_MAX_N : KVC_NNLS_MAX_N)) return KVC_ERR_SHAPE;
             long long gper = (long long)n * n;
             if (!p.skip_beta) gper = std::max<long long>(gper, (long long)kvc_nnls_doubles_per_head(pu.t, pu.nq));
             u.g_off = bt.gs; bt.gs += al32((long long)H * gper);
@@ -819,7 +883,8 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     auto arrive = [&](cudaEvent_t e, const kvc_stream_io::input & in, const float * dst, int ncols, int r0,
                       int r1, cudaStream_t s) -> int {
         KVC_CUDA(cudaStreamWaitEvent(s, e, 0));
-        if (in.type < 0 || (v_blocks && &in == &io->v)) return KVC_OK;     // used as they are
+        if (in.type < 0 || (v_blocks && &in == &io->v) || (io->k_blocks_only && &in == &io->k))
+            return KVC_OK;                                                 // used as they are
         kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1, s);
         return kvc_launch_decode(in.stage + (size_t)r0 * in.row_bytes, in.row_bytes, in.type,
                                  const_cast<float *>(dst) + (size_t)r0 * ncols, r1 - r0, ncols, s);
@@ -832,8 +897,10 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         int e;
         {
             kvc_stage_timer tm(ctx, KVC_ST_SCORE, 1, s);
-            e = tc_score ? kvc_launch_score_tc(du, nu, P, F, d_maps, tcg, 2, s)
-                         : kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, 2, s, rows_aligned);
+            // fused: Y = softmax(S) V comes out of the same launch (timed as scoring)
+            e = fused_pv ? kvc_launch_score_pv_tc(du, nu, P, F, d_maps, d_vmaps, tcg, vg, 2, s)
+                : tc_score ? kvc_launch_score_tc(du, nu, P, F, d_maps, tcg, 2, s)
+                           : kvc_launch_score(du, nu, bt.max_nq, bt.max_C, P, F, 2, s, rows_aligned);
             if (e) return e;
         }
         if (P.use_omp) {                             // needs the raw scores: before the softmax
@@ -858,7 +925,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         const kvc_unit * du = ctx->d_units + bt.u0;
         const int max_nq = bt.max_nq, max_t = bt.max_t, max_n = bt.max_n;
         int e;
-        {
+        if (!fused_pv) {
             kvc_stage_timer tm(ctx, KVC_ST_PV, 1, s);
             if ((e = kvc_launch_pv(du, nu, max_nq, P, F, true, s))) return e;
         }
@@ -926,11 +993,12 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             const batch & bt = B[bi];
             cudaStream_t gs = ctx->group_stream[bi % KVC_GROUP_STREAMS];
             if (ev_k[bi] && (rc = arrive(ev_k[bi], io->k, jobs[0].K, H * dk, bt.row0, bt.row1, gs))) return rc;
+            if (fused_pv && (rc = arrive(ev_v[bi], io->v, jobs[0].V, H * dv, bt.row0, bt.row1, gs))) return rc;
             if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), gs));
             if ((rc = scoring(bt, gs))) return rc;
             kvc_trace(ctx, "s" + std::to_string(bi), gs);
             if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), gs));
-            if ((rc = arrive(ev_v[bi], io->v, jobs[0].V, H * dv, bt.row0, bt.row1, gs))) return rc;
+            if (!fused_pv && (rc = arrive(ev_v[bi], io->v, jobs[0].V, H * dv, bt.row0, bt.row1, gs))) return rc;
             if ((rc = refit(bt, gs))) return rc;
             if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), gs));
             kvc_trace(ctx, "r" + std::to_string(bi), gs);
@@ -967,10 +1035,11 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         const batch & bt = B[bi];
         if ((rc = weights(bt, st))) return rc;
         if (io && ev_k[bi] && (rc = arrive(ev_k[bi], io->k, jobs[0].K, H * dk, bt.row0, bt.row1, st))) return rc;
+        if (io && fused_pv && (rc = arrive(ev_v[bi], io->v, jobs[0].V, H * dv, bt.row0, bt.row1, st))) return rc;
         if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
         if ((rc = shared ? scoring_shared(bt, st) : scoring(bt, st))) return rc;
         if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
-        if (io && (rc = arrive(ev_v[bi], io->v, jobs[0].V, H * dv, bt.row0, bt.row1, st))) return rc;
+        if (io && !fused_pv && (rc = arrive(ev_v[bi], io->v, jobs[0].V, H * dv, bt.row0, bt.row1, st))) return rc;
         if ((rc = refit(bt, st))) return rc;
         if (phase) KVC_CUDA(cudaEventRecord(phase_event(ctx), st));
         if (io) kvc_trace(ctx, "r" + std::to_string(bi), st);

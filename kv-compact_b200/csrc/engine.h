@@ -65,12 +65,21 @@ struct kvc_stream_io {
         int type = -1;
     } k, v;
     bool k_resident = false;   // K already uploaded and decoded in full (top-level cheap queries)
+    bool k_blocks_only = false; // K is read only in its block format (kvc_k_blocks_only): not decoded
     int max_groups = 1;        // upper bound on the number of groups
     double size_ratio = 1.0;   // size of group g+1 / size of group g
     // Queue whatever consumes output rows [r0, r1) (requantisation, copies
     // to the host) on stream `st`, after the group's results.
     std::function<int(int r0, int r1, cudaStream_t st)> emit;
 };
+
+// Whether a layer's pipeline reads K only in its stored block format: the
+// tensor-core scoring takes it (kvc_score_tc_ok) and nothing needs fp32 K
+// rows (no cheap queries, which sample K rows; no diversity greedy, which
+// compares K rows; the quality metrics come from the per-chunk records).
+// K_out is then re-encoded from the stored rows (kvc_launch_transcode_gather).
+bool kvc_k_blocks_only(const kv_compact_params & p, const struct kvc_plan & pl, int k_type, size_t k_row_bytes,
+                       const void * k_base, int H, int dk);
 
 // Device-side job for one layer: fp32 caches resident on the device.
 struct kvc_layer_job {
@@ -267,13 +276,24 @@ struct kvc_score_tc_geom {
 bool kvc_score_tc_ok(int k_type, size_t k_row_bytes, const void * k_base, int H, int dk, int max_nq,
                      kvc_score_tc_geom * g);
 size_t kvc_score_tc_map_bytes();
-// Encode the TMA map of one layer's K rows into `map` (kvc_score_tc_map_bytes() bytes, 64-byte aligned).
-int kvc_score_tc_make_map(void * map, const uint8_t * k_base, size_t k_row_bytes, int rows, int raww);
+// Encode the TMA map of one layer's K (or V) rows into `map` (kvc_score_tc_map_bytes()
+// bytes, 64-byte aligned); `fused`: the box height of the fused kernel's tiles.
+int kvc_score_tc_make_map(void * map, const uint8_t * k_base, size_t k_row_bytes, int rows, int raww, bool fused);
 // S (and, mode 2, each row's maximum in pm slot 0) of every (unit, head);
 // d_maps[layer] = the TMA map of the layer's K rows.
 int kvc_launch_score_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,
                         const void * d_maps, const kvc_score_tc_geom & g, int mode, cudaStream_t st);
 int kvc_score_tc_take_error(cudaStream_t st);
+// Scoring fused with the refit target Y = softmax(S) V (d_k = d_v = 128, V
+// in Q8_0 / Q4_0 rows read by TMA): whether it applies (fills V's geometry),
+// and the launch (Y into each unit's y_off block; no separate refit-target
+// pass). Opt-in with KVC_FUSED_PV=1: on cfg4 it measured slower (7.6 ms per
+// step) than the separate scoring and refit-target kernels (3.0 + 3.4 ms).
+bool kvc_score_pv_tc_ok(int dk, int dv, int max_nq, const kvc_score_tc_geom & kg, int v_type, size_t v_row_bytes,
+                        const void * v_base, int H, kvc_score_tc_geom * vg);
+int kvc_launch_score_pv_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,
+                           const void * d_kmaps, const void * d_vmaps, const kvc_score_tc_geom & kg,
+                           const kvc_score_tc_geom & vg, int mode, cudaStream_t st);
 int kvc_launch_softmax_x(const kvc_unit * d_units, int n_units, int max_nq, const kvc_params_dev & P,
                          float * fs, const kvc_layer_out * d_outs, cudaStream_t st);
 int kvc_launch_aggregate(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,

@@ -50,6 +50,11 @@ enum {
 
 // Largest head dimension the kernels are instantiated for.
 #define KVC_MAX_D 256
+// Most unknowns of one least-squares solve (min(n_q, t) of a chunk): the
+// global-memory Cholesky's right-hand-side panel must fit shared memory.
+// The beta fit and OMP selection keep their own bound (KVC_NNLS_MAX_N).
+#define KVC_LSQ_MAX_N 24576
+#define KVC_NNLS_MAX_N 3072
 
 struct kvc_unit {
     const float * K;      // first row of the chunk, row stride ek = H*d_k
@@ -161,6 +166,10 @@ int kvc_launch_decode(const uint8_t * src, size_t src_row_bytes, int type, float
 int kvc_launch_encode_gather(const float * src, size_t src_stride, const int * rows_idx,
                              int rows, int n, int type, uint8_t * dst, size_t dst_row_bytes,
                              cudaStream_t st);
+// Output row r = encode(decode(src row idx[r])) straight from the stored
+// rows (K_out without an fp32 copy of K), bit-identical to decoding first.
+int kvc_launch_transcode_gather(const uint8_t * src, size_t src_rb, const int * idx, int rows, int n, int type,
+                                uint8_t * dst, size_t dst_rb, cudaStream_t st);
 // V_out rows 0..rows-1 from cv[h][j][:] (heads t rows apart).
 int kvc_launch_encode_heads(const float * cv, int H, int t, int rows, int dv, int type, uint8_t * dst,
                             size_t dst_row_bytes, cudaStream_t st);

@@ -409,7 +409,11 @@ __global__ void __launch_bounds__(128) k_dgemm_async(const kvc_unit * __restrict
 }
 
 // Panel width for n unknowns: keeps the n x PW fp64 panel within 96 KB.
-__host__ __device__ inline int lsq_panel(int n) { return n <= 384 ? 32 : (n <= 1536 ? 8 : 4); }
+// Right-hand-side columns per panel of k_chol_solve: n x panel doubles of
+// shared memory (at most 192 KB up to KVC_LSQ_MAX_N unknowns).
+__host__ __device__ inline int lsq_panel(int n) {
+    return n <= 384 ? 32 : (n <= 1536 ? 8 : (n <= 6144 ? 4 : (n <= 12288 ? 2 : 1)));
+}
 
 __global__ void __launch_bounds__(256) k_chol_solve(const kvc_unit * __restrict__ units, kvc_params_dev P,
                                                     const float * __restrict__ fs, double * __restrict__ gs,

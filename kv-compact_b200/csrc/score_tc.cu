@@ -27,7 +27,8 @@
 // tile i into the B layout; one thread issues tile i's 16 MMAs (M = 128 query
 // rows, N = 64 keys, K = 16) into one of two TMEM accumulator sets while all
 // threads run the epilogue of tile i-1 (TMEM -> registers, block scales,
-// transpose through shared memory, coalesced stores of S, running row maxima).
+// 16-byte stores of each thread's 16 consecutive scores of its row, running
+// row maxima).
 // Every mbarrier wait is bounded: a wait that runs out records an error the
 // host reads (kvc_tc_take_error), and the CTA waits (bounded) for its copies
 // and MMAs in flight, frees its TMEM and returns.
@@ -46,9 +47,9 @@ constexpr int TC_N = 64;           // keys per tile
 constexpr int TC_RS = 4;           // raw K tiles in flight
 constexpr int TC_THREADS = 256;
 constexpr int TC_NPIECE = 2;       // fp16 pieces of each scaled query value
-constexpr int TB_LD = TC_M + 1;    // transpose buffer stride (floats): conflict-free both ways
+constexpr int FN = 32;             // keys per tile of the fused scoring + refit-target kernel
 constexpr uint32_t TC_RAW_MAX = 256;        // raw bytes per key row of a head, at most (the TMA box width)
-constexpr uint32_t TC_POLLS = 1u << 20;     // bound of every mbarrier wait
+constexpr uint32_t TC_POLLS = 1u << 16;     // bound of every mbarrier wait (far above any legitimate wait)
 
 __device__ int g_score_tc_error;   // first error code of k_score_tc (0: none)
 
@@ -64,8 +65,7 @@ struct tc_cfg {
     static constexpr uint32_t OFF_B = OFF_A + TC_NPIECE * A_PIECE;
     static constexpr uint32_t OFF_RAW = OFF_B + 2 * B_TILE;
     static constexpr uint32_t OFF_SC = OFF_RAW + TC_RS * RAW_STAGE;
-    static constexpr uint32_t OFF_TB = OFF_SC + 2 * NBLK * TC_N * 4;
-    static constexpr uint32_t OFF_ROWC = OFF_TB + TC_N * TB_LD * 4;
+    static constexpr uint32_t OFF_ROWC = OFF_SC + 2 * NBLK * TC_N * 4;
     static constexpr uint32_t OFF_RED = OFF_ROWC + TC_M * 4;
     static constexpr uint32_t SMEM = OFF_RED + 2 * TC_M * 4;
     static constexpr uint32_t TMEM_COLS = 2 * NBLK * TC_N;  // two accumulator sets
@@ -96,27 +96,14 @@ __device__ __forceinline__ uint32_t q4_pair(uint32_t n) {
     return *reinterpret_cast<const uint32_t *>(&v);
 }
 
-// Raw bytes of one 64-key tile (row k at raw + k*raww, the head's first
-// block `off` bytes in) -> the B operand (fp16 codes, K-major canonical
-// layout) and the per-(block, key) scales.
-template <int DK, int KT>
-__device__ __forceinline__ void convert_tile(const uint8_t * raw, int raww, int off, uint8_t * B, float * sc,
-                                             int tid) {
+// One (block b, key k) of a K tile: its 32 codes into the B operand, its scale into sc.
+template <int DK, int KT, int TN>
+__device__ __forceinline__ void convert_block(const uint8_t * raw, int raww, int off, uint8_t * B, float * sc,
+                                              int b, int k) {
     using CF = tc_cfg<DK>;
-    if (KT == 1) {                                  // F16: the values are the operand
-        for (int it = tid; it < TC_N * (DK / 8); it += TC_THREADS) {
-            const int k = it & (TC_N - 1), c = it >> 6;
-            const uint4 v = *reinterpret_cast<const uint4 *>(raw + k * raww + off + 16 * c);
-            *reinterpret_cast<uint4 *>(B + (k >> 3) * CF::SBO + c * 128 + (k & 7) * 16) = v;
-        }
-        if (tid < CF::NBLK * TC_N) sc[tid] = 1.0f;
-        return;
-    }
-    if (tid >= CF::NBLK * TC_N) return;
-    const int b = tid >> 6, k = tid & (TC_N - 1);   // one (block, key) per thread
     constexpr int BB = KT == 8 ? 34 : 18;
     const unsigned short * w = reinterpret_cast<const unsigned short *>(raw + k * raww + off + BB * b);
-    sc[b * TC_N + k] = __half2float(__ushort_as_half(w[0]));
+    sc[b * TN + k] = __half2float(__ushort_as_half(w[0]));
     uint8_t * dst = B + (k >> 3) * CF::SBO + (4 * b) * 128 + (k & 7) * 16;
     if (KT == 8) {
 #pragma unroll
@@ -142,60 +129,36 @@ __device__ __forceinline__ void convert_tile(const uint8_t * raw, int raww, int 
     }
 }
 
-}  // namespace
 
-// One CTA per (unit = blockIdx.y, head = blockIdx.x). maps[u.layer]: the 2-D
-// TMA map of the layer's K rows (bytes x rows); `seg` = bytes of one head in a
-// row, `raww` = TMA box width in bytes (covers any head's bytes from the
-// 16-byte boundary below them). mode 2 also writes each row's maximum score
-// (pm slot 0 of the row: one tile spanning the whole chunk).
-template <int DK, int KT>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __restrict__ units, kvc_params_dev P,
-                                                            float * __restrict__ fs,
-                                                            const CUtensorMap * __restrict__ maps, int seg, int raww,
-                                                            int mode) {
-    using namespace kvc_tc;
+// Raw bytes of one tile of TN keys (row k at raw + k*raww, the head's first
+// block `off` bytes in) -> the B operand (fp16 codes, K-major canonical
+// layout) and the per-(block, key) scales, stored [block][TN]. NT threads
+// (tid in [0, NT)) share the work.
+template <int DK, int KT, int TN = TC_N, int NT = TC_THREADS>
+__device__ __forceinline__ void convert_tile(const uint8_t * raw, int raww, int off, uint8_t * B, float * sc,
+                                             int tid) {
     using CF = tc_cfg<DK>;
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bar_tma[TC_RS];
-    __shared__ __align__(8) uint64_t bar_mma[2];
-    __shared__ uint32_t tmem_slot;
-    const kvc_unit u = units[blockIdx.y];
-    if (!u.active) return;
-    const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int C = u.C, nq = u.nq;
-    const int ntiles = (C + TC_N - 1) / TC_N;
-    const void * map = maps + u.layer;
-    const int hx = seg * h, x0 = hx & ~15, off = hx - x0;
-    const uint32_t raw_bytes = (uint32_t)raww * TC_N;
-    uint8_t * sA = smem + CF::OFF_A;
-    uint8_t * sB = smem + CF::OFF_B;
-    uint8_t * sRaw = smem + CF::OFF_RAW;
-    float * sSC = reinterpret_cast<float *>(smem + CF::OFF_SC);
-    float * sTB = reinterpret_cast<float *>(smem + CF::OFF_TB);
-    float * rowc = reinterpret_cast<float *>(smem + CF::OFF_ROWC);
-    float * red = reinterpret_cast<float *>(smem + CF::OFF_RED);
-
-    if (warp == 0) tmem_alloc(&tmem_slot, CF::TMEM_COLS);
-    if (tid == 0) {
-        for (int s = 0; s < TC_RS; s++) mbar_init(&bar_tma[s], 1);
-        mbar_init(&bar_mma[0], 1);
-        mbar_init(&bar_mma[1], 1);
-        mbar_init_fence();
-    }
-    fence_before_sync();
-    __syncthreads();
-    fence_after_sync();
-    const uint32_t tmem = tmem_slot;
-    int issued = 0;                                  // raw tiles whose load was issued (thread 0)
-    if (tid == 0) {
-        for (; issued < TC_RS && issued < ntiles; issued++) {
-            mbar_arrive_expect_tx(&bar_tma[issued], raw_bytes);
-            tma_load_2d(sRaw + issued * CF::RAW_STAGE, map, x0, u.token_base + issued * TC_N, &bar_tma[issued]);
+    if constexpr (KT == 1) {                        // F16: the values are the operand
+        for (int it = tid; it < TN * (DK / 8); it += NT) {
+            const int k = it % TN, c = it / TN;
+            const uint4 v = *reinterpret_cast<const uint4 *>(raw + k * raww + off + 16 * c);
+            *reinterpret_cast<uint4 *>(B + (k >> 3) * CF::SBO + c * 128 + (k & 7) * 16) = v;
         }
+        for (int it = tid; it < CF::NBLK * TN; it += NT) sc[it] = 1.0f;
+    } else {
+        for (int it = tid; it < CF::NBLK * TN; it += NT)
+            convert_block<DK, KT, TN>(raw, raww, off, B, sc, it / TN, it % TN);
     }
+}
 
-    // ---- A: the query rows of head h, scaled per row by 2^e and split in two fp16 pieces
+// The A operand: the query rows of head h (rows >= n_q zero), each scaled by
+// 2^e (max |Q| in [2^14, 2^15)) and split in two fp16 pieces, in the K-major
+// canonical layout; rowc[r] = 2^-e / sqrt(d_k). 256 threads, two per row.
+template <int DK>
+__device__ __forceinline__ void load_query_pieces(const kvc_unit & u, const kvc_params_dev & P, int h, uint8_t * sA,
+                                                  float * rowc, int tid) {
+    using CF = tc_cfg<DK>;
+    const int nq = u.nq, C = u.C;
     {
         const int r = tid >> 1, hf = tid & 1;       // two threads per row, DK/2 values each
         const int ek = P.H * DK;
@@ -246,6 +209,60 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __r
             *reinterpret_cast<uint4 *>(sA + CF::A_PIECE + o) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
         }
     }
+}
+}  // namespace
+
+// One CTA per (unit = blockIdx.y, head = blockIdx.x). maps[u.layer]: the 2-D
+// TMA map of the layer's K rows (bytes x rows); `seg` = bytes of one head in a
+// row, `raww` = TMA box width in bytes (covers any head's bytes from the
+// 16-byte boundary below them). mode 2 also writes each row's maximum score
+// (pm slot 0 of the row: one tile spanning the whole chunk).
+template <int DK, int KT>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __restrict__ units, kvc_params_dev P,
+                                                            float * __restrict__ fs,
+                                                            const CUtensorMap * __restrict__ maps, int seg, int raww,
+                                                            int mode, uint32_t polls, int stall) {
+    using namespace kvc_tc;
+    using CF = tc_cfg<DK>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bar_tma[TC_RS];
+    __shared__ __align__(8) uint64_t bar_mma[2];
+    __shared__ uint32_t tmem_slot;
+    const kvc_unit u = units[blockIdx.y];
+    if (!u.active) return;
+    const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int C = u.C, nq = u.nq;
+    const int ntiles = (C + TC_N - 1) / TC_N;
+    const void * map = maps + u.layer;
+    const int hx = seg * h, x0 = hx & ~15, off = hx - x0;
+    const uint32_t raw_bytes = (uint32_t)raww * TC_N;
+    uint8_t * sA = smem + CF::OFF_A;
+    uint8_t * sB = smem + CF::OFF_B;
+    uint8_t * sRaw = smem + CF::OFF_RAW;
+    float * sSC = reinterpret_cast<float *>(smem + CF::OFF_SC);
+    float * rowc = reinterpret_cast<float *>(smem + CF::OFF_ROWC);
+    float * red = reinterpret_cast<float *>(smem + CF::OFF_RED);
+
+    if (warp == 0) tmem_alloc(&tmem_slot, CF::TMEM_COLS);
+    if (tid == 0) {
+        for (int s = 0; s < TC_RS; s++) mbar_init(&bar_tma[s], 1);
+        mbar_init(&bar_mma[0], 1);
+        mbar_init(&bar_mma[1], 1);
+        mbar_init_fence();
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    int issued = 0;                                  // raw tiles whose load was issued (thread 0)
+    if (tid == 0) {
+        for (; issued < TC_RS && issued < ntiles; issued++) {
+            mbar_arrive_expect_tx(&bar_tma[issued], raw_bytes);
+            tma_load_2d(sRaw + issued * CF::RAW_STAGE, map, x0, u.token_base + issued * TC_N, &bar_tma[issued]);
+        }
+    }
+
+    load_query_pieces<DK>(u, P, h, sA, rowc, tid);
     fence_smem_to_async();
     __syncthreads();
 
@@ -254,11 +271,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __r
     const float rc = rowc[q];
     float rmax = -INFINITY;
     float * out = fs + u.s_off + (long long)h * nq * C;
+    const bool vec_out = ((C & 3) == 0) && ((((uintptr_t)out) & 15) == 0);
     int err = 0, committed = -1, waited_tma = 0;
     for (int i = 0; i <= ntiles; i++) {
         bool ok = true;
-        if (i < ntiles) ok = mbar_wait(&bar_tma[i % TC_RS], (uint32_t)((i / TC_RS) & 1), TC_POLLS);
-        if (i >= 1) ok = ok && mbar_wait(&bar_mma[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), TC_POLLS);
+        if (stall && i == 0) ok = mbar_wait(&bar_mma[1], 0u, 64u);   // nothing completes this phase yet
+        if (ok && i < ntiles) ok = mbar_wait(&bar_tma[i % TC_RS], (uint32_t)((i / TC_RS) & 1), polls);
+        if (i >= 1) ok = ok && mbar_wait(&bar_mma[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), polls);
         if (__syncthreads_or(!ok)) {                 // the same decision in every thread
             err = 1;
             break;
@@ -279,7 +298,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __r
                 issued++;
             }
             fence_after_sync();
-            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB + (i & 1) * CF::B_TILE);
+            // descriptors: base + (byte offset >> 4) in the start-address field
+            const uint64_t a0 = sdesc(smem_u32(sA), 128, CF::SBO), b0 = sdesc(smem_u32(sB + (i & 1) * CF::B_TILE), 128, CF::SBO);
             const uint32_t d0 = tmem + (uint32_t)((i & 1) * CF::NBLK * TC_N);
 #pragma unroll
             for (int b = 0; b < CF::NBLK; b++)
@@ -288,8 +308,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __r
 #pragma unroll
                     for (int s = 0; s < 2; s++) {
                         const uint32_t ko = (uint32_t)(4 * b + 2 * s) * 128;
-                        mma_f16(d0 + (uint32_t)(b * TC_N), sdesc(a0 + p * CF::A_PIECE + ko, 128, CF::SBO),
-                                sdesc(b0 + ko, 128, CF::SBO), IDESC, (p | s) != 0);
+                        mma_f16(d0 + (uint32_t)(b * TC_N), a0 + ((p * CF::A_PIECE + ko) >> 4), b0 + (ko >> 4), IDESC,
+                                (p | s) != 0);
                     }
             commit(&bar_mma[i & 1]);
         }
@@ -297,6 +317,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __r
         if (i >= 1) {                                // epilogue of tile j = i - 1
             const int j = i - 1, bj = j & 1, j0 = j * TC_N;
             const float * scb = sSC + bj * CF::NBLK * TC_N;
+            const bool full = j0 + TC_N <= C;        // every column of the tile is a key of the chunk
 #pragma unroll
             for (int c16 = 0; c16 < 2; c16++) {
                 const int cb = ch * 32 + c16 * 16;
@@ -306,6 +327,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __r
                     tmem_ld16_nowait(tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(bj * CF::NBLK * TC_N + b * TC_N + cb),
                                      acc[b]);
                 tmem_wait_ld();
+                float v[16];
 #pragma unroll
                 for (int e4 = 0; e4 < 4; e4++) {
                     float4 sc[CF::NBLK];
@@ -314,7 +336,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __r
                         sc[b] = *reinterpret_cast<const float4 *>(scb + b * TC_N + cb + 4 * e4);
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        const int col = cb + 4 * e4 + e;
                         const float s0 = e == 0 ? sc[0].x : (e == 1 ? sc[0].y : (e == 2 ? sc[0].z : sc[0].w));
                         float s = __fmul_rn(__uint_as_float(acc[0][4 * e4 + e]), s0);
 #pragma unroll
@@ -322,22 +343,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __r
                             const float sb = e == 0 ? sc[b].x : (e == 1 ? sc[b].y : (e == 2 ? sc[b].z : sc[b].w));
                             s = __fmaf_rn(__uint_as_float(acc[b][4 * e4 + e]), sb, s);
                         }
-                        s = __fmul_rn(s, rc);
-                        sTB[col * TB_LD + q] = s;
-                        if (j0 + col < C) rmax = fmaxf(rmax, s);
+                        v[4 * e4 + e] = __fmul_rn(s, rc);
                     }
                 }
+                // 16 consecutive scores of this thread's row: four 16-byte stores
+                if (q < nq) {
+                    float * dst = out + (long long)q * C + j0 + cb;
+                    if (full && vec_out) {
+#pragma unroll
+                        for (int e4 = 0; e4 < 4; e4++)
+                            reinterpret_cast<float4 *>(dst)[e4] =
+                                make_float4(v[4 * e4], v[4 * e4 + 1], v[4 * e4 + 2], v[4 * e4 + 3]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; e++)
+                            if (j0 + cb + e < C) dst[e] = v[e];
+                    }
+                }
+                if (full) {
+#pragma unroll
+                    for (int e = 0; e < 16; e++) rmax = fmaxf(rmax, v[e]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 16; e++)
+                        if (j0 + cb + e < C) rmax = fmaxf(rmax, v[e]);
+                }
             }
-            fence_before_sync();
-            __syncthreads();                         // the tile's scores are in the transpose buffer
-#pragma unroll 4
-            for (int r = 0; r < TC_M / 8; r++) {
-                const int q2 = warp + 8 * r;
-                if (q2 >= nq) break;
-                float * row = out + (long long)q2 * C + j0;
-                if (j0 + lane < C) row[lane] = sTB[lane * TB_LD + q2];
-                if (j0 + 32 + lane < C) row[32 + lane] = sTB[(32 + lane) * TB_LD + q2];
-            }
+            fence_before_sync();                     // TMEM reads done before the next barrier
         }
     }
     if (err) {
@@ -423,12 +455,13 @@ bool kvc_score_tc_ok(int k_type, size_t k_row_bytes, const void * k_base, int H,
 
 size_t kvc_score_tc_map_bytes() { return sizeof(CUtensorMap); }
 
-int kvc_score_tc_make_map(void * map, const uint8_t * k_base, size_t k_row_bytes, int rows, int raww) {
+int kvc_score_tc_make_map(void * map, const uint8_t * k_base, size_t k_row_bytes, int rows, int raww, bool fused) {
     encode_fn enc = tensor_map_encoder();
     if (!enc) return KVC_ERR_CUDA;
     const cuuint64_t dims[2] = {(cuuint64_t)k_row_bytes, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)k_row_bytes};
-    const cuuint32_t box[2] = {(cuuint32_t)raww, (cuuint32_t)TC_N};
+    // box: raww bytes x the tile's keys (64 for k_score_tc, 32 for k_score_pv_tc)
+    const cuuint32_t box[2] = {(cuuint32_t)raww, (cuuint32_t)(fused ? FN : TC_N)};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(reinterpret_cast<CUtensorMap *>(map), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
                            const_cast<uint8_t *>(k_base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -441,13 +474,24 @@ int kvc_score_tc_make_map(void * map, const uint8_t * k_base, size_t k_row_bytes
     return KVC_OK;
 }
 
+// Test hook: with KVC_TC_STALL_TEST=1 in the environment the scoring
+// kernels' first pipeline wait targets an mbarrier phase that nothing
+// completes, so the wait runs out on its bound: the kernel records its error
+// status, waits (with the full bound) for its loads and MMAs in flight, frees
+// its TMEM and returns; the call reports the error and the context stays
+// usable. Read on every launch.
+static int tc_stall() {
+    const char * e = getenv("KVC_TC_STALL_TEST");
+    return (e && atoi(e) > 0) ? 1 : 0;
+}
+
 template <int DK, int KT>
 static int launch_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs, const void * maps,
                      int seg, int raww, int mode, cudaStream_t st) {
     const uint32_t sm = tc_cfg<DK>::SMEM;
     KVC_CUDA(cudaFuncSetAttribute(k_score_tc<DK, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
     k_score_tc<DK, KT><<<dim3(P.H, n_units), TC_THREADS, sm, st>>>(
-        d_units, P, fs, reinterpret_cast<const CUtensorMap *>(maps), seg, raww, mode);
+        d_units, P, fs, reinterpret_cast<const CUtensorMap *>(maps), seg, raww, mode, TC_POLLS, tc_stall());
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
@@ -477,4 +521,451 @@ int kvc_score_tc_take_error(cudaStream_t st) {
     if (h && cudaMemcpyToSymbolAsync(g_score_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) == cudaSuccess)
         cudaStreamSynchronize(st);
     return h;
+}
+
+// ---------------------------------------------------------------------------
+// Scoring fused with the refit target Y = softmax(S) V
+// ---------------------------------------------------------------------------
+//
+// The same scores as k_score_tc (written to S, row maxima to pm), and in the
+// same pass Y_h = A_h V_h (src/kv-compact-api.cpp:754-783) accumulated on the
+// tensor cores the way attention kernels do it: per row a reference maximum
+// m_ref, P = exp(S - m_ref) as the A operand (two fp16 pieces), V's values
+// (Q8_0 / Q4_0 decoded exactly, two fp16 pieces) as B, O += P V in TMEM and
+// l += sum(P); Y = O / l at the end. m_ref moves only when a tile's maximum
+// exceeds it by more than F_TAU (then O and l are scaled by exp(m_ref - m)),
+// so P <= e^F_TAU and the rescale is rare. Mathematically Y is the
+// reference's A V; the rounding differs (Y only feeds the tolerance-checked
+// least-squares right-hand side). S is not read back for Y.
+//
+// Keys in tiles of 32. Warps 0-3 own one query row per thread (TMEM lane) and
+// run the epilogue of tile i-1 (scores, row maximum, rescale, P); warps 4-7
+// convert K tile i+1 and V tile i into operands; one thread (tid 128) issues
+// the TMA loads (raw K and V rows, one ring each) and the MMAs. One
+// __syncthreads_or per tile; every other dependency is an mbarrier wait with
+// a bound.
+namespace {
+constexpr int F_RS = 3;           // raw K / raw V tiles in flight
+constexpr float F_TAU = 8.0f;     // rescale when a tile's maximum exceeds m_ref by more than this
+constexpr int F_ISSUER = 128;
+
+struct fcfg {                     // d_k = d_v = 128
+    static constexpr int NBLK = 4;
+    static constexpr uint32_t A_PIECE = TC_M * 256;           // query piece: 128 rows x 256 bytes
+    static constexpr uint32_t BK_TILE = FN * 256;             // K codes of one tile
+    static constexpr uint32_t SBO_32 = 512;                   // 32-key rows: four 16-byte chunks
+    static constexpr uint32_t P_PIECE = TC_M * FN * 2;        // P piece: 128 rows x 32 keys
+    static constexpr uint32_t BV_PIECE = 128 * FN * 2;        // V piece: 128 columns x 32 keys
+    static constexpr uint32_t RAW_STAGE = FN * TC_RAW_MAX;
+    static constexpr uint32_t OFF_A = 0;
+    static constexpr uint32_t OFF_BK = OFF_A + TC_NPIECE * A_PIECE;
+    static constexpr uint32_t OFF_RK = OFF_BK + 2 * BK_TILE;
+    static constexpr uint32_t OFF_RV = OFF_RK + F_RS * RAW_STAGE;
+    static constexpr uint32_t OFF_P = OFF_RV + F_RS * RAW_STAGE;
+    static constexpr uint32_t OFF_BV = OFF_P + 2 * 2 * P_PIECE;
+    // three V buffers: V tile i is converted while the MMAs of tile i-1 read
+    // buffer (i-1) % 3 and those of tile i-2 may still read buffer (i-2) % 3
+    static constexpr uint32_t OFF_SC = OFF_BV + 3 * 2 * BV_PIECE;
+    // three scale buffers: the converters fill tile i+1's while the epilogue reads tile i-1's
+    static constexpr uint32_t OFF_ROWC = OFF_SC + 3 * NBLK * FN * 4;
+    static constexpr uint32_t SMEM = OFF_ROWC + TC_M * 4;
+    static constexpr uint32_t TM_S = 0;                       // two score sets: 2 x NBLK x FN columns
+    static constexpr uint32_t TM_O = 2 * NBLK * FN;           // Y accumulator: 128 columns
+    static constexpr uint32_t TMEM_COLS = 512;
+};
+static_assert(fcfg::TM_O + 128 <= fcfg::TMEM_COLS, "TMEM columns");
+static_assert(fcfg::SMEM <= 227 * 1024, "shared memory");
+
+// Value n of one V row of head h (row points at the head's first block), with
+// the codec's arithmetic: exactly the fp32 value a decoded row holds.
+template <int VT>
+__device__ __forceinline__ float v_value(const uint8_t * row, int n) {
+    constexpr int BB = VT == 8 ? 34 : 18;
+    const uint8_t * blk = row + BB * (n >> 5);
+    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(blk)));
+    if (VT == 8) return __fmul_rn(d, (float)(int8_t)blk[2 + (n & 31)]);
+    const uint8_t b = blk[2 + ((n & 31) >> 1)];
+    return __fmul_rn(d, __fsub_rn((float)((n & 1) ? (b >> 4) : (b & 15)), 8.0f));
+}
+
+// V tile (32 keys, raw rows) -> B operand [128 columns x 32 keys] K-major, two
+// fp16 pieces v = hi + lo (exact for these values up to fp16 subnormal
+// spacing); keys past `nvalid` are zero. 256 threads: thread tid takes column
+// tid % 128 and the key octets tid / 128 and tid / 128 + 2.
+template <int VT>
+__device__ __forceinline__ void convert_v_tile(const uint8_t * raw, int raww, int off, uint8_t * BV, int tid,
+                                               int nvalid) {
+    const int n = tid & 127;
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int ko = (tid >> 7) + 2 * r;
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int kk = 0; kk < 8; kk += 2) {
+            const int k = 8 * ko + kk;
+            const float v0 = k < nvalid ? v_value<VT>(raw + k * raww + off, n) : 0.0f;
+            const float v1 = k + 1 < nvalid ? v_value<VT>(raw + (k + 1) * raww + off, n) : 0.0f;
+            const __half2 a = __floats2half2_rn(v0, v1);
+            const float2 af = __half22float2(a);
+            const __half2 b = __floats2half2_rn(__fsub_rn(v0, af.x), __fsub_rn(v1, af.y));
+            hi[kk >> 1] = *reinterpret_cast<const uint32_t *>(&a);
+            lo[kk >> 1] = *reinterpret_cast<const uint32_t *>(&b);
+        }
+        const uint32_t o = (n >> 3) * fcfg::SBO_32 + ko * 128 + (n & 7) * 16;
+        *reinterpret_cast<uint4 *>(BV + o) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(BV + fcfg::BV_PIECE + o) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+}  // namespace
+
+template <int KT, int VT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_score_pv_tc(const kvc_unit * __restrict__ units, kvc_params_dev P, float * __restrict__ fs,
+                  const CUtensorMap * __restrict__ kmaps, const CUtensorMap * __restrict__ vmaps, int kseg, int kraww,
+                  int vseg, int vraww, int mode, uint32_t polls, int stall) {
+    using namespace kvc_tc;
+    using F = fcfg;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bar_k[F_RS];
+    __shared__ __align__(8) uint64_t bar_v[F_RS];
+    __shared__ __align__(8) uint64_t bar_s[2];
+    __shared__ __align__(8) uint64_t bar_y[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ float s_tmax[2][TC_M];                // the two halves' maxima of each row's tile
+    __shared__ float s_l[2][TC_M];                   // the two halves' row sums at the end
+    const kvc_unit u = units[blockIdx.y];
+    if (!u.active) return;
+    const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5;
+    const int C = u.C, nq = u.nq;
+    const int ntiles = (C + FN - 1) / FN;
+    const void * kmap = kmaps + u.layer;
+    const void * vmap = vmaps + u.layer;
+    const int kx0 = (kseg * h) & ~15, koff = kseg * h - kx0;
+    const int vx0 = (vseg * h) & ~15, voff = vseg * h - vx0;
+    uint8_t * sA = smem + F::OFF_A;
+    uint8_t * sBK = smem + F::OFF_BK;
+    uint8_t * sRK = smem + F::OFF_RK;
+    uint8_t * sRV = smem + F::OFF_RV;
+    uint8_t * sP = smem + F::OFF_P;
+    uint8_t * sBV = smem + F::OFF_BV;
+    float * sSC = reinterpret_cast<float *>(smem + F::OFF_SC);
+    float * rowc = reinterpret_cast<float *>(smem + F::OFF_ROWC);
+
+    if (warp == 0) tmem_alloc(&tmem_slot, F::TMEM_COLS);
+    if (tid == 0) {
+        for (int s = 0; s < F_RS; s++) {
+            mbar_init(&bar_k[s], 1);
+            mbar_init(&bar_v[s], 1);
+        }
+        for (int s = 0; s < 2; s++) {
+            mbar_init(&bar_s[s], 1);
+            mbar_init(&bar_y[s], 1);
+        }
+        mbar_init_fence();
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    constexpr uint32_t IDESC_S = idesc_f16(TC_M, FN), IDESC_Y = idesc_f16(TC_M, 128);
+
+    int k_issued = 0, v_issued = 0;                  // issued raw tiles (issuer thread)
+    uint64_t * last_bar = nullptr;                   // last committed MMA barrier and its parity (issuer)
+    uint32_t last_par = 0;
+    auto issue_k = [&]() {
+        const int st = k_issued % F_RS;
+        mbar_arrive_expect_tx(&bar_k[st], (uint32_t)kraww * FN);
+        tma_load_2d(sRK + st * F::RAW_STAGE, kmap, kx0, u.token_base + k_issued * FN, &bar_k[st]);
+        k_issued++;
+    };
+    auto issue_v = [&]() {
+        const int st = v_issued % F_RS;
+        mbar_arrive_expect_tx(&bar_v[st], (uint32_t)vraww * FN);
+        tma_load_2d(sRV + st * F::RAW_STAGE, vmap, vx0, u.token_base + v_issued * FN, &bar_v[st]);
+        v_issued++;
+    };
+    // shared-memory descriptors built once: an operand at byte offset o from
+    // a base is the base descriptor plus o >> 4 (the start-address field)
+    const uint64_t dA = sdesc(smem_u32(sA), 128, tc_cfg<128>::SBO);
+    const uint64_t dBK = sdesc(smem_u32(sBK), 128, tc_cfg<128>::SBO);
+    const uint64_t dP = sdesc(smem_u32(sP), 128, F::SBO_32);
+    const uint64_t dBV = sdesc(smem_u32(sBV), 128, F::SBO_32);
+    auto issue_score = [&](int t) {                 // S(t) into score set t & 1
+        const uint64_t b0 = dBK + (((t & 1) * F::BK_TILE) >> 4);
+        const uint32_t d0 = tmem + F::TM_S + (uint32_t)((t & 1) * F::NBLK * FN);
+#pragma unroll
+        for (int b = 0; b < F::NBLK; b++)
+#pragma unroll
+            for (int p = 0; p < TC_NPIECE; p++)
+#pragma unroll
+                for (int s = 0; s < 2; s++) {
+                    const uint32_t ko = (uint32_t)(4 * b + 2 * s) * 128;
+                    mma_f16(d0 + (uint32_t)(b * FN), dA + ((p * F::A_PIECE + ko) >> 4), b0 + (ko >> 4), IDESC_S,
+                            (p | s) != 0);
+                }
+        commit(&bar_s[t & 1]);
+        last_bar = &bar_s[t & 1];
+        last_par = (uint32_t)((t >> 1) & 1);
+    };
+    auto issue_y = [&](int t) {                     // O += P(t) V(t): hi*hi + hi*lo + lo*hi
+        const uint64_t pa = dP + (((t & 1) * 2 * F::P_PIECE) >> 4), vb = dBV + (((t % 3) * 2 * F::BV_PIECE) >> 4);
+#pragma unroll
+        for (int s = 0; s < FN / 16; s++) {
+            const uint32_t ko = ((uint32_t)s * 256) >> 4;
+            mma_f16(tmem + F::TM_O, pa + ko, vb + ko, IDESC_Y, (t | s) != 0);
+            mma_f16(tmem + F::TM_O, pa + ko, vb + (F::BV_PIECE >> 4) + ko, IDESC_Y, 1u);
+            mma_f16(tmem + F::TM_O, pa + (F::P_PIECE >> 4) + ko, vb + ko, IDESC_Y, 1u);
+        }
+        commit(&bar_y[t & 1]);
+        last_bar = &bar_y[t & 1];
+        last_par = (uint32_t)((t >> 1) & 1);
+    };
+
+    if (tid == F_ISSUER) {
+        while (k_issued < F_RS && k_issued < ntiles) issue_k();
+        while (v_issued < F_RS && v_issued < ntiles) issue_v();
+    }
+    load_query_pieces<128>(u, P, h, sA, rowc, tid);
+    bool ok = mbar_wait(&bar_k[0], 0u, polls);       // K tile 0
+    if (ok) convert_tile<128, KT, FN, TC_THREADS>(sRK, kraww, koff, sBK, sSC, tid);
+    fence_smem_to_async();
+    int err = __syncthreads_or(!ok) ? 1 : 0;
+    if (!err && tid == F_ISSUER) {
+        fence_after_sync();
+        if (k_issued < ntiles) issue_k();            // K slot 0 is free again
+        issue_score(0);
+    }
+
+    // Every thread owns 16 columns of one query row: row q = TMEM lane
+    // 32*(warp % 4) + lane, columns 16*ch .. 16*ch+15 of each 32-key tile
+    // (ch = warp / 4). The two threads of a row keep identical reference
+    // maxima (they see the same tile maxima) and partial sums l of their own
+    // columns; O's columns are split between them the same way (64 each).
+    const int lq = warp & 3, ch = warp >> 2, q = 32 * lq + (tid & 31);
+    float m_ref = -INFINITY, l = 0.0f, rmax = -INFINITY;
+    const float rc = rowc[q];
+    float * out = fs + u.s_off + (long long)h * nq * C;
+    const bool vec_out = ((C & 3) == 0) && ((((uintptr_t)out) & 15) == 0);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * lq) << 16);
+    float sv[16];
+    for (int i = 0; !err && i <= ntiles; i++) {
+        ok = true;
+        if (stall && i == 0) ok = mbar_wait(&bar_y[1], 0u, 64u);     // nothing completes this phase yet
+        // ---- phase A: scores of tile j = i-1 (16 per thread); K tile i+1 and V tile i into operands
+        const int j = i - 1, j0 = j * FN;
+        const int nv = i >= 1 ? min(FN, C - j0) : 0;
+        if (ok && i >= 1) {
+            const int bj = j & 1;
+            ok = mbar_wait(&bar_s[bj], (uint32_t)((j >> 1) & 1), polls);
+            if (ok) {
+                fence_after_sync();
+                const float * scb = sSC + (j % 3) * F::NBLK * FN + 16 * ch;
+                uint32_t acc[F::NBLK][16];
+#pragma unroll
+                for (int b = 0; b < F::NBLK; b++)
+                    tmem_ld16_nowait(lane_base + F::TM_S + (uint32_t)(bj * F::NBLK * FN + b * FN + 16 * ch), acc[b]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e4 = 0; e4 < 4; e4++) {
+                    float4 sc[F::NBLK];
+#pragma unroll
+                    for (int b = 0; b < F::NBLK; b++) sc[b] = *reinterpret_cast<const float4 *>(scb + b * FN + 4 * e4);
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float s0 = e == 0 ? sc[0].x : (e == 1 ? sc[0].y : (e == 2 ? sc[0].z : sc[0].w));
+                        float x = __fmul_rn(__uint_as_float(acc[0][4 * e4 + e]), s0);
+#pragma unroll
+                        for (int b = 1; b < F::NBLK; b++) {
+                            const float sb = e == 0 ? sc[b].x : (e == 1 ? sc[b].y : (e == 2 ? sc[b].z : sc[b].w));
+                            x = __fmaf_rn(__uint_as_float(acc[b][4 * e4 + e]), sb, x);
+                        }
+                        sv[4 * e4 + e] = __fmul_rn(x, rc);
+                    }
+                }
+                const int c0 = 16 * ch;                  // this thread's first column of the tile
+                if (q < nq) {
+                    float * dst = out + (long long)q * C + j0 + c0;
+                    if (c0 + 16 <= nv && vec_out) {
+#pragma unroll
+                        for (int e4 = 0; e4 < 4; e4++)
+                            reinterpret_cast<float4 *>(dst)[e4] =
+                                make_float4(sv[4 * e4], sv[4 * e4 + 1], sv[4 * e4 + 2], sv[4 * e4 + 3]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; e++)
+                            if (c0 + e < nv) dst[e] = sv[e];
+                    }
+                }
+                float tm = -INFINITY;
+#pragma unroll
+                for (int e = 0; e < 16; e++)
+                    if (c0 + e < nv) tm = fmaxf(tm, sv[e]);
+                s_tmax[ch][q] = tm;
+            }
+        }
+        if (ok && i + 1 < ntiles) {                      // K tile i+1 into K buffer (i+1) & 1 (last read by S(i-1))
+            const int t = i + 1, st = t % F_RS;
+            ok = mbar_wait(&bar_k[st], (uint32_t)((t / F_RS) & 1), polls);
+            if (ok && i >= 1) ok = mbar_wait(&bar_s[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), polls);
+            if (ok)
+                convert_tile<128, KT, FN, TC_THREADS>(sRK + st * F::RAW_STAGE, kraww, koff, sBK + (t & 1) * F::BK_TILE,
+                                                      sSC + (t % 3) * F::NBLK * FN, tid);
+        }
+        if (ok && i < ntiles) {                          // V tile i into V buffer i % 3 (last read by the MMAs of tile i-3)
+            const int st = i % F_RS;
+            ok = mbar_wait(&bar_v[st], (uint32_t)((i / F_RS) & 1), polls);
+            if (ok && i >= 3) ok = mbar_wait(&bar_y[(i - 3) & 1], (uint32_t)(((i - 3) >> 1) & 1), polls);
+            if (ok) convert_v_tile<VT>(sRV + st * F::RAW_STAGE, vraww, voff, sBV + (i % 3) * 2 * F::BV_PIECE, tid,
+                                       min(FN, C - i * FN));
+        }
+        fence_smem_to_async();
+        if (__syncthreads_or(!ok)) {
+            err = 1;
+            break;
+        }
+        // ---- phase B: the row's reference maximum, O's rescale, P of tile j
+        if (i >= 1) {
+            const float tm = fmaxf(s_tmax[0][q], s_tmax[1][q]);
+            rmax = fmaxf(rmax, tm);
+            if (tm > m_ref + F_TAU) {                    // move the reference maximum (first tile: set it)
+                if (j >= 1) {                            // O holds P V of tiles 0..j-1: scale it (and l)
+                    ok = mbar_wait(&bar_y[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), polls);
+                    if (ok) {
+                        fence_after_sync();
+                        const float f = __expf(__fsub_rn(m_ref, tm));
+                        l = __fmul_rn(l, f);
+#pragma unroll
+                        for (int c = 0; c < 64; c += 16) {
+                            uint32_t o[16];
+                            tmem_ld16_nowait(lane_base + F::TM_O + (uint32_t)(64 * ch + c), o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__fmul_rn(__uint_as_float(o[e]), f));
+                            tmem_st16(lane_base + F::TM_O + (uint32_t)(64 * ch + c), o);
+                        }
+                        tmem_wait_st();
+                    }
+                }
+                m_ref = tm;
+            }
+            // P = exp(S - m_ref) into P buffer j & 1 (last read by the MMAs of tile j-2)
+            if (ok && j >= 2) ok = mbar_wait(&bar_y[j & 1], (uint32_t)(((j - 2) >> 1) & 1), polls);
+            if (ok) {
+                const int c0 = 16 * ch;
+                uint8_t * pb = sP + (j & 1) * 2 * F::P_PIECE + (q >> 3) * F::SBO_32 + (q & 7) * 16;
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    uint32_t p1[4], p2[4];
+#pragma unroll
+                    for (int e = 0; e < 8; e += 2) {
+                        const int k = 8 * c + e;
+                        const float x0 = c0 + k < nv ? __expf(__fsub_rn(sv[k], m_ref)) : 0.0f;
+                        const float x1 = c0 + k + 1 < nv ? __expf(__fsub_rn(sv[k + 1], m_ref)) : 0.0f;
+                        l = __fadd_rn(__fadd_rn(l, x0), x1);
+                        const __half2 hi = __floats2half2_rn(x0, x1);
+                        const float2 hf = __half22float2(hi);
+                        const __half2 lo = __floats2half2_rn(__fsub_rn(x0, hf.x), __fsub_rn(x1, hf.y));
+                        p1[e >> 1] = *reinterpret_cast<const uint32_t *>(&hi);
+                        p2[e >> 1] = *reinterpret_cast<const uint32_t *>(&lo);
+                    }
+                    *reinterpret_cast<uint4 *>(pb + (2 * ch + c) * 128) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+                    *reinterpret_cast<uint4 *>(pb + F::P_PIECE + (2 * ch + c) * 128) =
+                        make_uint4(p2[0], p2[1], p2[2], p2[3]);
+                }
+            }
+        }
+        fence_before_sync();
+        fence_smem_to_async();
+        if (__syncthreads_or(!ok)) {
+            err = 1;
+            break;
+        }
+        if (tid == F_ISSUER) {
+            fence_after_sync();
+            if (i + 1 < ntiles && k_issued < ntiles) issue_k();     // the slot of K tile i+1
+            if (i < ntiles && v_issued < ntiles) issue_v();         // the slot of V tile i
+            if (i + 1 < ntiles) issue_score(i + 1);
+            if (i >= 1) issue_y(i - 1);
+        }
+    }
+
+    if (!err) {                                          // Y = O / (l of both halves of the row)
+        s_l[ch][q] = l;
+        __syncthreads();
+        const int last = ntiles - 1;
+        const bool okw = mbar_wait(&bar_y[last & 1], (uint32_t)((last >> 1) & 1), TC_POLLS);
+        if (okw) {
+            fence_after_sync();
+            const float inv = __fdiv_rn(1.0f, __fadd_rn(s_l[0][q], s_l[1][q]));
+            float * y = fs + u.y_off + ((long long)h * nq + q) * 128 + 64 * ch;
+#pragma unroll
+            for (int c = 0; c < 64; c += 16) {
+                uint32_t o[16];
+                tmem_ld16_nowait(lane_base + F::TM_O + (uint32_t)(64 * ch + c), o);
+                tmem_wait_ld();
+                if (q < nq)
+#pragma unroll
+                    for (int e4 = 0; e4 < 4; e4++)
+                        reinterpret_cast<float4 *>(y + c)[e4] =
+                            make_float4(__fmul_rn(__uint_as_float(o[4 * e4]), inv), __fmul_rn(__uint_as_float(o[4 * e4 + 1]), inv),
+                                        __fmul_rn(__uint_as_float(o[4 * e4 + 2]), inv), __fmul_rn(__uint_as_float(o[4 * e4 + 3]), inv));
+            }
+            if (mode == 2 && ch == 0 && q < nq) {
+                const int ntile_alloc = (C + 127) / 128;
+                fs[u.pm_off + (long long)h * nq * ntile_alloc + (long long)q * ntile_alloc] = rmax;
+            }
+        } else {
+            atomicCAS(&g_score_tc_error, 0, 211);
+        }
+    }
+    if (err && tid == F_ISSUER) {                    // wait (bounded) for the copies and MMAs in flight
+        for (int t = max(0, k_issued - F_RS); t < k_issued; t++)
+            mbar_wait(&bar_k[t % F_RS], (uint32_t)((t / F_RS) & 1), TC_POLLS);
+        for (int t = max(0, v_issued - F_RS); t < v_issued; t++)
+            mbar_wait(&bar_v[t % F_RS], (uint32_t)((t / F_RS) & 1), TC_POLLS);
+        if (last_bar) mbar_wait(last_bar, last_par, TC_POLLS);
+        atomicCAS(&g_score_tc_error, 0, 210);
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tmem_free(tmem, F::TMEM_COLS);
+}
+
+bool kvc_score_pv_tc_ok(int dk, int dv, int max_nq, const kvc_score_tc_geom & kg, int v_type, size_t v_row_bytes,
+                        const void * v_base, int H, kvc_score_tc_geom * vg) {
+    // opt-in: measured slower than the separate scoring and refit-target
+    // kernels on cfg4 (7.6 ms against 3.0 + 3.4 ms per step)
+    if (getenv("KVC_FUSED_PV") == nullptr) return false;
+    if (dk != 128 || dv != 128 || max_nq > TC_M || kg.k_type < 0) return false;
+    if (v_type != 8 && v_type != 2) return false;
+    kvc_score_tc_geom g;
+    if (!kvc_score_tc_ok(v_type, v_row_bytes, v_base, H, dv, max_nq, &g)) return false;
+    if (vg) *vg = g;
+    return true;
+}
+
+template <int KT, int VT>
+static int launch_fused(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,
+                        const void * kmaps, const void * vmaps, const kvc_score_tc_geom & kg,
+                        const kvc_score_tc_geom & vg, int mode, cudaStream_t st) {
+    const uint32_t sm = fcfg::SMEM;
+    KVC_CUDA(cudaFuncSetAttribute(k_score_pv_tc<KT, VT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    k_score_pv_tc<KT, VT><<<dim3(P.H, n_units), TC_THREADS, sm, st>>>(
+        d_units, P, fs, reinterpret_cast<const CUtensorMap *>(kmaps), reinterpret_cast<const CUtensorMap *>(vmaps),
+        kg.seg, kg.raww, vg.seg, vg.raww, mode, TC_POLLS, tc_stall());
+    KVC_CUDA(cudaGetLastError());
+    return KVC_OK;
+}
+
+int kvc_launch_score_pv_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev & P, float * fs,
+                           const void * d_kmaps, const void * d_vmaps, const kvc_score_tc_geom & kg,
+                           const kvc_score_tc_geom & vg, int mode, cudaStream_t st) {
+    if (n_units <= 0) return KVC_OK;
+    if (P.dk != 128 || P.dv != 128) return KVC_ERR_SHAPE;
+#define KVC_FUSED(KT, VT)                                                                                     \
+    if (kg.k_type == KT && vg.k_type == VT)                                                                   \
+        return launch_fused<KT, VT>(d_units, n_units, P, fs, d_kmaps, d_vmaps, kg, vg, mode, st);
+    KVC_FUSED(8, 8) KVC_FUSED(8, 2) KVC_FUSED(2, 8) KVC_FUSED(2, 2) KVC_FUSED(1, 8) KVC_FUSED(1, 2)
+#undef KVC_FUSED
+    return KVC_ERR_SHAPE;
 }

@@ -140,6 +140,18 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t * r) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 16 consecutive fp32 columns into this thread's TMEM lane (then tmem_wait_st
+// before the values are relied on).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t * r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+        :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Arm the mbarrier for one arrival (this thread's) plus `bytes` of
 // asynchronous-copy transactions.
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * mbar, uint32_t bytes) {

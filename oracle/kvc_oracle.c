@@ -781,6 +781,13 @@ void oracle_trace_importance(float * buf, int cap) {
 }
 int oracle_trace_len(void) { return g_trace_len; }
 
+/* Test aid: with `on`, the next calls stop after the key selection (indices
+ * only; beta and C_v zero, stats zero), for shapes whose refit the oracle
+ * would take minutes to solve while the parity tests need only the
+ * selection and the traced importances. */
+static int g_select_only = 0;
+void oracle_select_only(int on) { g_select_only = on; }
+
 /* beta for one head: w from NNLS on exp-scores, beta = log(max(1e-12, w))
  * (src/kv-compact-api.cpp:812-831). */
 static void orc_beta_head(const float * E, const float * rs, const int * sel, int nq, int T,
@@ -912,6 +919,19 @@ static int orc_compact_body(const float * K, const float * V, const float * Q, i
     }
     double t_score = orc_now_ms() - t0;
     double t1 = orc_now_ms();
+    if (g_select_only) {
+        orc_result_alloc(res, t, H, dv);
+        memcpy(res->selected_indices, sel, (size_t)t * sizeof(int));
+        for (int h = 0; h < H; h++) {
+            memset(res->beta[h], 0, (size_t)t * 4);
+            memset(res->C_v[h], 0, (size_t)t * dv * 4);
+        }
+        memset(&res->stats, 0, sizeof(res->stats));
+        for (int h = 0; h < H; h++) { free(S[h]); free(A[h]); free(E[h]); free(RS[h]); free(pimp[h]); }
+        free(S); free(A); free(E); free(RS); free(pimp);
+        free(gimp); free(himp); free(sens); free(sel); free(omp_w);
+        return 0;
+    }
 
     /* Y_h = A_h V_h with sequential sums over T (math.h:70-80) */
     float ** Y = (float **)malloc((size_t)H * sizeof(float *));

@@ -34,6 +34,8 @@ def oracle():
         pytest.fail("oracle/liboracle.so missing: run `make -C oracle oracle`")
     lib = ctypes.CDLL(ORACLE_PATH, mode=ctypes.RTLD_LOCAL)
     fns = abi.bind(lib, prefix="oracle_")
+    lib.oracle_select_only.restype = None
+    lib.oracle_select_only.argtypes = [ctypes.c_int]
     fns["_lib"] = lib
     return fns
 

@@ -170,12 +170,18 @@ def test_reference_api_suite_on_libkvc():
     assert "All tests passed!" in p.stdout
 
 
-@pytest.mark.parametrize("typ", [abi.KV_TYPE_Q8_0, abi.KV_TYPE_Q4_0, abi.KV_TYPE_F16], ids=["q8_0", "q4_0", "f16"])
-def test_tensor_core_scores_match_exact_mode(kvc, reference, oracle_traced, monkeypatch, typ):
+@pytest.mark.parametrize("typ,fused", [(abi.KV_TYPE_Q8_0, False), (abi.KV_TYPE_Q4_0, False), (abi.KV_TYPE_F16, False),
+                                       (abi.KV_TYPE_Q8_0, True), (abi.KV_TYPE_Q4_0, True)],
+                         ids=["q8_0", "q4_0", "f16", "q8_0_fused", "q4_0_fused"])
+def test_tensor_core_scores_match_exact_mode(kvc, reference, oracle_traced, monkeypatch, typ, fused):
     """Scores from K's block bytes on the tensor cores (the default) against
     the bit-exact SIMT scoring (KVC_EXACT_SCORES=1): the exact mode still
     selects the reference's keys bit for bit, and the tensor-core mode selects
-    them too, except near-ties (< parity.NEAR_TIE_REL relative importance gap)."""
+    them too, except near-ties (< parity.NEAR_TIE_REL relative importance gap).
+    `fused`: the opt-in kernel that also forms the refit target Y = A V in the
+    scoring pass (KVC_FUSED_PV=1)."""
+    if fused:
+        monkeypatch.setenv("KVC_FUSED_PV", "1")
     T, H, d, nq = 12_800, 8, 128, 128
     K, V, Q = workloads.small_case(300 + typ, T, nq, H, d, "rope")
     Kq, Vq = abi.quantize_rows(kvc, K, typ), abi.quantize_rows(kvc, V, typ)
@@ -189,6 +195,8 @@ def test_tensor_core_scores_match_exact_mode(kvc, reference, oracle_traced, monk
     rc, exact = abi.run_quantized(kvc, *args, abi.make_params(kvc, **pk))
     assert rc == 0
     monkeypatch.delenv("KVC_EXACT_SCORES")
+    if fused:                                   # the refit targets of the two paths agree (C_v through them)
+        assert parity.rel_l2(tc["C_v"], exact["C_v"]) < 1e-4
     np.testing.assert_array_equal(exact["indices"], theirs["indices"])
     np.testing.assert_array_equal(exact["K_out"], theirs["K_out"])
     units = parity.plan_units(T, pk)

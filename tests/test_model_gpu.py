@@ -358,3 +358,40 @@ def test_full_size_cfg4_properties(kvc):
         st = model.stats(l)
         print(f"\nfull-size layer {l}: stats {st}")
         assert 0.9 < st["avg_cosine_sim"] <= 1.0001, st
+
+
+def test_large_unchunked_solve(kvc, oracle):
+    """An unchunked call whose least-squares system has 4,096 unknowns
+    (min(n_q, t) = 4096 > 3,072, the former limit): T = 8,192, explicit
+    n_q = 4,096 queries, 50% (t = 4,096), chunk_size = -1. The reference
+    solves any size by Gaussian elimination (include/kv-compact-math.h:463-557);
+    here the global-memory Cholesky takes it. Indices against the oracle's
+    selection (its refit skipped: minutes at this size), C_v against the fp64
+    solve of the same ridge system."""
+    T, H, d, nq = 8192, 1, 128, 4096
+    rng = np.random.default_rng(4096)
+    K = workloads.lowrank_keys(rng, T, H, d)
+    V = rng.standard_normal((T, H * d)).astype(np.float32)
+    Q = rng.standard_normal((nq, H * d)).astype(np.float32)
+    pk = dict(target_ratio=0.5, chunk_size=-1)
+    rc, ours = abi.run_compact(kvc, K, V, Q, nq, H, d, d, abi.make_params(kvc, **pk))
+    assert rc == 0
+    assert ours["t"] == 4096
+    lib = oracle["_lib"]
+    lib.oracle_select_only(1)
+    got = []
+    try:
+        imp = trace_importance(oracle, lambda: got.append(abi.run_compact(oracle, K, V, Q, nq, H, d, d,
+                                                                            abi.make_params(oracle, **pk))))(T)
+        rc, theirs = got[0]
+    finally:
+        lib.oracle_select_only(0)
+    assert rc == 0 and theirs["t"] == 4096
+    units = parity.plan_units(T, pk)
+    n_ties = check_indices(ours["indices"], theirs["indices"], imp, units)
+    ex = parity.exact_cv(K, V, Q, H, d, ours["indices"], np.zeros((H, 4096), np.float32), units, pk, False)
+    e = parity.rel_l2(ours["C_v"], ex)
+    print(f"\n4,096-unknown solve: {n_ties} near-tie swaps; C_v rel-L2 vs fp64 {e:.2e}; "
+          f"cosine {ours['stats']['avg_cosine_sim']:.6f}")
+    assert e <= parity.CV_REL_TOL
+    assert np.all(np.isfinite(ours["C_v"]))
