@@ -45,7 +45,8 @@ namespace {
 constexpr int TC_M = 128;          // query rows of a tile (TMEM lanes)
 constexpr int TC_N = 64;           // keys per tile
 constexpr int TC_RS = 4;           // raw K tiles in flight
-constexpr int TC_THREADS = 256;
+constexpr int TC_THREADS = 256;   // the fused kernel's CTA
+constexpr int SC_THREADS = 512;   // k_score_tc's CTA: four warps per TMEM lane quarter
 constexpr int TC_NPIECE = 2;       // fp16 pieces of each scaled query value
 constexpr int FN = 32;             // keys per tile of the fused scoring + refit-target kernel
 constexpr uint32_t TC_RAW_MAX = 256;        // raw bytes per key row of a head, at most (the TMA box width)
@@ -63,11 +64,15 @@ struct tc_cfg {
     static constexpr uint32_t RAW_STAGE = TC_N * TC_RAW_MAX;
     static constexpr uint32_t OFF_A = 0;
     static constexpr uint32_t OFF_B = OFF_A + TC_NPIECE * A_PIECE;
-    static constexpr uint32_t OFF_RAW = OFF_B + 2 * B_TILE;
+    static constexpr uint32_t OFF_RAW = OFF_B + 3 * B_TILE;      // three operand buffers
     static constexpr uint32_t OFF_SC = OFF_RAW + TC_RS * RAW_STAGE;
-    static constexpr uint32_t OFF_ROWC = OFF_SC + 2 * NBLK * TC_N * 4;
+    static constexpr uint32_t OFF_ROWC = OFF_SC + 4 * NBLK * TC_N * 4;   // four scale buffers
     static constexpr uint32_t OFF_RED = OFF_ROWC + TC_M * 4;
-    static constexpr uint32_t SMEM = OFF_RED + 2 * TC_M * 4;
+    // score staging of the bulk stores: 256 epilogue threads x 32 scores,
+    // 144 bytes apart (16-byte writes of 8 consecutive threads hit distinct banks)
+    static constexpr uint32_t STG_LD = 144;
+    static constexpr uint32_t OFF_STG = OFF_RED + 2 * TC_M * 4;
+    static constexpr uint32_t SMEM = OFF_STG + 256 * STG_LD;
     static constexpr uint32_t TMEM_COLS = 2 * NBLK * TC_N;  // two accumulator sets
 };
 
@@ -153,34 +158,37 @@ __device__ __forceinline__ void convert_tile(const uint8_t * raw, int raww, int 
 
 // The A operand: the query rows of head h (rows >= n_q zero), each scaled by
 // 2^e (max |Q| in [2^14, 2^15)) and split in two fp16 pieces, in the K-major
-// canonical layout; rowc[r] = 2^-e / sqrt(d_k). 256 threads, two per row.
-template <int DK>
+// canonical layout; rowc[r] = 2^-e / sqrt(d_k). NTHR threads (256 or 512),
+// NTHR / 128 consecutive threads per row.
+template <int DK, int NTHR = TC_THREADS>
 __device__ __forceinline__ void load_query_pieces(const kvc_unit & u, const kvc_params_dev & P, int h, uint8_t * sA,
                                                   float * rowc, int tid) {
     using CF = tc_cfg<DK>;
+    constexpr int TPR = NTHR / TC_M, PER = DK / TPR;   // threads per row, values per thread
     const int nq = u.nq, C = u.C;
     {
-        const int r = tid >> 1, hf = tid & 1;       // two threads per row, DK/2 values each
+        const int r = tid / TPR, hf = tid % TPR;
         const int ek = P.H * DK;
         const float * qp = nullptr;
         if (r < nq)
             qp = (u.qmode == 0 ? u.Q + (long long)r * ek : u.K + (long long)cheap_pos_tc(r, u.nq, C) * ek) +
-                 (long long)h * DK + hf * (DK / 2);
-        float v[DK / 2];
+                 (long long)h * DK + hf * PER;
+        float v[PER];
         float mx = 0.0f;
         if (qp && ((((uintptr_t)qp) & 15) == 0)) {
 #pragma unroll
-            for (int i = 0; i < DK / 2; i += 4) {
+            for (int i = 0; i < PER; i += 4) {
                 const float4 t = *reinterpret_cast<const float4 *>(qp + i);
                 v[i] = t.x; v[i + 1] = t.y; v[i + 2] = t.z; v[i + 3] = t.w;
             }
         } else {
 #pragma unroll
-            for (int i = 0; i < DK / 2; i++) v[i] = qp ? qp[i] : 0.0f;
+            for (int i = 0; i < PER; i++) v[i] = qp ? qp[i] : 0.0f;
         }
 #pragma unroll
-        for (int i = 0; i < DK / 2; i++) mx = fmaxf(mx, fabsf(v[i]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        for (int i = 0; i < PER; i++) mx = fmaxf(mx, fabsf(v[i]));
+#pragma unroll
+        for (int o = 1; o < TPR; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         int sh = 0;                                  // max |Q * 2^sh| in [2^14, 2^15)
         if (mx > 0.0f && mx <= 3.0e38f) {
             int ex;
@@ -191,8 +199,8 @@ __device__ __forceinline__ void load_query_pieces(const kvc_unit & u, const kvc_
         const float up = __int_as_float((127 + sh) << 23), down = __int_as_float((127 - sh) << 23);
         if (hf == 0) rowc[r] = __fmul_rn(P.isd, down);
 #pragma unroll
-        for (int c = 0; c < DK / 16; c++) {
-            const int kc = hf * (DK / 16) + c;       // 16-byte chunk along d
+        for (int c = 0; c < PER / 8; c++) {
+            const int kc = hf * (PER / 8) + c;       // 16-byte chunk along d
             uint32_t p1[4], p2[4];
 #pragma unroll
             for (int e = 0; e < 4; e++) {
@@ -212,22 +220,42 @@ __device__ __forceinline__ void load_query_pieces(const kvc_unit & u, const kvc_
 }
 }  // namespace
 
-// One CTA per (unit = blockIdx.y, head = blockIdx.x). maps[u.layer]: the 2-D
-// TMA map of the layer's K rows (bytes x rows); `seg` = bytes of one head in a
-// row, `raww` = TMA box width in bytes (covers any head's bytes from the
-// 16-byte boundary below them). mode 2 also writes each row's maximum score
-// (pm slot 0 of the row: one tile spanning the whole chunk).
+// One CTA per (unit = blockIdx.y, head = blockIdx.x), warp-specialised, no
+// CTA-wide barrier inside the key loop:
+//   warp 0 (one thread)  TMA loads of the raw K tiles into a ring of TC_RS
+//                        stages (raw_full / raw_empty mbarriers);
+//   warp 1 (one thread)  the MMAs of tile i into TMEM accumulator set i & 1
+//                        once its operand (b_full) and the set (acc_empty)
+//                        are ready; commits to acc_full and b_empty;
+//   warps 4-7            convert raw tile i into operand buffer i % 2 (fp16
+//                        codes + block scales), once the MMAs (b_empty) and the
+//                        epilogue (sc_empty) of tile i-2 are done with it;
+//   warps 8-15           the epilogue: TMEM -> registers (then acc_empty), the
+//                        block scales (then sc_empty), 16-byte stores of S,
+//                        running row maxima. Warp 8+e reads TMEM lanes
+//                        32*(e%4).. and 32 columns from 32*(e/4).
+// maps[u.layer]: the 2-D TMA map of the layer's K rows (bytes x rows); `seg`
+// = bytes of one head in a row, `raww` = TMA box width in bytes (covers any
+// head's bytes from the 16-byte boundary below them). mode 2 also writes each
+// row's maximum score (pm slot 0 of the row: one tile spanning the chunk).
+// Every wait is bounded; a role whose wait runs out raises the CTA's error
+// flag, every role stops at its next check, the loads and MMAs in flight are
+// awaited (full bound), TMEM is freed and the error goes to the host.
 template <int DK, int KT>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __restrict__ units, kvc_params_dev P,
+__global__ void __launch_bounds__(SC_THREADS, 1) k_score_tc(const kvc_unit * __restrict__ units, kvc_params_dev P,
                                                             float * __restrict__ fs,
                                                             const CUtensorMap * __restrict__ maps, int seg, int raww,
                                                             int mode, uint32_t polls, int stall) {
     using namespace kvc_tc;
     using CF = tc_cfg<DK>;
+    constexpr int NB = 3;                            // operand buffers (fp16 codes), released by the MMAs
+    constexpr int NSC = 4;                           // scale buffers, released by the epilogue
     extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bar_tma[TC_RS];
-    __shared__ __align__(8) uint64_t bar_mma[2];
+    __shared__ __align__(8) uint64_t raw_full[TC_RS], raw_empty[TC_RS];
+    __shared__ __align__(8) uint64_t b_full[NB], b_empty[NB], sc_empty[NSC];
+    __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
+    __shared__ volatile int s_err;
     const kvc_unit u = units[blockIdx.y];
     if (!u.active) return;
     const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -243,156 +271,197 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_score_tc(const kvc_unit * __r
     float * rowc = reinterpret_cast<float *>(smem + CF::OFF_ROWC);
     float * red = reinterpret_cast<float *>(smem + CF::OFF_RED);
 
-    if (warp == 0) tmem_alloc(&tmem_slot, CF::TMEM_COLS);
+    if (warp == 1) tmem_alloc(&tmem_slot, CF::TMEM_COLS);
     if (tid == 0) {
-        for (int s = 0; s < TC_RS; s++) mbar_init(&bar_tma[s], 1);
-        mbar_init(&bar_mma[0], 1);
-        mbar_init(&bar_mma[1], 1);
+        for (int s = 0; s < TC_RS; s++) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], 4);             // one arrival per converter warp
+        }
+        for (int s = 0; s < NB; s++) {
+            mbar_init(&b_full[s], 4);
+            mbar_init(&b_empty[s], 1);               // the MMA commit
+        }
+        for (int s = 0; s < NSC; s++) mbar_init(&sc_empty[s], 8);   // one arrival per epilogue warp
+        for (int s = 0; s < 2; s++) {
+            mbar_init(&acc_full[s], 1);
+            mbar_init(&acc_empty[s], 8);
+        }
+        s_err = 0;
         mbar_init_fence();
     }
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = tmem_slot;
-    int issued = 0;                                  // raw tiles whose load was issued (thread 0)
-    if (tid == 0) {
+    int issued = 0;                                  // raw tiles loaded (producer)
+    int committed = -1;                              // last tile whose MMAs were committed (issuer)
+    if (tid == 0)                                    // the first stages load while the queries convert
         for (; issued < TC_RS && issued < ntiles; issued++) {
-            mbar_arrive_expect_tx(&bar_tma[issued], raw_bytes);
-            tma_load_2d(sRaw + issued * CF::RAW_STAGE, map, x0, u.token_base + issued * TC_N, &bar_tma[issued]);
+            mbar_arrive_expect_tx(&raw_full[issued], raw_bytes);
+            tma_load_2d(sRaw + issued * CF::RAW_STAGE, map, x0, u.token_base + issued * TC_N, &raw_full[issued]);
         }
-    }
-
-    load_query_pieces<DK>(u, P, h, sA, rowc, tid);
+    load_query_pieces<DK, SC_THREADS>(u, P, h, sA, rowc, tid);
     fence_smem_to_async();
     __syncthreads();
 
-    constexpr uint32_t IDESC = idesc_f16(TC_M, TC_N);
-    const int lq = warp & 3, ch = warp >> 2, q = 32 * lq + lane;
-    const float rc = rowc[q];
-    float rmax = -INFINITY;
-    float * out = fs + u.s_off + (long long)h * nq * C;
-    const bool vec_out = ((C & 3) == 0) && ((((uintptr_t)out) & 15) == 0);
-    int err = 0, committed = -1, waited_tma = 0;
-    for (int i = 0; i <= ntiles; i++) {
-        bool ok = true;
-        if (stall && i == 0) ok = mbar_wait(&bar_mma[1], 0u, 64u);   // nothing completes this phase yet
-        if (ok && i < ntiles) ok = mbar_wait(&bar_tma[i % TC_RS], (uint32_t)((i / TC_RS) & 1), polls);
-        if (i >= 1) ok = ok && mbar_wait(&bar_mma[(i - 1) & 1], (uint32_t)(((i - 1) >> 1) & 1), polls);
-        if (__syncthreads_or(!ok)) {                 // the same decision in every thread
-            err = 1;
-            break;
-        }
-        fence_after_sync();
-        if (i < ntiles) {
-            waited_tma = i + 1;
-            convert_tile<DK, KT>(sRaw + (i % TC_RS) * CF::RAW_STAGE, raww, off, sB + (i & 1) * CF::B_TILE,
-                                 sSC + (i & 1) * CF::NBLK * TC_N, tid);
-            fence_smem_to_async();
-        }
-        __syncthreads();                             // B(i) ready, raw stage of tile i free
-        if (tid == 0 && i < ntiles) {
-            if (issued < ntiles) {                   // the tile TC_RS ahead into the freed stage
-                const int st = issued % TC_RS;
-                mbar_arrive_expect_tx(&bar_tma[st], raw_bytes);
-                tma_load_2d(sRaw + st * CF::RAW_STAGE, map, x0, u.token_base + issued * TC_N, &bar_tma[st]);
-                issued++;
+    auto fail = [&]() { s_err = 1; };
+    if (warp == 0) {
+        // ---- TMA producer
+        if (lane == 0)
+            for (; issued < ntiles && !s_err; issued++) {
+                const int s = issued % TC_RS, use = issued / TC_RS;
+                if (!mbar_wait_backoff(&raw_empty[s], (uint32_t)((use - 1) & 1), polls, 64)) { fail(); break; }
+                mbar_arrive_expect_tx(&raw_full[s], raw_bytes);
+                tma_load_2d(sRaw + s * CF::RAW_STAGE, map, x0, u.token_base + issued * TC_N, &raw_full[s]);
             }
-            fence_after_sync();
-            // descriptors: base + (byte offset >> 4) in the start-address field
-            const uint64_t a0 = sdesc(smem_u32(sA), 128, CF::SBO), b0 = sdesc(smem_u32(sB + (i & 1) * CF::B_TILE), 128, CF::SBO);
-            const uint32_t d0 = tmem + (uint32_t)((i & 1) * CF::NBLK * TC_N);
+    } else if (warp == 1) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t IDESC = idesc_f16(TC_M, TC_N);
+            const uint64_t a0 = sdesc(smem_u32(sA), 128, CF::SBO), bd = sdesc(smem_u32(sB), 128, CF::SBO);
+            for (int i = 0; i < ntiles && !s_err; i++) {
+                const int b = i % NB, a = i & 1;
+                bool ok = mbar_wait_backoff(&b_full[b], (uint32_t)((i / NB) & 1), polls, 32);
+                if (ok && i >= 2) ok = mbar_wait_backoff(&acc_empty[a], (uint32_t)(((i >> 1) - 1) & 1), polls, 32);
+                if (!ok) { fail(); break; }
+                fence_after_sync();
+                const uint64_t b0 = bd + ((b * CF::B_TILE) >> 4);
+                const uint32_t d0 = tmem + (uint32_t)(a * CF::NBLK * TC_N);
 #pragma unroll
-            for (int b = 0; b < CF::NBLK; b++)
+                for (int blk = 0; blk < CF::NBLK; blk++)
 #pragma unroll
-                for (int p = 0; p < TC_NPIECE; p++)
+                    for (int p = 0; p < TC_NPIECE; p++)
 #pragma unroll
-                    for (int s = 0; s < 2; s++) {
-                        const uint32_t ko = (uint32_t)(4 * b + 2 * s) * 128;
-                        mma_f16(d0 + (uint32_t)(b * TC_N), a0 + ((p * CF::A_PIECE + ko) >> 4), b0 + (ko >> 4), IDESC,
-                                (p | s) != 0);
-                    }
-            commit(&bar_mma[i & 1]);
+                        for (int s = 0; s < 2; s++) {
+                            const uint32_t ko = (uint32_t)(4 * blk + 2 * s) * 128;
+                            mma_f16(d0 + (uint32_t)(blk * TC_N), a0 + ((p * CF::A_PIECE + ko) >> 4), b0 + (ko >> 4),
+                                    IDESC, (p | s) != 0);
+                        }
+                commit(&acc_full[a]);
+                commit(&b_empty[b]);
+                committed = i;
+            }
         }
-        if (i < ntiles) committed = i;
-        if (i >= 1) {                                // epilogue of tile j = i - 1
-            const int j = i - 1, bj = j & 1, j0 = j * TC_N;
-            const float * scb = sSC + bj * CF::NBLK * TC_N;
-            const bool full = j0 + TC_N <= C;        // every column of the tile is a key of the chunk
+    } else if (warp >= 4 && warp < 8) {
+        // ---- converters: raw tile i -> operand buffer i % NB
+        const int ct = tid - 128;
+        for (int i = 0; i < ntiles && !s_err; i++) {
+            const int s = i % TC_RS, b = i % NB, ub = i / NB, c = i % NSC, uc = i / NSC;
+            bool ok = mbar_wait_backoff(&raw_full[s], (uint32_t)((i / TC_RS) & 1), polls, 64);
+            if (ok && ub >= 1) ok = mbar_wait_backoff(&b_empty[b], (uint32_t)((ub - 1) & 1), polls, 64);
+            if (ok && uc >= 1) ok = mbar_wait_backoff(&sc_empty[c], (uint32_t)((uc - 1) & 1), polls, 64);
+            if (!ok) { fail(); break; }
+            convert_tile<DK, KT, TC_N, 128>(sRaw + s * CF::RAW_STAGE, raww, off, sB + b * CF::B_TILE,
+                                            sSC + c * CF::NBLK * TC_N, ct);
+            fence_smem_to_async();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&raw_empty[s]);
+                mbar_arrive(&b_full[b]);
+            }
+        }
+    } else if (warp >= 8) {
+        // ---- epilogue
+        const int e = warp - 8, lq = e & 3, ch = e >> 2, q = 32 * lq + lane;
+        const float rc = rowc[q];
+        float rmax = -INFINITY;
+        float * out = fs + u.s_off + (long long)h * nq * C;
+        const bool vec_out = ((C & 3) == 0) && ((((uintptr_t)out) & 15) == 0);
+        uint8_t * stg = smem + CF::OFF_STG + (uint32_t)(tid - 256) * CF::STG_LD;   // this thread's 32 scores
+        for (int i = 0; i < ntiles && !s_err; i++) {
+            const int a = i & 1, j0 = i * TC_N;
+            bool ok = true;
+            // the epilogue itself arrives on acc_empty: its phase 0 cannot complete before tile 1
+            if (stall && i == 0) ok = mbar_wait(&acc_empty[1], 0u, 64u);
+            if (ok) ok = mbar_wait_backoff(&acc_full[a], (uint32_t)((i >> 1) & 1), polls, 32);
+            if (!ok) { fail(); break; }
+            fence_after_sync();
+            const float * scb = sSC + (i % NSC) * CF::NBLK * TC_N;
+            const bool full = j0 + TC_N <= C;
+            const bool bulk = full && vec_out && q < nq;  // the row's 32 scores go out as one bulk copy
+            if (bulk) bulk_wait_read<0>();               // the previous tile's copy has read the staging
 #pragma unroll
             for (int c16 = 0; c16 < 2; c16++) {
-                const int cb = ch * 32 + c16 * 16;
-                uint32_t acc[CF::NBLK][16];
+                const int cb = 32 * ch + 16 * c16;
+                uint32_t acc[1][CF::NBLK][16];
 #pragma unroll
-                for (int b = 0; b < CF::NBLK; b++)
-                    tmem_ld16_nowait(tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(bj * CF::NBLK * TC_N + b * TC_N + cb),
-                                     acc[b]);
+                for (int blk = 0; blk < CF::NBLK; blk++)
+                    tmem_ld16_nowait(tmem + ((uint32_t)(32 * lq) << 16) +
+                                         (uint32_t)(a * CF::NBLK * TC_N + blk * TC_N + cb),
+                                     acc[0][blk]);
                 tmem_wait_ld();
+                if (c16 == 1) {                          // every column of the set is in registers
+                    fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[a]);
+                }
                 float v[16];
 #pragma unroll
                 for (int e4 = 0; e4 < 4; e4++) {
                     float4 sc[CF::NBLK];
 #pragma unroll
-                    for (int b = 0; b < CF::NBLK; b++)
-                        sc[b] = *reinterpret_cast<const float4 *>(scb + b * TC_N + cb + 4 * e4);
+                    for (int blk = 0; blk < CF::NBLK; blk++)
+                        sc[blk] = *reinterpret_cast<const float4 *>(scb + blk * TC_N + cb + 4 * e4);
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float s0 = e == 0 ? sc[0].x : (e == 1 ? sc[0].y : (e == 2 ? sc[0].z : sc[0].w));
-                        float s = __fmul_rn(__uint_as_float(acc[0][4 * e4 + e]), s0);
+                    for (int x = 0; x < 4; x++) {
+                        const float s0 = x == 0 ? sc[0].x : (x == 1 ? sc[0].y : (x == 2 ? sc[0].z : sc[0].w));
+                        float sv = __fmul_rn(__uint_as_float(acc[0][0][4 * e4 + x]), s0);
 #pragma unroll
-                        for (int b = 1; b < CF::NBLK; b++) {
-                            const float sb = e == 0 ? sc[b].x : (e == 1 ? sc[b].y : (e == 2 ? sc[b].z : sc[b].w));
-                            s = __fmaf_rn(__uint_as_float(acc[b][4 * e4 + e]), sb, s);
+                        for (int blk = 1; blk < CF::NBLK; blk++) {
+                            const float sb = x == 0 ? sc[blk].x : (x == 1 ? sc[blk].y : (x == 2 ? sc[blk].z : sc[blk].w));
+                            sv = __fmaf_rn(__uint_as_float(acc[0][blk][4 * e4 + x]), sb, sv);
                         }
-                        v[4 * e4 + e] = __fmul_rn(s, rc);
+                        v[4 * e4 + x] = __fmul_rn(sv, rc);
                     }
                 }
-                // 16 consecutive scores of this thread's row: four 16-byte stores
-                if (q < nq) {
+                if (bulk) {
+#pragma unroll
+                    for (int e4 = 0; e4 < 4; e4++)
+                        reinterpret_cast<float4 *>(stg + 64 * c16)[e4] =
+                            make_float4(v[4 * e4], v[4 * e4 + 1], v[4 * e4 + 2], v[4 * e4 + 3]);
+                } else if (q < nq) {
                     float * dst = out + (long long)q * C + j0 + cb;
-                    if (full && vec_out) {
 #pragma unroll
-                        for (int e4 = 0; e4 < 4; e4++)
-                            reinterpret_cast<float4 *>(dst)[e4] =
-                                make_float4(v[4 * e4], v[4 * e4 + 1], v[4 * e4 + 2], v[4 * e4 + 3]);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 16; e++)
-                            if (j0 + cb + e < C) dst[e] = v[e];
-                    }
+                    for (int x = 0; x < 16; x++)
+                        if (j0 + cb + x < C) dst[x] = v[x];
                 }
                 if (full) {
 #pragma unroll
-                    for (int e = 0; e < 16; e++) rmax = fmaxf(rmax, v[e]);
+                    for (int x = 0; x < 16; x++) rmax = fmaxf(rmax, v[x]);
                 } else {
 #pragma unroll
-                    for (int e = 0; e < 16; e++)
-                        if (j0 + cb + e < C) rmax = fmaxf(rmax, v[e]);
+                    for (int x = 0; x < 16; x++)
+                        if (j0 + cb + x < C) rmax = fmaxf(rmax, v[x]);
                 }
             }
-            fence_before_sync();                     // TMEM reads done before the next barrier
+            if (bulk) {
+                fence_smem_to_async();                   // the staged scores, visible to the copy engine
+                bulk_store(out + (long long)q * C + j0 + 32 * ch, stg, 128);
+                bulk_commit();
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sc_empty[i % NSC]);   // the tile's scales are read
         }
-    }
-    if (err) {
-        // wait (bounded) for this CTA's loads and MMAs still in flight
-        if (tid == 0) {
-            for (int t = waited_tma; t < issued; t++)
-                mbar_wait(&bar_tma[t % TC_RS], (uint32_t)((t / TC_RS) & 1), TC_POLLS);
-            if (committed >= 0)
-                mbar_wait(&bar_mma[committed & 1], (uint32_t)((committed >> 1) & 1), TC_POLLS);
-            atomicCAS(&g_score_tc_error, 0, 200 + err);
-        }
-    } else {
+        bulk_wait<0>();                                  // every score store of this thread has completed
         red[ch * TC_M + q] = rmax;
-        __syncthreads();
-        if (mode == 2 && tid < TC_M && tid < nq) {
-            const int ntile_alloc = (C + 127) / 128;
-            fs[u.pm_off + (long long)h * nq * ntile_alloc + (long long)tid * ntile_alloc] =
-                fmaxf(red[tid], red[TC_M + tid]);
-        }
+    }
+    __syncthreads();
+    if (s_err) {
+        // wait (bounded) for this CTA's loads and MMAs still in flight
+        if (tid == 0)
+            for (int t = issued - TC_RS > 0 ? issued - TC_RS : 0; t < issued; t++)
+                mbar_wait(&raw_full[t % TC_RS], (uint32_t)((t / TC_RS) & 1), TC_POLLS);
+        if (tid == 32 && committed >= 0)
+            mbar_wait(&acc_full[committed & 1], (uint32_t)((committed >> 1) & 1), TC_POLLS);
+        if (tid == 0) atomicCAS(&g_score_tc_error, 0, 201);
+    } else if (mode == 2 && tid < TC_M && tid < nq) {
+        const int ntile_alloc = (C + 127) / 128;
+        fs[u.pm_off + (long long)h * nq * ntile_alloc + (long long)tid * ntile_alloc] =
+            fmaxf(red[tid], red[TC_M + tid]);
     }
     fence_before_sync();
     __syncthreads();
-    if (warp == 0) tmem_free(tmem, CF::TMEM_COLS);
+    if (warp == 1) tmem_free(tmem, CF::TMEM_COLS);
 }
 
 // ---------------------------------------------------------------------------
@@ -490,7 +559,7 @@ static int launch_tc(const kvc_unit * d_units, int n_units, const kvc_params_dev
                      int seg, int raww, int mode, cudaStream_t st) {
     const uint32_t sm = tc_cfg<DK>::SMEM;
     KVC_CUDA(cudaFuncSetAttribute(k_score_tc<DK, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    k_score_tc<DK, KT><<<dim3(P.H, n_units), TC_THREADS, sm, st>>>(
+    k_score_tc<DK, KT><<<dim3(P.H, n_units), SC_THREADS, sm, st>>>(
         d_units, P, fs, reinterpret_cast<const CUtensorMap *>(maps), seg, raww, mode, TC_POLLS, tc_stall());
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;

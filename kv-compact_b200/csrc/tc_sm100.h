@@ -152,6 +152,26 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t * r) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// One arrival on the mbarrier (release semantics at CTA scope).
+__device__ __forceinline__ void mbar_arrive(uint64_t * mbar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(mbar)) : "memory");
+}
+
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from this CTA's shared memory to global memory, in this thread's current
+// bulk group; bulk_commit closes the group, bulk_wait_read<N> waits until at
+// most N of this thread's groups still read their shared-memory source, and
+// bulk_wait<0> until every group has completed.
+__device__ __forceinline__ void bulk_store(void * gdst, const void * ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 :: "l"(gdst), "r"(smem_u32(ssrc)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group %0;" :: "n"(N) : "memory"); }
+
 // Arm the mbarrier for one arrival (this thread's) plus `bytes` of
 // asynchronous-copy transactions.
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * mbar, uint32_t bytes) {
@@ -167,6 +187,24 @@ __device__ __forceinline__ void tma_load_2d(void * dst, const void * tmap, int x
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
         :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(mbar)) : "memory");
+}
+
+// The same wait for a role that may wait long (a producer ahead of its
+// consumer): after the first polls it sleeps `ns` nanoseconds between polls,
+// leaving the issue slots to the warps that have work. At most `limit` polls.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t * mbar, uint32_t parity, uint32_t limit, uint32_t ns) {
+    const uint32_t a = smem_u32(mbar);
+    for (uint32_t i = 0; i < limit; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+        if (i >= 4) __nanosleep(ns);
+    }
+    return false;
 }
 
 // Round an fp32 value to the nearest TF32 value (10 explicit mantissa bits,
