@@ -68,11 +68,7 @@ struct tc_cfg {
     static constexpr uint32_t OFF_SC = OFF_RAW + TC_RS * RAW_STAGE;
     static constexpr uint32_t OFF_ROWC = OFF_SC + 4 * NBLK * TC_N * 4;   // four scale buffers
     static constexpr uint32_t OFF_RED = OFF_ROWC + TC_M * 4;
-    // score staging of the bulk stores: 256 epilogue threads x 32 scores,
-    // 144 bytes apart (16-byte writes of 8 consecutive threads hit distinct banks)
-    static constexpr uint32_t STG_LD = 144;
-    static constexpr uint32_t OFF_STG = OFF_RED + 2 * TC_M * 4;
-    static constexpr uint32_t SMEM = OFF_STG + 256 * STG_LD;
+    static constexpr uint32_t SMEM = OFF_RED + 2 * TC_M * 4;
     static constexpr uint32_t TMEM_COLS = 2 * NBLK * TC_N;  // two accumulator sets
 };
 
@@ -231,7 +227,7 @@ __device__ __forceinline__ void load_query_pieces(const kvc_unit & u, const kvc_
 //                        codes + block scales), once the MMAs (b_empty) and the
 //                        epilogue (sc_empty) of tile i-2 are done with it;
 //   warps 8-15           the epilogue: TMEM -> registers (then acc_empty), the
-//                        block scales (then sc_empty), 16-byte stores of S,
+//                        block scales (then sc_empty), 32-byte stores of S,
 //                        running row maxima. Warp 8+e reads TMEM lanes
 //                        32*(e%4).. and 32 columns from 32*(e/4).
 // maps[u.layer]: the 2-D TMA map of the layer's K rows (bytes x rows); `seg`
@@ -366,8 +362,7 @@ __global__ void __launch_bounds__(SC_THREADS, 1) k_score_tc(const kvc_unit * __r
         const float rc = rowc[q];
         float rmax = -INFINITY;
         float * out = fs + u.s_off + (long long)h * nq * C;
-        const bool vec_out = ((C & 3) == 0) && ((((uintptr_t)out) & 15) == 0);
-        uint8_t * stg = smem + CF::OFF_STG + (uint32_t)(tid - 256) * CF::STG_LD;   // this thread's 32 scores
+        const bool vec_out = ((C & 7) == 0) && ((((uintptr_t)out) & 31) == 0);
         for (int i = 0; i < ntiles && !s_err; i++) {
             const int a = i & 1, j0 = i * TC_N;
             bool ok = true;
@@ -378,8 +373,7 @@ __global__ void __launch_bounds__(SC_THREADS, 1) k_score_tc(const kvc_unit * __r
             fence_after_sync();
             const float * scb = sSC + (i % NSC) * CF::NBLK * TC_N;
             const bool full = j0 + TC_N <= C;
-            const bool bulk = full && vec_out && q < nq;  // the row's 32 scores go out as one bulk copy
-            if (bulk) bulk_wait_read<0>();               // the previous tile's copy has read the staging
+            const bool bulk = full && vec_out && q < nq;  // the row's 32 scores as four 32-byte stores
 #pragma unroll
             for (int c16 = 0; c16 < 2; c16++) {
                 const int cb = 32 * ch + 16 * c16;
@@ -415,10 +409,9 @@ __global__ void __launch_bounds__(SC_THREADS, 1) k_score_tc(const kvc_unit * __r
                     }
                 }
                 if (bulk) {
-#pragma unroll
-                    for (int e4 = 0; e4 < 4; e4++)
-                        reinterpret_cast<float4 *>(stg + 64 * c16)[e4] =
-                            make_float4(v[4 * e4], v[4 * e4 + 1], v[4 * e4 + 2], v[4 * e4 + 3]);
+                    float * dst = out + (long long)q * C + j0 + cb;
+                    st_global_v8(dst, v);
+                    st_global_v8(dst + 8, v + 8);
                 } else if (q < nq) {
                     float * dst = out + (long long)q * C + j0 + cb;
 #pragma unroll
@@ -434,15 +427,9 @@ __global__ void __launch_bounds__(SC_THREADS, 1) k_score_tc(const kvc_unit * __r
                         if (j0 + cb + x < C) rmax = fmaxf(rmax, v[x]);
                 }
             }
-            if (bulk) {
-                fence_smem_to_async();                   // the staged scores, visible to the copy engine
-                bulk_store(out + (long long)q * C + j0 + 32 * ch, stg, 128);
-                bulk_commit();
-            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sc_empty[i % NSC]);   // the tile's scales are read
         }
-        bulk_wait<0>();                                  // every score store of this thread has completed
         red[ch * TC_M + q] = rmax;
     }
     __syncthreads();

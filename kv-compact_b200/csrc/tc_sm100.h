@@ -157,20 +157,13 @@ __device__ __forceinline__ void mbar_arrive(uint64_t * mbar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(mbar)) : "memory");
 }
 
-// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
-// from this CTA's shared memory to global memory, in this thread's current
-// bulk group; bulk_commit closes the group, bulk_wait_read<N> waits until at
-// most N of this thread's groups still read their shared-memory source, and
-// bulk_wait<0> until every group has completed.
-__device__ __forceinline__ void bulk_store(void * gdst, const void * ssrc, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
-                 :: "l"(gdst), "r"(smem_u32(ssrc)), "r"(bytes) : "memory");
+// 32 bytes (8 consecutive fp32, 32-byte aligned) in one access: a whole
+// 32-byte sector per thread.
+__device__ __forceinline__ void st_global_v8(float * p, const float * v) {
+    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+                 :: "l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+                 : "memory");
 }
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory"); }
-template <int N>
-__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group %0;" :: "n"(N) : "memory"); }
 
 // Arm the mbarrier for one arrival (this thread's) plus `bytes` of
 // asynchronous-copy transactions.
