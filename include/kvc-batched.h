@@ -15,8 +15,9 @@
  * inputs written on other non-blocking streams must be synchronised by the
  * caller first. Calls return after the work has completed.
  *
- * Limits: d_k, d_v <= 256; min(n_q, t) <= 3072 per chunk; H <= 64 with
- * use_sensitivity. Violations return -13.
+ * Limits: d_k, d_v <= 256; min(n_q, t) <= 24576 per chunk with skip_beta
+ * and no OMP selection, <= 3072 otherwise; H <= 64 with use_sensitivity.
+ * Violations return -13.
  */
 #pragma once
 

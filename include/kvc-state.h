@@ -31,7 +31,8 @@
  * layer's K/V width is not n_head_kv * d; -20 malformed or truncated state;
  * -21 unsupported layout (more than one non-empty stream; quantised
  * transposed V); -13 shape beyond the engine's limits (d > 256; min(n_ref,
- * t) > 3072; all compacted layers must fit one device batch); -10..-12
+ * t) > 24576, or > 3072 with the beta fit; all compacted layers must fit one
+ * device batch); -10..-12
  * no device / CUDA failure.
  */
 #pragma once
