@@ -384,10 +384,15 @@ def run_kvc(args, cfg, name):
                    "kout": torch.empty(t * krb, dtype=torch.uint8, device=device),
                    "vout": torch.empty(t * vrb, dtype=torch.uint8, device=device)} for _ in range(L)]
 
+    g = shard.Gather(dist, rank, world, plan, finals, H) if gather else None
+
     def step():
-        job.run(want_stats=True)
-        if gather:
-            shard.gather_to_root(dist, rank, world, plan, job.outputs(), finals, H)
+        if g is None:
+            job.run(want_stats=True)
+            return
+        g.begin()                      # rank 0: every receive posted before its own compute
+        outs = job.run(want_stats=True, gather=g)
+        g.finish(outs)
 
     for _ in range(args.warmup):
         step()
@@ -488,9 +493,9 @@ def run_kvc(args, cfg, name):
         elif world == 1:
             par = "one GPU"
         else:
-            par = (f"(layer, chunk) partition x{world}: {units_r} units per rank; final gather of the kept indices, "
-                   f"beta and requantised K/V rows to rank 0 over NCCL inside the timed region (C_v stays on "
-                   f"the rank that computed it)")
+            par = (f"(layer, chunk) partition x{world}: {units_r} units per rank; gather of the kept indices, "
+                   f"beta and requantised K/V rows to rank 0 over NCCL inside the timed region, each batched "
+                   f"call's slices sent as it returns (C_v stays on the rank that computed it)")
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,

@@ -104,19 +104,39 @@ __device__ __forceinline__ void convert_block(const uint8_t * raw, int raww, int
     using CF = tc_cfg<DK>;
     constexpr int BB = KT == 8 ? 34 : 18;
     const unsigned short * w = reinterpret_cast<const unsigned short *>(raw + k * raww + off + BB * b);
-    sc[b * TN + k] = __half2float(__ushort_as_half(w[0]));
     uint8_t * dst = B + (k >> 3) * CF::SBO + (4 * b) * 128 + (k & 7) * 16;
     if (KT == 8) {
+        // the block's 34 bytes as nine aligned 32-bit words from the 4-byte
+        // boundary at or below it (its start is 0 or 2 bytes past one)
+        const uint8_t * blk = raw + k * raww + off + BB * b;
+        const uint32_t sh = (uint32_t)((uintptr_t)blk & 3);
+        const uint32_t * w4 = reinterpret_cast<const uint32_t *>(blk - sh);
+        uint32_t x[9];
+#pragma unroll
+        for (int j = 0; j < 9; j++) x[j] = w4[j];
+        // scale = bytes 0-1 of the block, codes = bytes 2-33: word j of codes
+        // is block bytes 2+4j .. 5+4j
+        const uint32_t scale_bits = sh ? (x[0] >> 16) : (x[0] & 0xFFFFu);
+        sc[b * TN + k] = __half2float(__ushort_as_half((unsigned short)scale_bits));
 #pragma unroll
         for (int i = 0; i < 4; i++) {
+            uint32_t c0, c1;                        // codes 8i..8i+3 and 8i+4..8i+7
+            if (sh) {
+                c0 = x[1 + 2 * i];
+                c1 = x[2 + 2 * i];
+            } else {
+                c0 = __byte_perm(x[2 * i], x[2 * i + 1], 0x5432);
+                c1 = __byte_perm(x[2 * i + 1], x[2 * i + 2], 0x5432);
+            }
             uint4 o;
-            o.x = q8_pair(w[1 + 4 * i + 0]);
-            o.y = q8_pair(w[1 + 4 * i + 1]);
-            o.z = q8_pair(w[1 + 4 * i + 2]);
-            o.w = q8_pair(w[1 + 4 * i + 3]);
+            o.x = q8_pair(c0 & 0xFFFFu);
+            o.y = q8_pair(c0 >> 16);
+            o.z = q8_pair(c1 & 0xFFFFu);
+            o.w = q8_pair(c1 >> 16);
             *reinterpret_cast<uint4 *>(dst + i * 128) = o;
         }
-    } else {                                        // Q4_0: value 2i = low nibble of byte i, 2i+1 = its high nibble
+    } else {
+        sc[b * TN + k] = __half2float(__ushort_as_half(w[0]));                                        // Q4_0: value 2i = low nibble of byte i, 2i+1 = its high nibble
 #pragma unroll
         for (int i = 0; i < 4; i++) {               // chunk i: bytes 4i..4i+3 = words 2i, 2i+1
             const uint32_t x = w[1 + 2 * i], y = w[2 + 2 * i];

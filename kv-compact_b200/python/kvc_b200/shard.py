@@ -181,9 +181,15 @@ class SliceJob:
                 assert m.t[j] == slices[i].kept, (m.t[j], slices[i].kept)
             self.models.append((idx, m))
 
-    def run(self, want_stats=True):
-        for _, m in self.models:
+    def run(self, want_stats=True, gather=None):
+        """Compact every slice; with a Gather, each batched call's slices are
+        sent as soon as the call has returned."""
+        outs = self.outputs() if gather is not None else None
+        for idx, m in self.models:
             m.run(want_stats=want_stats)
+            if gather is not None:
+                gather.send(idx, outs)
+        return outs
 
     def outputs(self):
         """Per slice, in order: flat views of its device results."""
@@ -194,3 +200,66 @@ class SliceJob:
                 out[i] = {"sel": m.sel[j][:t], "beta": m.beta[j][:self.H * t], "kout": m.kout[j],
                           "vout": m.vout[j], "cv": m.cv[j][:self.H * t * m.md.d_v]}
         return out
+
+
+class Gather:
+    """The merge of gather_to_root, overlapped with the compute: rank 0 posts
+    every receive before it starts computing (begin), every rank sends the
+    slices of a batched call as soon as that call has returned (send), and
+    finish() waits for all transfers and places rank 0's own slices and the
+    head-major beta runs. Point-to-point operations between two ranks are
+    posted in the same (slice, array) order on both sides."""
+
+    def __init__(self, dist, rank, world, plan, finals, H):
+        self.dist, self.rank, self.world, self.plan, self.finals, self.H = dist, rank, world, plan, finals, H
+        self.works, self.beta_tmp = [], []
+
+    def _rows(self, s):
+        f = self.finals[s.layer]
+        t = max(f["sel"].numel(), 1)
+        return f, f["kout"].numel() // t, f["vout"].numel() // t
+
+    def begin(self):
+        self.works, self.beta_tmp = [], []
+        if self.rank != 0:
+            return
+        d = self.dist
+        for r in range(1, self.world):
+            for s in self.plan[r]:
+                f, kb, vb = self._rows(s)
+                bt = f["beta"].new_empty(self.H * s.kept)
+                self.beta_tmp.append((s, bt))
+                ops = [d.P2POp(d.irecv, f["sel"][s.out0:s.out1], r), d.P2POp(d.irecv, bt, r),
+                       d.P2POp(d.irecv, f["kout"][s.out0 * kb:s.out1 * kb], r),
+                       d.P2POp(d.irecv, f["vout"][s.out0 * vb:s.out1 * vb], r)]
+                self.works += d.batch_isend_irecv(ops)
+
+    def send(self, idx, outs):
+        """Slices plan[rank][i] for i in idx are computed (outs[i] their outputs)."""
+        d = self.dist
+        for i in idx:
+            s, out = self.plan[self.rank][i], outs[i]
+            out["sel"] += s.tok0                 # layer positions (src/kv-compact-api.cpp:533)
+            if self.rank == 0:
+                continue
+            ops = [d.P2POp(d.isend, out[k].contiguous(), 0) for k in ("sel", "beta", "kout", "vout")]
+            self.works += d.batch_isend_irecv(ops)
+
+    def finish(self, outs):
+        if self.rank == 0:
+            H = self.H
+            for s, out in zip(self.plan[0], outs):
+                f, kb, vb = self._rows(s)
+                t = f["sel"].numel()
+                f["sel"][s.out0:s.out1].copy_(out["sel"])
+                f["beta"].view(H, t)[:, s.out0:s.out1].copy_(out["beta"].view(H, s.kept))
+                f["kout"][s.out0 * kb:s.out1 * kb].copy_(out["kout"])
+                f["vout"][s.out0 * vb:s.out1 * vb].copy_(out["vout"])
+        for w in self.works:
+            w.wait()
+        if self.rank == 0:
+            for s, bt in self.beta_tmp:
+                f = self.finals[s.layer]
+                t = f["sel"].numel()
+                f["beta"].view(self.H, t)[:, s.out0:s.out1].copy_(bt.view(self.H, s.kept))
+        self.works, self.beta_tmp = [], []

@@ -56,7 +56,7 @@ def _whole(n_layers, T, ratio, H, kb, vb):
     return out
 
 
-def _worker(rank, world, port, q, n_layers, T, ratio, H, kb, vb):
+def _worker(rank, world, port, q, n_layers, T, ratio, H, kb, vb, overlapped=False):
     os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
                        "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
     import torch
@@ -80,7 +80,14 @@ def _worker(rank, world, port, q, n_layers, T, ratio, H, kb, vb):
             finals = [{"sel": torch.full((t,), -1, dtype=torch.int32), "beta": torch.full((H * t,), np.nan),
                        "kout": torch.zeros(t * kb, dtype=torch.uint8), "vout": torch.zeros(t * vb, dtype=torch.uint8)}
                       for _ in range(n_layers)]
-        shard.gather_to_root(dist, rank, world, plan, local, finals, H)
+        if overlapped:                             # receives first, each slice sent as it is "computed"
+            g = shard.Gather(dist, rank, world, plan, finals, H)
+            g.begin()
+            for i in range(len(local)):
+                g.send([i], local)
+            g.finish(local)
+        else:
+            shard.gather_to_root(dist, rank, world, plan, local, finals, H)
         ok = True
         if rank == 0:
             for l in range(n_layers):
@@ -92,9 +99,9 @@ def _worker(rank, world, port, q, n_layers, T, ratio, H, kb, vb):
         q.put((rank, False, repr(e)))
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_gather_rebuilds_whole_model_arrays(world):
-    args = (3, 5000, 0.2, 2, 34, 18)           # 3 layers x 4 chunks, 2 heads, row bytes 34 / 18
+@pytest.mark.parametrize("world,overlapped", [(2, False), (3, False), (3, True)])
+def test_gather_rebuilds_whole_model_arrays(world, overlapped):
+    args = (3, 5000, 0.2, 2, 34, 18, overlapped)   # 3 layers x 4 chunks, 2 heads, row bytes 34 / 18
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
