@@ -219,12 +219,13 @@ def run_reference(args, cfg, name):
 # summarised in profiles/main_kernels_cfg4_q8_1layer.md. Traffic grows in
 # proportion to the layers of a launch, so a full-step launch is scaled by 12.
 NCU_TRAFFIC_PER_LAYER_HEAD = {
+    "k_score_tc": (113.8e6 + 358.3e6) / 8,
     "k_score": (410.2e6 + 366.6e6) / 8,
     "k_score_async": (410.2e6 + 366.6e6) / 8,
-    "k_pv_tc": (538.6e6 + 33.5e6) / 8,
-    "k_row_importance": (412.8e6 + 4.7e6) / 8,
-    "k_lsq_factor": (123.3e6 + 41.9e6) / 8,
-    "k_decode_span": (109.7e6 + 352.3e6) / 8,
+    "k_pv_tc": (538.6e6 + 33.0e6) / 8,
+    "k_row_importance": (412.8e6 + 4.6e6) / 8,
+    "k_lsq_factor": (123.2e6 + 43.4e6) / 8,
+    "k_gather_softmax_x_reg": (409.7e6 + 69.3e6) / 8,
 }
 
 
@@ -424,6 +425,24 @@ def run_kvc(args, cfg, name):
     tokens_per_step = world * T if args.replicas else T
     value = tokens_per_step / (ms_max * 1e-3)
 
+    # ---- the partitioned result checked against one GPU computing the whole
+    # model (rank 0, after the timed region): kept indices, beta and the
+    # requantised K/V rows must be identical bit for bit
+    gather_check = None
+    if gather and not args.no_check:
+        if rank == 0:
+            whole = shard.SliceJob(fns, shard.partition(L, T, cfg["ratio"], 1)[0], Kq, Vq, Q, T, H, d,
+                                   cfg["ktype"], cfg["vtype"], params)
+            whole.run(want_stats=False)
+            ref = whole.outputs()
+            torch.cuda.synchronize()
+            bad = [l for l in range(L) for k in ("sel", "beta", "kout", "vout")
+                   if not torch.equal(ref[l][k], finals[l][k])]
+            gather_check = ("rank 0's whole-model arrays identical to one GPU's" if not bad
+                            else f"MISMATCH in layers {sorted(set(bad))}")
+            del whole, ref
+        kdist.barrier(world)
+
     # ---- end to end through the drop-in C ABI: each rank's slices from
     # pinned host buffers (kv_compact_quantized per slice, results back in
     # its host memory), copies inside the timed region
@@ -507,6 +526,7 @@ def run_kvc(args, cfg, name):
                        "l2": "inputs (2.6 GB) exceed L2; no flush needed"},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
             "clocks": clocks,
+            **({"gather_check": gather_check} if gather_check else {}),
             "stage_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in stages.items() if v[1]},
             "stage_roofline": {k: {"kernel": v["kernel"], "bound": v["bound"], "frac": round(v["frac"], 3),
                                    "achieved": round(v["achieved"], 2), "unit": v["unit"]}
@@ -528,6 +548,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--replicas", action="store_true",
                     help="N>1: every rank compacts its own model (weak scaling) instead of a share of one model")
+    ap.add_argument("--no-check", action="store_true",
+                    help="N>1 partition: skip comparing rank 0's gathered result with one GPU's")
     ap.add_argument("--layers", type=int, default=0,
                     help="compact only the first N filtered layers (small cases for profiling)")
     args = ap.parse_args()

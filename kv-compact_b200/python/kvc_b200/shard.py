@@ -213,6 +213,7 @@ class Gather:
     def __init__(self, dist, rank, world, plan, finals, H):
         self.dist, self.rank, self.world, self.plan, self.finals, self.H = dist, rank, world, plan, finals, H
         self.works, self.beta_tmp = [], []
+        self.ready, self.next = set(), 0
 
     def _rows(self, s):
         f = self.finals[s.layer]
@@ -221,6 +222,7 @@ class Gather:
 
     def begin(self):
         self.works, self.beta_tmp = [], []
+        self.ready, self.next = set(), 0
         if self.rank != 0:
             return
         d = self.dist
@@ -235,17 +237,29 @@ class Gather:
                 self.works += d.batch_isend_irecv(ops)
 
     def send(self, idx, outs):
-        """Slices plan[rank][i] for i in idx are computed (outs[i] their outputs)."""
+        """Slices plan[rank][i] for i in idx are computed (outs[i] their
+        outputs). Sends leave in plan order whatever order the slices are
+        computed in: a slice waits until every earlier slice of this rank
+        has been sent, because rank 0 posted its receives in plan order and
+        point-to-point operations between two ranks match in posting order."""
         d = self.dist
         for i in idx:
             s, out = self.plan[self.rank][i], outs[i]
             out["sel"] += s.tok0                 # layer positions (src/kv-compact-api.cpp:533)
+            self.ready.add(i)
+        while self.next in self.ready:
+            i = self.next
+            self.ready.discard(i)
+            self.next += 1
             if self.rank == 0:
                 continue
-            ops = [d.P2POp(d.isend, out[k].contiguous(), 0) for k in ("sel", "beta", "kout", "vout")]
+            ops = [d.P2POp(d.isend, outs[i][k].contiguous(), 0) for k in ("sel", "beta", "kout", "vout")]
             self.works += d.batch_isend_irecv(ops)
 
     def finish(self, outs):
+        if self.next != len(self.plan[self.rank]):
+            raise RuntimeError(f"rank {self.rank}: slices {sorted(set(range(len(self.plan[self.rank]))) - set(range(self.next)))} "
+                               "were never sent")
         if self.rank == 0:
             H = self.H
             for s, out in zip(self.plan[0], outs):

@@ -83,7 +83,7 @@ def _worker(rank, world, port, q, n_layers, T, ratio, H, kb, vb, overlapped=Fals
         if overlapped:                             # receives first, each slice sent as it is "computed"
             g = shard.Gather(dist, rank, world, plan, finals, H)
             g.begin()
-            for i in range(len(local)):
+            for i in reversed(range(len(local))):  # computed out of plan order: sends must still match
                 g.send([i], local)
             g.finish(local)
         else:
@@ -99,9 +99,10 @@ def _worker(rank, world, port, q, n_layers, T, ratio, H, kb, vb, overlapped=Fals
         q.put((rank, False, repr(e)))
 
 
-@pytest.mark.parametrize("world,overlapped", [(2, False), (3, False), (3, True)])
+@pytest.mark.parametrize("world,overlapped", [(2, False), (3, False), (2, True), (3, True)])
 def test_gather_rebuilds_whole_model_arrays(world, overlapped):
     args = (3, 5000, 0.2, 2, 34, 18, overlapped)   # 3 layers x 4 chunks, 2 heads, row bytes 34 / 18
+    # world 2: each rank holds two slices, sent below in reverse order when overlapped
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
