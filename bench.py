@@ -370,28 +370,35 @@ def run_kvc(args, cfg, name):
     Kq, Vq, Q = make_layers(cfg, seed, device, fns)
     cs = shard.auto_chunk(T, cfg["ratio"])
     params = abi.make_params(fns, target_ratio=cfg["ratio"], chunk_size=cs)
+    gather = not replicas and world > 1
+    peer = gather and args.gather == "peer"
     if replicas:
         plan = [shard.partition(L, T, cfg["ratio"], 1)[0] for _ in range(world)]
     else:
-        plan = shard.partition(L, T, cfg["ratio"], world)
-    job = shard.SliceJob(fns, plan[rank], Kq, Vq, Q, T, H, d, cfg["ktype"], cfg["vtype"], params)
+        # peer writes overlap rank 0's compute when rank 0 holds a larger share
+        weights = shard.root_weights(world, args.root_extra) if peer else None
+        plan = shard.partition(L, T, cfg["ratio"], world, weights)
     krb, vrb = Kq[0].shape[1], Vq[0].shape[1]
-    finals = None
-    gather = not replicas and world > 1
-    if gather and rank == 0:
-        t = shard.layer_kept(T, cfg["ratio"])
-        finals = [{"sel": torch.empty(t, dtype=torch.int32, device=device),
-                   "beta": torch.empty(H * t, dtype=torch.float32, device=device),
-                   "kout": torch.empty(t * krb, dtype=torch.uint8, device=device),
-                   "vout": torch.empty(t * vrb, dtype=torch.uint8, device=device)} for _ in range(L)]
-
-    g = shard.Gather(dist, rank, world, plan, finals, H) if gather else None
+    finals, g = None, None
+    if peer:
+        g = shard.PeerGather(dist, fns, rank, world, plan, L, T, cfg["ratio"], H, krb, vrb, device)
+        finals = g.finals
+    job = shard.SliceJob(fns, plan[rank], Kq, Vq, Q, T, H, d, cfg["ktype"], cfg["vtype"], params,
+                         out_ptrs=g.out_ptrs() if peer else None)
+    if gather and not peer:
+        if rank == 0:
+            t = shard.layer_kept(T, cfg["ratio"])
+            finals = [{"sel": torch.empty(t, dtype=torch.int32, device=device),
+                       "beta": torch.empty(H * t, dtype=torch.float32, device=device),
+                       "kout": torch.empty(t * krb, dtype=torch.uint8, device=device),
+                       "vout": torch.empty(t * vrb, dtype=torch.uint8, device=device)} for _ in range(L)]
+        g = shard.Gather(dist, rank, world, plan, finals, H)
 
     def step():
         if g is None:
             job.run(want_stats=True)
             return
-        g.begin()                      # rank 0: every receive posted before its own compute
+        g.begin()                      # previous step's transfers done; NCCL: receives posted
         outs = job.run(want_stats=True, gather=g)
         g.finish(outs)
 
@@ -512,9 +519,12 @@ def run_kvc(args, cfg, name):
         elif world == 1:
             par = "one GPU"
         else:
-            par = (f"(layer, chunk) partition x{world}: {units_r} units per rank; gather of the kept indices, "
-                   f"beta and requantised K/V rows to rank 0 over NCCL inside the timed region, each batched "
-                   f"call's slices sent as it returns (C_v stays on the rank that computed it)")
+            how = ("writes into rank 0's result buffer over NVLink (CUDA IPC: requantisation kernels store K_out/V_out "
+                   "rows in place, one kernel places indices and beta), rank 0 weighted "
+                   f"{shard.root_weights(world, args.root_extra)[0]:.2f}x" if peer else "NCCL send/recv to rank 0")
+            par = (f"(layer, chunk) partition x{world}: {units_r} units per rank; merge of the kept indices, "
+                   f"beta and requantised K/V rows into rank 0's whole-model arrays inside the timed region by "
+                   f"{how}, each batched call's slices sent as it returns (C_v stays on the rank that computed it)")
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
@@ -534,6 +544,8 @@ def run_kvc(args, cfg, name):
         }
         print(json.dumps(line))
     del job, finals
+    if peer:
+        g.close()
     kdist.finish(world)
 
 
@@ -548,6 +560,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--replicas", action="store_true",
                     help="N>1: every rank compacts its own model (weak scaling) instead of a share of one model")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N>1 partition: merge by copy-engine puts into rank 0's buffer, or NCCL send/recv")
+    ap.add_argument("--root-extra", type=float, default=0.03,
+                    help="peer merge: rank 0's share is 1 + extra*(N-1) times another rank's")
     ap.add_argument("--no-check", action="store_true",
                     help="N>1 partition: skip comparing rank 0's gathered result with one GPU's")
     ap.add_argument("--layers", type=int, default=0,

@@ -43,10 +43,14 @@ typedef struct kvc_model_desc {
 } kvc_model_desc;
 
 typedef struct kvc_layer_desc {
-    const void *  K;      /* device [T x k_row_bytes] */
-    const void *  V;      /* device [T x v_row_bytes] */
+    const void *  K;      /* device [T_l x k_row_bytes] */
+    const void *  V;      /* device [T_l x v_row_bytes] */
     const float * Q_ref;  /* device [n_q x n_head_kv*d_k] fp32, or NULL (cheap queries) */
     int           n_q;
+    int           n_tokens; /* T_l, this layer's cache positions; 0 = model->T. Layers
+                               of different lengths (e.g. slices of a model's layers
+                               on one GPU) share one call; R-KV weighting
+                               (params->reasoning) needs every T_l = model->T */
 } kvc_layer_desc;
 
 typedef struct kvc_layer_result {

@@ -26,6 +26,11 @@ int check(const kvc_model_desc * m, const kvc_layer_desc * L) {
     return KVC_OK;
 }
 
+// Cache positions of layer l (its own n_tokens, else the model's T).
+int layer_T(const kvc_model_desc * m, const kvc_layer_desc & Ld) {
+    return Ld.n_tokens > 0 ? Ld.n_tokens : m->T;
+}
+
 kv_compact_params params_or_default(const kv_compact_params * p) {
     return p ? *p : kv_compact_params_default();
 }
@@ -65,8 +70,9 @@ KVC_EXPORT int kvc_plan_layers(const kvc_model_desc * m, const kvc_layer_desc * 
         if (!layer_on(m, p, l)) continue;
         const bool qn = p.use_cheap_qref || !L[l].Q_ref;
         if (!L[l].K || !L[l].V) return KVC_ERR_NULL;
+        if (L[l].n_tokens < 0) return KVC_ERR_DIMS;
         kvc_plan pl;
-        if ((rc = kvc_make_plan(m->T, L[l].n_q, qn, m->n_head_kv, m->d_k, m->d_v, p, &pl))) return rc;
+        if ((rc = kvc_make_plan(layer_T(m, L[l]), L[l].n_q, qn, m->n_head_kv, m->d_k, m->d_v, p, &pl))) return rc;
         t_out[l] = pl.t_total;
     }
     return KVC_OK;
@@ -84,6 +90,7 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
     cudaStream_t st = ctx->stream;
     const int H = m->n_head_kv, dk = m->d_k, dv = m->d_v, T = m->T;
     const int ek = H * dk, ev = H * dv;
+    const bool rkv = p.reasoning && p.reasoning->classifier;
 
     std::vector<int> on;
     for (int l = 0; l < m->n_layers; l++) {
@@ -96,15 +103,20 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
     for (int i = 0; i < n; i++) {
         const int l = on[i];
         if (!L[l].K || !L[l].V) return KVC_ERR_NULL;
+        if (L[l].n_tokens < 0 || (rkv && layer_T(m, L[l]) != T)) return KVC_ERR_DIMS;
         const bool qn = p.use_cheap_qref || !L[l].Q_ref;
-        if ((rc = kvc_make_plan(T, L[l].n_q, qn, H, dk, dv, p, &plans[i]))) return rc;
+        if ((rc = kvc_make_plan(layer_T(m, L[l]), L[l].n_q, qn, H, dk, dv, p, &plans[i]))) return rc;
     }
-    // fp32 caches of every filtered layer, plus generated cheap queries and R-KV weights
-    const size_t nk = ((size_t)T * ek + 31) & ~31ULL, nv = ((size_t)T * ev + 31) & ~31ULL;
+    // fp32 caches of every filtered layer (each T_l rows), plus generated
+    // cheap queries and R-KV weights
+    std::vector<size_t> kv_off(n + 1, 0);
+    for (int i = 0; i < n; i++) {
+        const size_t Tl = (size_t)layer_T(m, L[on[i]]);
+        kv_off[i + 1] = kv_off[i] + ((Tl * ek + 31) & ~31ULL) + ((Tl * ev + 31) & ~31ULL);
+    }
     void * a;
-    if ((rc = kvc_arena(ctx, SLOT_BATCH_KV, (size_t)n * (nk + nv) * 4, &a))) return rc;
+    if ((rc = kvc_arena(ctx, SLOT_BATCH_KV, kv_off[n] * 4, &a))) return rc;
     float * F = (float *)a;
-    const bool rkv = p.reasoning && p.reasoning->classifier;
     size_t io = 0;
     for (int i = 0; i < n; i++) if (plans[i].top_cheap) io += (((size_t)plans[i].nq_top * ek) + 31) & ~31ULL;
     if (rkv) io += (size_t)T + 32;
@@ -130,12 +142,12 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
         k_blocks = kvc_k_blocks_only(p, plans[i], m->k_type, m->k_row_bytes, L[on[i]].K, H, dk);
     std::vector<kvc_layer_job> jobs(n);
     for (int i = 0; i < n; i++) {
-        const int l = on[i];
-        float * dK = F + (size_t)i * (nk + nv);
-        float * dV = dK + nk;
+        const int l = on[i], Tl = layer_T(m, L[l]);
+        float * dK = F + kv_off[i];
+        float * dV = dK + (((size_t)Tl * ek + 31) & ~31ULL);
         if (!k_blocks) {
             kvc_stage_timer tm(ctx, KVC_ST_DECODE, 1);
-            if ((rc = kvc_launch_decode((const uint8_t *)L[l].K, m->k_row_bytes, m->k_type, dK, T, ek, st))) return rc;
+            if ((rc = kvc_launch_decode((const uint8_t *)L[l].K, m->k_row_bytes, m->k_type, dK, Tl, ek, st))) return rc;
         }
         kvc_layer_job & J = jobs[i];
         J.K = dK;
@@ -150,7 +162,7 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
         if (plans[i].top_cheap) {
             float * q = io_p;
             io_p += (((size_t)plans[i].nq_top * ek) + 31) & ~31ULL;
-            if ((rc = kvc_launch_cheap_q(dK, T, ek, plans[i].nq_top, q, st))) return rc;
+            if ((rc = kvc_launch_cheap_q(dK, Tl, ek, plans[i].nq_top, q, st))) return rc;
             ctx->launches += 1;
             J.Q = q;
         } else {

@@ -22,6 +22,8 @@ SEAM_SYMBOLS = [
 ]
 BATCHED_SYMBOLS = ["kvc_plan_layers", "kvc_compact_layers_dev", "kvc_launch_count", "kvc_profile",
                    "kvc_quantize_rows_dev", "kvc_dequantize_rows_dev"]
+PEER_SYMBOLS = ["kvc_peer_alloc", "kvc_peer_free", "kvc_peer_open", "kvc_peer_close", "kvc_copy_async",
+                "kvc_copy2d_async", "kvc_place_slice"]
 STAGES = ["decode", "score", "softmax_importance", "select", "refit_target", "beta", "x_build", "ls_gram",
           "refine", "metrics", "requant", "ls_factor", "ls_out"]
 
@@ -32,7 +34,7 @@ class ModelDesc(Structure):
 
 
 class LayerDesc(Structure):
-    _fields_ = [("K", c_void_p), ("V", c_void_p), ("Q_ref", c_void_p), ("n_q", c_int)]
+    _fields_ = [("K", c_void_p), ("V", c_void_p), ("Q_ref", c_void_p), ("n_q", c_int), ("n_tokens", c_int)]
 
 
 class LayerResult(Structure):
@@ -80,6 +82,20 @@ def load(path=None):
     lib.kvc_dequantize_rows_dev.argtypes = [c_void_p, c_size_t, c_int, c_int, c_int, c_void_p]
     lib.kvc_profile.restype = c_int
     lib.kvc_profile.argtypes = [c_int, POINTER(ctypes.c_double), POINTER(c_uint64), c_int]
+    lib.kvc_peer_alloc.restype = c_int
+    lib.kvc_peer_alloc.argtypes = [c_size_t, POINTER(c_void_p), c_void_p]
+    lib.kvc_peer_free.restype = c_int
+    lib.kvc_peer_free.argtypes = [c_void_p]
+    lib.kvc_peer_open.restype = c_int
+    lib.kvc_peer_open.argtypes = [c_void_p, POINTER(c_void_p)]
+    lib.kvc_peer_close.restype = c_int
+    lib.kvc_peer_close.argtypes = [c_void_p]
+    lib.kvc_copy_async.restype = c_int
+    lib.kvc_copy_async.argtypes = [c_void_p, c_void_p, c_size_t, c_void_p]
+    lib.kvc_copy2d_async.restype = c_int
+    lib.kvc_copy2d_async.argtypes = [c_void_p, c_size_t, c_void_p, c_size_t, c_size_t, c_size_t, c_void_p]
+    lib.kvc_place_slice.restype = c_int
+    lib.kvc_place_slice.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p]
     fns["_lib"] = lib
     fns["_path"] = path
     if path == LIB_PATH or _LIB is None:
@@ -123,12 +139,16 @@ def profile(fns, enable):
 class BatchedModel:
     """Whole-model device-resident compaction over torch tensors.
 
-    K[l], V[l]: uint8 (or float32) CUDA tensors [T, row_bytes]; Q[l]: float32
-    CUDA tensors [n_q, H*d_k] or None. Output buffers are allocated once from
-    kvc_plan_layers() and reused by every run().
+    K[l], V[l]: uint8 (or float32) CUDA tensors [T_l, row_bytes]; Q[l]: float32
+    CUDA tensors [n_q, H*d_k] or None. tokens: per-layer T_l (default: T for
+    every layer). Output buffers are allocated once from kvc_plan_layers()
+    and reused by every run(); out_ptrs[l] = (K_out, V_out) device pointers
+    makes layer l's requantised rows go there instead (self.kout[l] and
+    self.vout[l] are then None).
     """
 
-    def __init__(self, fns, K, V, Q, T, H, dk, dv, k_type, v_type, params, requant=True):
+    def __init__(self, fns, K, V, Q, T, H, dk, dv, k_type, v_type, params, requant=True, tokens=None,
+                 out_ptrs=None):
         import torch
         self.fns, self.lib = fns, fns["_lib"]
         self.params = params
@@ -140,7 +160,7 @@ class BatchedModel:
         for l in range(n):
             q = Q[l] if Q is not None else None
             self.layers[l] = LayerDesc(K[l].data_ptr(), V[l].data_ptr(), q.data_ptr() if q is not None else None,
-                                       q.shape[0] if q is not None else 0)
+                                       q.shape[0] if q is not None else 0, 0 if tokens is None else tokens[l])
         ts = (c_int * n)()
         rc = self.lib.kvc_plan_layers(ctypes.byref(self.md), self.layers, ctypes.byref(params), ts)
         if rc != 0:
@@ -154,11 +174,14 @@ class BatchedModel:
             self.sel.append(torch.empty(t, dtype=torch.int32, device=dev))
             self.beta.append(torch.empty(H * t, dtype=torch.float32, device=dev))
             self.cv.append(torch.empty(H * t * dv, dtype=torch.float32, device=dev))
-            self.kout.append(torch.empty(t * self.md.k_row_bytes, dtype=torch.uint8, device=dev) if requant else None)
-            self.vout.append(torch.empty(t * self.md.v_row_bytes, dtype=torch.uint8, device=dev) if requant else None)
+            ext = out_ptrs is not None and out_ptrs[l] is not None
+            own = requant and not ext
+            self.kout.append(torch.empty(t * self.md.k_row_bytes, dtype=torch.uint8, device=dev) if own else None)
+            self.vout.append(torch.empty(t * self.md.v_row_bytes, dtype=torch.uint8, device=dev) if own else None)
+            kp = out_ptrs[l][0] if ext else (self.kout[l].data_ptr() if own else None)
+            vp = out_ptrs[l][1] if ext else (self.vout[l].data_ptr() if own else None)
             self.results[l] = LayerResult(0, self.sel[l].data_ptr(), self.beta[l].data_ptr(), self.cv[l].data_ptr(),
-                                          self.kout[l].data_ptr() if requant else None,
-                                          self.vout[l].data_ptr() if requant else None, abi.Stats())
+                                          kp, vp, abi.Stats())
 
     def run(self, want_stats=True):
         rc = self.lib.kvc_compact_layers_dev(ctypes.byref(self.md), self.layers, ctypes.byref(self.params),

@@ -68,17 +68,22 @@ class Slice:
         return self.out1 - self.out0
 
 
-def partition(n_layers, T, ratio, world):
+def partition(n_layers, T, ratio, world, weights=None):
     """Per rank, the list of its slices: contiguous ranges of the flattened
-    (layer, chunk) units with about total_tokens / world tokens each."""
+    (layer, chunk) units with about total_tokens * weights[r] / sum(weights)
+    tokens each (equal shares by default)."""
     chunks = chunk_table(T, ratio)
     out_off = np.concatenate([[0], np.cumsum([c[2] for c in chunks])]).astype(int)
     units = [(l, c) for l in range(n_layers) for c in range(len(chunks))]
     w = np.array([chunks[c][1] for _, c in units], dtype=np.int64)
     cum = np.concatenate([[0], np.cumsum(w)])
     total = int(cum[-1])
-    # rank r starts at the first unit whose preceding tokens reach r * total / world
-    starts = [int(np.searchsorted(cum[:-1], r * total / world, side="left")) for r in range(world)]
+    wt = np.ones(world) if weights is None else np.asarray(weights, dtype=np.float64)
+    if len(wt) != world or np.any(wt <= 0):
+        raise ValueError("one positive weight per rank")
+    bound = np.concatenate([[0.0], np.cumsum(wt)]) / wt.sum() * total
+    # rank r starts at the first unit whose preceding tokens reach bound[r]
+    starts = [int(np.searchsorted(cum[:-1], bound[r], side="left")) for r in range(world)]
     starts.append(len(units))
     ranks = []
     for r in range(world):
@@ -160,31 +165,38 @@ def gather_to_root(dist, rank, world, plan, local, finals, H):
 
 class SliceJob:
     """A rank's slices, compacted through the device-resident batched API
-    (kvc_compact_layers_dev): slices of equal token count share one batched
-    call. K[l], V[l]: the model's block-format rows of filtered layer l
-    (device uint8 tensors [T, row_bytes]); Q[l]: its reference queries."""
+    (kvc_compact_layers_dev) in one call: each slice is a layer of the call
+    with its own token count (kvc_layer_desc.n_tokens). K[l], V[l]: the
+    model's block-format rows of filtered layer l (device uint8 tensors
+    [T, row_bytes]); Q[l]: its reference queries. out_ptrs: per slice, the
+    device addresses (K_out, V_out) its requantised rows are written to
+    (e.g. PeerGather.out_ptrs(): rank 0's result arrays, local or mapped),
+    else buffers of its own."""
 
-    def __init__(self, fns, slices, K, V, Q, T, H, d, k_type, v_type, params):
+    def __init__(self, fns, slices, K, V, Q, T, H, d, k_type, v_type, params, out_ptrs=None):
         from . import lib
         self.slices = slices
         self.H = H
-        groups = {}
-        for i, s in enumerate(slices):
-            groups.setdefault(s.tokens, []).append(i)
         self.models = []
-        for tokens, idx in groups.items():
-            Ks = [K[slices[i].layer][slices[i].tok0:slices[i].tok1] for i in idx]
-            Vs = [V[slices[i].layer][slices[i].tok0:slices[i].tok1] for i in idx]
-            Qs = [Q[slices[i].layer] for i in idx]
-            m = lib.BatchedModel(fns, Ks, Vs, Qs, tokens, H, d, d, k_type, v_type, params)
-            for j, i in enumerate(idx):
-                assert m.t[j] == slices[i].kept, (m.t[j], slices[i].kept)
-            self.models.append((idx, m))
+        if not slices:
+            return
+        idx = list(range(len(slices)))
+        Ks = [K[s.layer][s.tok0:s.tok1] for s in slices]
+        Vs = [V[s.layer][s.tok0:s.tok1] for s in slices]
+        Qs = [Q[s.layer] for s in slices]
+        tokens = [s.tokens for s in slices]
+        m = lib.BatchedModel(fns, Ks, Vs, Qs, max(tokens), H, d, d, k_type, v_type, params, tokens=tokens,
+                             out_ptrs=out_ptrs)
+        for j, s in enumerate(slices):
+            assert m.t[j] == s.kept, (m.t[j], s.kept)
+        self.models.append((idx, m))
 
     def run(self, want_stats=True, gather=None):
         """Compact every slice; with a Gather, each batched call's slices are
         sent as soon as the call has returned."""
-        outs = self.outputs() if gather is not None else None
+        if gather is not None and getattr(self, "_outs", None) is None:
+            self._outs = self.outputs()          # the same views every step
+        outs = self._outs if gather is not None else None
         for idx, m in self.models:
             m.run(want_stats=want_stats)
             if gather is not None:
@@ -221,6 +233,12 @@ class Gather:
         return f, f["kout"].numel() // t, f["vout"].numel() // t
 
     def begin(self):
+        """Post rank 0's receives. First wait until the previous step's
+        transfers are done: the library computes on its own stream, so the
+        next batched call must not rewrite arrays that a send still reads."""
+        import torch
+        if torch.cuda.is_available():
+            torch.cuda.current_stream().synchronize()
         self.works, self.beta_tmp = [], []
         self.ready, self.next = set(), 0
         if self.rank != 0:
@@ -277,3 +295,143 @@ class Gather:
                 t = f["sel"].numel()
                 f["beta"].view(self.H, t)[:, s.out0:s.out1].copy_(bt.view(self.H, s.kept))
         self.works, self.beta_tmp = [], []
+
+
+def root_weights(world, extra=0.03):
+    """Partition weights that give rank 0 a larger share: the other ranks
+    finish their compute earlier by about the time their peer copies into
+    rank 0's result arrays take, so the copies land while rank 0 computes."""
+    return [1.0 + extra * (world - 1)] + [1.0] * (world - 1)
+
+
+def result_layout(n_layers, T, ratio, H, k_row_bytes, v_row_bytes, align=256):
+    """Byte layout of one model's result arrays in a single buffer: per layer
+    {"sel": (offset, bytes), "beta", "kout", "vout"}, each array aligned to
+    `align` bytes; returns (layers, total bytes). sel int32 [t], beta fp32
+    [H, t] (head-major, as the reference returns it), K_out / V_out rows."""
+    t = layer_kept(T, ratio)
+    sizes = (("sel", 4 * t), ("beta", 4 * H * t), ("kout", t * k_row_bytes), ("vout", t * v_row_bytes))
+    off, layers = 0, []
+    for _ in range(n_layers):
+        d = {}
+        for k, nb in sizes:
+            d[k] = (off, nb)
+            off += (nb + align - 1) // align * align
+        layers.append(d)
+    return layers, off
+
+
+def put_ops(s, layout, T, ratio, H, k_row_bytes, v_row_bytes):
+    """The copies that place slice s's outputs into the result buffer:
+    ("1d", array, dst offset, src offset, bytes) and, for beta's H runs,
+    ("2d", "beta", dst offset, dst pitch, src pitch, width, height). Source
+    offsets are within the slice's own flat output arrays."""
+    t = layer_kept(T, ratio)
+    L = layout[s.layer]
+    kept = s.kept
+    return [("1d", "sel", L["sel"][0] + 4 * s.out0, 0, 4 * kept),
+            ("2d", "beta", L["beta"][0] + 4 * s.out0, 4 * t, 4 * kept, 4 * kept, H),
+            ("1d", "kout", L["kout"][0] + k_row_bytes * s.out0, 0, k_row_bytes * kept),
+            ("1d", "vout", L["vout"][0] + v_row_bytes * s.out0, 0, v_row_bytes * kept)]
+
+
+class _CudaBuffer:
+    """A raw device allocation seen by torch.as_tensor (no copy)."""
+
+    def __init__(self, ptr, nbytes, device_index):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+        self.device_index = device_index
+
+
+class PeerGather:
+    """The reference's chunk merge across GPUs through peer memory: rank 0
+    owns one buffer with the whole model's result arrays (result_layout),
+    allocated through kvc_peer_alloc; every other rank maps it
+    (kvc_peer_open). Each rank's batched call writes its slices' requantised
+    K_out / V_out rows straight to their rows there (out_ptrs(), given to
+    SliceJob: the requantisation kernels store over NVLink), and send() adds
+    one kvc_place_slice launch per slice for the kept indices (offset to
+    layer positions) and the head-major beta runs. finish() orders the step:
+    a one-element all-reduce on every rank's current stream, which on the
+    other ranks runs after their writes, so rank 0's arrays are complete once
+    it returns. No receive is posted and nothing is copied twice. Construct
+    and close() on every rank together (collective)."""
+
+    def __init__(self, dist, fns, rank, world, plan, n_layers, T, ratio, H, k_row_bytes, v_row_bytes, device):
+        import ctypes
+        import torch
+        self.dist, self.lib, self.rank, self.world, self.plan = dist, fns["_lib"], rank, world, plan
+        self.T, self.ratio, self.H, self.krb, self.vrb = T, ratio, H, k_row_bytes, v_row_bytes
+        self.device = device
+        self.layout, self.nbytes = result_layout(n_layers, T, ratio, H, k_row_bytes, v_row_bytes)
+        self.ptr = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        if rank == 0:
+            rc = self.lib.kvc_peer_alloc(self.nbytes, ctypes.byref(self.ptr), handle)
+            if rc != 0:
+                raise RuntimeError(f"kvc_peer_alloc failed: {rc}")
+        box = [bytes(handle)]
+        dist.broadcast_object_list(box, src=0, device=device)
+        if rank != 0:
+            ctypes.memmove(handle, box[0], 64)
+            rc = self.lib.kvc_peer_open(handle, ctypes.byref(self.ptr))
+            if rc != 0:
+                raise RuntimeError(f"kvc_peer_open failed: {rc}")
+        self.base = self.ptr.value
+        self.finals = None
+        if rank == 0:
+            buf = torch.as_tensor(_CudaBuffer(self.base, self.nbytes, device.index), device=device)
+            t = layer_kept(T, ratio)
+            self.finals = []
+            for L in self.layout:
+                view = lambda k, dt: buf[L[k][0]:L[k][0] + L[k][1]].view(dt)   # noqa: E731
+                self.finals.append({"sel": view("sel", torch.int32), "beta": view("beta", torch.float32),
+                                    "kout": view("kout", torch.uint8), "vout": view("vout", torch.uint8)})
+            assert all(f["sel"].numel() == t for f in self.finals)
+        self.flag = torch.zeros(1, dtype=torch.int32, device=device)
+        # per slice of this rank: (kept, tok0, sel address, beta address, K_out, V_out addresses)
+        self.t = layer_kept(T, ratio)
+        self.dst = []
+        for s in plan[rank]:
+            ops = {op[1]: op for op in put_ops(s, self.layout, T, ratio, H, k_row_bytes, v_row_bytes)}
+            self.dst.append((s.kept, s.tok0, self.base + ops["sel"][2], self.base + ops["beta"][2],
+                             self.base + ops["kout"][2], self.base + ops["vout"][2]))
+
+    def begin(self):
+        """Wait until the previous step's copies (and its all-reduce) are
+        done: the library computes on its own stream, so the next batched
+        call must not rewrite output arrays that a copy still reads."""
+        import torch
+        torch.cuda.current_stream(self.device).synchronize()
+
+    def out_ptrs(self):
+        """Per slice of this rank, the addresses of its K_out / V_out rows in
+        rank 0's result buffer (put_ops' destinations)."""
+        return [(d[4], d[5]) for d in self.dst]
+
+    def send(self, idx, outs):
+        """Slices plan[rank][i] for i in idx are computed (outs[i] their
+        outputs; their K_out / V_out rows are already in place)."""
+        import torch
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        for i in idx:
+            kept, tok0, sel_dst, beta_dst = self.dst[i][:4]
+            rc = self.lib.kvc_place_slice(outs[i]["sel"].data_ptr(), outs[i]["beta"].data_ptr(), kept, self.H, tok0,
+                                          sel_dst, beta_dst, self.t, st)
+            if rc != 0:
+                raise RuntimeError(f"kvc_place_slice failed: {rc}")
+
+    def finish(self, outs):
+        self.dist.all_reduce(self.flag)          # after this rank's copies, on every rank
+
+    def close(self):
+        import torch
+        torch.cuda.synchronize(self.device)
+        if self.rank != 0 and self.base:
+            self.lib.kvc_peer_close(self.base)
+        self.dist.barrier()
+        if self.rank == 0 and self.base:
+            self.finals = None
+            self.lib.kvc_peer_free(self.base)
+        self.base = None

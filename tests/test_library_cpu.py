@@ -34,7 +34,7 @@ def declared_functions(header):
     return sorted(names)
 
 
-@pytest.mark.parametrize("header", ["kv-compact-api.h", "kv-compact-accel-cuda.h", "kvc-batched.h"])
+@pytest.mark.parametrize("header", ["kv-compact-api.h", "kv-compact-accel-cuda.h", "kvc-batched.h", "kvc-peer.h"])
 def test_every_declared_symbol_is_exported(kvc, header):
     names = declared_functions(header)
     assert names, header
@@ -44,9 +44,9 @@ def test_every_declared_symbol_is_exported(kvc, header):
 
 def test_symbol_lists_cover_headers():
     declared = set()
-    for h in ("kv-compact-api.h", "kv-compact-accel-cuda.h", "kvc-batched.h"):
+    for h in ("kv-compact-api.h", "kv-compact-accel-cuda.h", "kvc-batched.h", "kvc-peer.h"):
         declared |= set(declared_functions(h))
-    listed = set(kvclib.DROPIN_SYMBOLS + kvclib.SEAM_SYMBOLS + kvclib.BATCHED_SYMBOLS)
+    listed = set(kvclib.DROPIN_SYMBOLS + kvclib.SEAM_SYMBOLS + kvclib.BATCHED_SYMBOLS + kvclib.PEER_SYMBOLS)
     assert declared == listed
 
 

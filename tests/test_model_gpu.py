@@ -286,6 +286,36 @@ def test_multibatch_equals_single_batch(kvc, monkeypatch):
             assert s1[k] == s2[k], (k, s1[k], s2[k])
 
 
+def test_layers_of_different_lengths_in_one_call(kvc):
+    """Layers with their own token counts (kvc_layer_desc.n_tokens: a layer's
+    tail, a whole layer, another layer's head, as one GPU's share of a
+    partitioned model) in one call == each compacted alone, bit for bit."""
+    import torch
+    from kvc_b200 import lib, shard
+    T, H, d, ratio = 12000, 2, 64, 0.2
+    Kq, Vq, Q = _model(kvc, T, H, d, 2, abi.KV_TYPE_Q8_0, 31)
+    cs = shard.auto_chunk(T, ratio)
+    params = abi.make_params(kvc, target_ratio=ratio, chunk_size=cs)
+    pieces = [(0, 3 * cs, T), (1, 0, T), (0, 0, 2 * cs)]      # (layer, first token, end)
+    Ks = [Kq[l][a:b] for l, a, b in pieces]
+    Vs = [Vq[l][a:b] for l, a, b in pieces]
+    Qs = [Q[l] for l, _, _ in pieces]
+    tokens = [b - a for _, a, b in pieces]
+    mixed = lib.BatchedModel(kvc, Ks, Vs, Qs, max(tokens), H, d, d, 8, 8, params, tokens=tokens)
+    mixed.run(want_stats=True)
+    torch.cuda.synchronize()
+    for j in range(len(pieces)):
+        alone = lib.BatchedModel(kvc, [Ks[j]], [Vs[j]], [Qs[j]], tokens[j], H, d, d, 8, 8, params)
+        alone.run(want_stats=True)
+        torch.cuda.synchronize()
+        t = alone.t[0]
+        assert mixed.t[j] == t
+        assert torch.equal(mixed.sel[j][:t], alone.sel[0][:t])
+        assert torch.equal(mixed.beta[j][:H * t], alone.beta[0][:H * t])
+        assert torch.equal(mixed.cv[j][:H * t * d], alone.cv[0][:H * t * d])
+        assert torch.equal(mixed.kout[j], alone.kout[0]) and torch.equal(mixed.vout[j], alone.vout[0])
+
+
 def test_layer_filter_periodic(kvc):
     """params.layer_filter (periodic, interval 4) selects layers 3, 7 of 8."""
     from kvc_b200 import lib

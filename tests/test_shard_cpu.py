@@ -118,3 +118,47 @@ def test_gather_rebuilds_whole_model_arrays(world, overlapped):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert res[0]
+
+
+@pytest.mark.parametrize("world,extra", [(2, 0.0), (2, 0.05), (3, 0.05), (8, 0.05), (5, 0.3)])
+def test_weighted_partition_and_peer_copy_plan(world, extra):
+    """Rank 0's larger share (root_weights) keeps the partition exact, and the
+    peer copies of every rank's slices (put_ops, applied here to one host
+    buffer as rank 0's result buffer) rebuild the whole-model arrays."""
+    n_layers, T, ratio, H, kb, vb = 3, 5000, 0.2, 2, 34, 18
+    w = shard.root_weights(world, extra)
+    plan = shard.partition(n_layers, T, ratio, world, w)
+    chunks = shard.chunk_table(T, ratio)
+    seen = [(s.layer, c) for sl in plan for s in sl for c in range(s.c0, s.c1)]
+    assert seen == [(l, c) for l in range(n_layers) for c in range(len(chunks))]
+    loads = np.array([sum(s.tokens for s in sl) for sl in plan], dtype=float)
+    want = np.array(w) / sum(w) * n_layers * T
+    assert np.all(np.abs(loads - want) <= max(c[1] for c in chunks))
+    whole = _whole(n_layers, T, ratio, H, kb, vb)
+    layout, nbytes = shard.result_layout(n_layers, T, ratio, H, kb, vb)
+    buf = np.zeros(nbytes, dtype=np.uint8)
+    for r in range(world):
+        for s in plan[r]:
+            wl = whole[s.layer]
+            t = len(wl["sel"])
+            out = {"sel": (wl["sel"][s.out0:s.out1]).astype(np.int32).view(np.uint8),
+                   "beta": np.ascontiguousarray(wl["beta"].reshape(H, t)[:, s.out0:s.out1]).view(np.uint8).ravel(),
+                   "kout": wl["kout"][s.out0 * kb:s.out1 * kb], "vout": wl["vout"][s.out0 * vb:s.out1 * vb]}
+            for op in shard.put_ops(s, layout, T, ratio, H, kb, vb):
+                src = out[op[1]]
+                if op[0] == "1d":
+                    _, _, dst, so, n = op
+                    buf[dst:dst + n] = src[so:so + n]
+                else:
+                    _, _, dst, dp, sp, width, height = op
+                    for i in range(height):
+                        buf[dst + i * dp:dst + i * dp + width] = src[i * sp:i * sp + width]
+    for l in range(n_layers):
+        L = layout[l]
+        got = {k: buf[L[k][0]:L[k][0] + L[k][1]] for k in L}
+        assert np.array_equal(got["sel"].view(np.int32), whole[l]["sel"])
+        assert np.array_equal(got["beta"].view(np.float32), whole[l]["beta"])
+        assert np.array_equal(got["kout"], whole[l]["kout"])
+        assert np.array_equal(got["vout"], whole[l]["vout"])
+        offs = sorted(v[0] for v in L.values())
+        assert all(o % 256 == 0 for o in offs)
