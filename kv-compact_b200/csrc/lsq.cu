@@ -339,11 +339,6 @@ __global__ void __launch_bounds__(128) k_dgemm_async(const kvc_unit * __restrict
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j][0] = acc[i][j][1] = 0.0;
-    // a Gram tile on the diagonal keeps only its lower triangle: the warp
-    // whose 32 x 32 block lies above it skips its products, and the two
-    // warps on it skip their 8 x 8 tiles above it (the store drops them)
-    const bool diag = mode == DG_GRAM && m0 == n0;
-    const bool skip_all = diag && wn > wm, lower_only = diag && wn == wm;
     const int nslab = (K + DK - 1) / DK;
     issue(0, 0);
     if (nslab > 1) issue(DK, 1);
@@ -356,7 +351,6 @@ __global__ void __launch_bounds__(128) k_dgemm_async(const kvc_unit * __restrict
         const float * As = Asm + b * DG_STAGE_F;
         const double * Bd = Bsm + b * (DK * AM_LD);
         const float * Bf = reinterpret_cast<const float *>(Bd);
-        if (skip_all) continue;
 #pragma unroll
         for (int kk = 0; kk < DK; kk += 4) {
             double a[4], bb[4];
@@ -369,8 +363,7 @@ __global__ void __launch_bounds__(128) k_dgemm_async(const kvc_unit * __restrict
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 4; j++)
-                    if (!lower_only || j <= i) dmma(acc[i][j], a[i], bb[j]);
+                for (int j = 0; j < 4; j++) dmma(acc[i][j], a[i], bb[j]);
         }
     }
     if (mode == DG_GRAM) {
