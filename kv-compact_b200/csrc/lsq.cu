@@ -245,9 +245,13 @@ __device__ __forceinline__ void dg_cp16(void * smem, const void * gmem, int byte
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(sa), "l"(gmem), "r"(bytes) : "memory");
 }
 
+// One instantiation per product (MODE: DG_GRAM, DG_RHS, DG_OUT), so the Gram
+// product's triangle logic costs the other products nothing.
+template <int MODE>
 __global__ void __launch_bounds__(128) k_dgemm_async(const kvc_unit * __restrict__ units, kvc_params_dev P,
                                                      const float * __restrict__ fs, double * __restrict__ gs,
-                                                     const kvc_layer_out * __restrict__ outs, int mode) {
+                                                     const kvc_layer_out * __restrict__ outs) {
+    constexpr int mode = MODE;
     const kvc_unit u = units[blockIdx.z];
     if (!u.active) return;
     const int h = blockIdx.y;
@@ -339,6 +343,11 @@ __global__ void __launch_bounds__(128) k_dgemm_async(const kvc_unit * __restrict
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j][0] = acc[i][j][1] = 0.0;
+    // a Gram tile on the diagonal keeps only its lower triangle: the warp
+    // whose 32 x 32 block lies above it skips its products, and the two
+    // warps on it skip their 8 x 8 tiles above it (the store drops them)
+    const bool diag = mode == DG_GRAM && m0 == n0;
+    const bool skip_all = diag && wn > wm, lower_only = diag && wn == wm;
     const int nslab = (K + DK - 1) / DK;
     issue(0, 0);
     if (nslab > 1) issue(DK, 1);
@@ -351,6 +360,7 @@ __global__ void __launch_bounds__(128) k_dgemm_async(const kvc_unit * __restrict
         const float * As = Asm + b * DG_STAGE_F;
         const double * Bd = Bsm + b * (DK * AM_LD);
         const float * Bf = reinterpret_cast<const float *>(Bd);
+        if (skip_all) continue;
 #pragma unroll
         for (int kk = 0; kk < DK; kk += 4) {
             double a[4], bb[4];
@@ -363,7 +373,8 @@ __global__ void __launch_bounds__(128) k_dgemm_async(const kvc_unit * __restrict
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) dmma(acc[i][j], a[i], bb[j]);
+                for (int j = 0; j < 4; j++)
+                    if (!lower_only || j <= i) dmma(acc[i][j], a[i], bb[j]);
         }
     }
     if (mode == DG_GRAM) {
@@ -763,8 +774,10 @@ static int launch_dgemm(dim3 grid, const kvc_unit * d_units, const kvc_params_de
                         double * gs, const kvc_layer_out * d_outs, int mode, bool aligned, cudaStream_t st) {
     if (aligned) {
         const size_t sm = kvc_dgemm_async_smem();
-        KVC_CUDA(cudaFuncSetAttribute(k_dgemm_async, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        k_dgemm_async<<<grid, 128, sm, st>>>(d_units, P, fs, gs, d_outs, mode);
+        auto kern = mode == DG_GRAM ? k_dgemm_async<DG_GRAM> : (mode == DG_RHS ? k_dgemm_async<DG_RHS>
+                                                                               : k_dgemm_async<DG_OUT>);
+        KVC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        kern<<<grid, 128, sm, st>>>(d_units, P, fs, gs, d_outs);
     } else {
         k_dgemm<<<grid, 128, 0, st>>>(d_units, P, fs, gs, d_outs, mode);
     }
