@@ -36,46 +36,36 @@ constexpr int FN = 128;   // max unknowns of the shared-memory path (k_lsq_facto
 
 enum { DG_GRAM = 0, DG_RHS = 1, DG_OUT = 2 };
 
-// In-place inverse of a 4x4 block by its adjugate (cofactor expansion over
-// the 2x2 minors of the top and bottom row pairs) divided by the
-// determinant. Returns false, leaving `a` unchanged, unless the block is
-// positive definite by Sylvester's criterion (leading minors > 0) with a
-// finite determinant.
-__device__ __forceinline__ bool inverse4_spd(double (&a)[4][4]) {
-    const double s0 = a[0][0] * a[1][1] - a[1][0] * a[0][1], s1 = a[0][0] * a[1][2] - a[1][0] * a[0][2];
-    const double s2 = a[0][0] * a[1][3] - a[1][0] * a[0][3], s3 = a[0][1] * a[1][2] - a[1][1] * a[0][2];
-    const double s4 = a[0][1] * a[1][3] - a[1][1] * a[0][3], s5 = a[0][2] * a[1][3] - a[1][2] * a[0][3];
-    const double c5 = a[2][2] * a[3][3] - a[3][2] * a[2][3], c4 = a[2][1] * a[3][3] - a[3][1] * a[2][3];
-    const double c3 = a[2][1] * a[3][2] - a[3][1] * a[2][2], c2 = a[2][0] * a[3][3] - a[3][0] * a[2][3];
-    const double c1 = a[2][0] * a[3][2] - a[3][0] * a[2][2], c0 = a[2][0] * a[3][1] - a[3][0] * a[2][1];
+// In-place inverse of a symmetric 4x4 block, read from its upper triangle,
+// by its adjugate (cofactor expansion over the 2x2 minors of the top and
+// bottom row pairs) divided by the determinant; only the ten distinct
+// entries of the symmetric inverse are formed (the pivot blocks of the
+// elimination are the symmetric Schur complements of G + ridge I, equal to
+// their transposes up to rounding). Returns false, leaving `a` unchanged,
+// unless the block is positive definite by Sylvester's criterion (leading
+// minors > 0) with a finite determinant.
+__device__ __forceinline__ bool inverse4_sym(double (&a)[4][4]) {
+    const double a00 = a[0][0], a01 = a[0][1], a02 = a[0][2], a03 = a[0][3];
+    const double a11 = a[1][1], a12 = a[1][2], a13 = a[1][3], a22 = a[2][2], a23 = a[2][3], a33 = a[3][3];
+    const double s0 = a00 * a11 - a01 * a01, s1 = a00 * a12 - a01 * a02, s2 = a00 * a13 - a01 * a03;
+    const double s3 = a01 * a12 - a11 * a02, s4 = a01 * a13 - a11 * a03, s5 = a02 * a13 - a12 * a03;
+    const double c5 = a22 * a33 - a23 * a23, c4 = a12 * a33 - a13 * a23, c3 = a12 * a23 - a13 * a22;
+    const double c2 = a02 * a33 - a03 * a23, c1 = a02 * a23 - a03 * a22, c0 = a02 * a13 - a03 * a12;
     const double det = s0 * c5 - s1 * c4 + s2 * c3 + s3 * c2 - s4 * c1 + s5 * c0;
-    const double m3 = a[0][0] * (a[1][1] * a[2][2] - a[1][2] * a[2][1]) - a[0][1] * (a[1][0] * a[2][2] - a[1][2] * a[2][0]) +
-                      a[0][2] * (a[1][0] * a[2][1] - a[1][1] * a[2][0]);
-    if (!(a[0][0] > 0.0 && s0 > 0.0 && m3 > 0.0 && det > 0.0 && isfinite(det))) return false;
+    const double m3 = a00 * (a11 * a22 - a12 * a12) - a01 * (a01 * a22 - a12 * a02) + a02 * (a01 * a12 - a11 * a02);
+    if (!(a00 > 0.0 && s0 > 0.0 && m3 > 0.0 && det > 0.0 && isfinite(det))) return false;
     const double id = 1.0 / det;
-    double b[4][4];
-    b[0][0] = (a[1][1] * c5 - a[1][2] * c4 + a[1][3] * c3) * id;
-    b[0][1] = (-a[0][1] * c5 + a[0][2] * c4 - a[0][3] * c3) * id;
-    b[0][2] = (a[3][1] * s5 - a[3][2] * s4 + a[3][3] * s3) * id;
-    b[0][3] = (-a[2][1] * s5 + a[2][2] * s4 - a[2][3] * s3) * id;
-    b[1][0] = (-a[1][0] * c5 + a[1][2] * c2 - a[1][3] * c1) * id;
-    b[1][1] = (a[0][0] * c5 - a[0][2] * c2 + a[0][3] * c1) * id;
-    b[1][2] = (-a[3][0] * s5 + a[3][2] * s2 - a[3][3] * s1) * id;
-    b[1][3] = (a[2][0] * s5 - a[2][2] * s2 + a[2][3] * s1) * id;
-    b[2][0] = (a[1][0] * c4 - a[1][1] * c2 + a[1][3] * c0) * id;
-    b[2][1] = (-a[0][0] * c4 + a[0][1] * c2 - a[0][3] * c0) * id;
-    b[2][2] = (a[3][0] * s4 - a[3][1] * s2 + a[3][3] * s0) * id;
-    b[2][3] = (-a[2][0] * s4 + a[2][1] * s2 - a[2][3] * s0) * id;
-    b[3][0] = (-a[1][0] * c3 + a[1][1] * c1 - a[1][2] * c0) * id;
-    b[3][1] = (a[0][0] * c3 - a[0][1] * c1 + a[0][2] * c0) * id;
-    b[3][2] = (-a[3][0] * s3 + a[3][1] * s1 - a[3][2] * s0) * id;
-    b[3][3] = (a[2][0] * s3 - a[2][1] * s1 + a[2][2] * s0) * id;
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) a[i][j] = b[i][j];
+    const double b00 = (a11 * c5 - a12 * c4 + a13 * c3) * id, b01 = (-a01 * c5 + a02 * c4 - a03 * c3) * id;
+    const double b02 = (a13 * s5 - a23 * s4 + a33 * s3) * id, b03 = (-a12 * s5 + a22 * s4 - a23 * s3) * id;
+    const double b11 = (a00 * c5 - a02 * c2 + a03 * c1) * id, b12 = (-a03 * s5 + a23 * s2 - a33 * s1) * id;
+    const double b13 = (a02 * s5 - a22 * s2 + a23 * s1) * id, b22 = (a03 * s4 - a13 * s2 + a33 * s0) * id;
+    const double b23 = (-a02 * s4 + a12 * s2 - a23 * s0) * id, b33 = (a02 * s3 - a12 * s1 + a22 * s0) * id;
+    a[0][0] = b00; a[0][1] = a[1][0] = b01; a[0][2] = a[2][0] = b02; a[0][3] = a[3][0] = b03;
+    a[1][1] = b11; a[1][2] = a[2][1] = b12; a[1][3] = a[3][1] = b13;
+    a[2][2] = b22; a[2][3] = a[3][2] = b23; a[3][3] = b33;
     return true;
 }
+
 constexpr int DT = 64, DK = 16, DLD = 72;   // CTA tile, k slab, shared row stride (doubles)
 
 // D (8x8) += A (8x4) B (4x8) on the fp64 tensor cores (warp-wide). Lane l
@@ -644,13 +634,13 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
             for (int q = 0; q < 4; q++)
 #pragma unroll
                 for (int c = 0; c < 4; c++) T[q][c] = G[(k + q) * GLD + k + c];
-            asm volatile("bar.sync 1, 128;" ::: "memory");   // P read before its columns are rewritten
+            // (no barrier: P's own columns of G are not rewritten below)
             // inverse of the pivot block: the adjugate over the determinant
             // (one division, a short dependency chain) when the block is
             // positive definite, which every pivot block of G + ridge I is;
             // otherwise in-place Gauss-Jordan inversion, where a skipped
             // (non-positive) pivot leaves its row and column to be zeroed
-            if (!inverse4_spd(T)) {
+            if (!inverse4_sym(T)) {
             bool skip[4];
 #pragma unroll
             for (int q = 0; q < 4; q++) {
@@ -685,7 +675,10 @@ __global__ void __launch_bounds__(512, 1) k_lsq_factor(const kvc_unit * __restri
                 for (int q = 0; q < 4; q++) {
                     const double x = fma(T[q][0], g[0], fma(T[q][1], g[1], fma(T[q][2], g[2], T[q][3] * g[3])));
                     PR[q * PLD + j] = x;
-                    G[(k + q) * GLD + j] = x;
+                    // the pivot block's own columns are dead after this step;
+                    // leaving them unwritten lets every thread read P without
+                    // a barrier (tile updates below give them zero multipliers)
+                    if (j >= k + 4) G[(k + q) * GLD + j] = x;
                 }
             }
             double rp[4];
