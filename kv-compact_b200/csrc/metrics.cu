@@ -35,6 +35,17 @@ constexpr int MQ = 32;       // queries per head
 constexpr int MK = 128;      // keys per scoring CTA
 constexpr int MD = 32;       // d slab
 constexpr int PK = 32;       // keys per value tile
+constexpr int MWLD = PK + 4;  // row stride of a staged X tile (floats)
+
+// 16-byte asynchronous global -> shared copy of `bytes` (0..16) valid bytes, the rest zero-filled.
+__device__ __forceinline__ void mcp16(void * smem, const void * gmem, int bytes) {
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(sa), "l"(gmem), "r"(bytes) : "memory");
+}
+// dynamic shared memory of k_metric_partial: two X tiles and two C_v tiles
+inline size_t metric_partial_smem(bool hi) {
+    return (size_t)(2 * 32 * (32 + 4) + 2 * 32 * (hi ? 256 : 128)) * sizeof(float);
+}
 }  // namespace
 
 struct kvc_metric_args {
@@ -299,40 +310,76 @@ __global__ void __launch_bounds__(256, HI ? 2 : 4) k_metric_partial(const kvc_un
         const int q = e / dv, c = e % dv;
         out[(long long)q * rec + 4 + c] = Y[(long long)q * dv + c];
     }
-    // (X C_v)[q][c]: 8 query groups x 32 column groups, 4 queries x 4 (or 8) columns a thread
-    __shared__ __align__(16) float Ws[PK][MQ];
-    __shared__ __align__(16) float Vs[PK][KVC_MAX_D];
+    // (X C_v)[q][c]: 8 query groups x 32 column groups, 4 queries x 4 (or 8)
+    // columns a thread. Tiles of PK kept keys — X's [q][j] rows and C_v's
+    // [j][c] rows, both in their own layout — arrive by 16-byte asynchronous
+    // copies into two buffers, the next tile in flight while the current one
+    // is multiplied; keys are summed in the same order either way.
+    constexpr int DVP = HI ? 2 * 128 : 128;
+    extern __shared__ __align__(16) float msm[];
+    float * Wt = msm;                                  // [2][MQ][MWLD]
+    float * Vt = msm + 2 * MQ * MWLD;                  // [2][PK][DVP]
     const int qg = tid >> 5, cg = tid & 31;
     float acc[4][NC];
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int c = 0; c < NC; c++) acc[i][c] = 0.0f;
-    for (int j0 = 0; j0 < t; j0 += PK) {
-        for (int e = tid; e < MQ * PK; e += 256) {
-            const int qq = e / PK, jj = e % PK;
-            Ws[jj][qq] = (qq < mq && j0 + jj < t) ? X[(long long)qq * t + j0 + jj] : 0.0f;
+    const bool vec = (t % 4 == 0) && (dv % 4 == 0) && ((((uintptr_t)X) | ((uintptr_t)cv)) & 15) == 0;
+    auto stage = [&](int j0, int b) {
+        float * W = Wt + b * MQ * MWLD;
+        float * V = Vt + b * PK * DVP;
+        if (vec) {
+            for (int e = tid; e < MQ * (PK / 4); e += 256) {
+                const int qq = e / (PK / 4), c4 = e % (PK / 4), j = j0 + 4 * c4;
+                const int bytes = (qq < mq && j < t) ? 4 * min(4, t - j) : 0;
+                mcp16(W + qq * MWLD + 4 * c4, bytes ? X + (long long)qq * t + j : X, bytes);
+            }
+            for (int e = tid; e < PK * (dv / 4); e += 256) {
+                const int jj = e / (dv / 4), c4 = e % (dv / 4), j = j0 + jj;
+                const int bytes = j < t ? 16 : 0;
+                mcp16(V + jj * DVP + 4 * c4, bytes ? cv + (long long)j * dv + 4 * c4 : cv, bytes);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        } else {
+            for (int e = tid; e < MQ * PK; e += 256) {
+                const int qq = e / PK, jj = e % PK;
+                W[qq * MWLD + jj] = (qq < mq && j0 + jj < t) ? X[(long long)qq * t + j0 + jj] : 0.0f;
+            }
+            for (int e = tid; e < PK * dv; e += 256) {
+                const int jj = e / dv, c = e % dv;
+                V[jj * DVP + c] = (j0 + jj < t) ? cv[(long long)(j0 + jj) * dv + c] : 0.0f;
+            }
         }
-        for (int e = tid; e < PK * dv; e += 256) {
-            const int jj = e / dv, c = e % dv;
-            Vs[jj][c] = (j0 + jj < t) ? cv[(long long)(j0 + jj) * dv + c] : 0.0f;
+    };
+    const int nst = (t + PK - 1) / PK;
+    if (nst > 0) stage(0, 0);
+    for (int st = 0; st < nst; st++) {
+        const int j0 = st * PK, b = st & 1;
+        if (st + 1 < nst) stage(j0 + PK, b ^ 1);
+        if (vec) {
+            if (st + 1 < nst) asm volatile("cp.async.wait_group 1;" ::: "memory");
+            else asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
+        const float * W = Wt + b * MQ * MWLD;
+        const float * V = Vt + b * PK * DVP;
         const int jn = min(PK, t - j0);
 #pragma unroll 4
         for (int jj = 0; jj < jn; jj++) {
-            const float4 w4 = *reinterpret_cast<const float4 *>(&Ws[jj][4 * qg]);
-            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+            float wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) wv[i] = W[(4 * qg + i) * MWLD + jj];
             float vv[NC];
             if (4 * cg < dv) {
-                const float4 v4 = *reinterpret_cast<const float4 *>(&Vs[jj][4 * cg]);
+                const float4 v4 = *reinterpret_cast<const float4 *>(V + jj * DVP + 4 * cg);
                 vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
             } else {
                 vv[0] = vv[1] = vv[2] = vv[3] = 0.0f;
             }
             if (HI) {
                 if (128 + 4 * cg < dv) {
-                    const float4 v4 = *reinterpret_cast<const float4 *>(&Vs[jj][128 + 4 * cg]);
+                    const float4 v4 = *reinterpret_cast<const float4 *>(V + jj * DVP + 128 + 4 * cg);
                     vv[NC - 4] = v4.x; vv[NC - 3] = v4.y; vv[NC - 2] = v4.z; vv[NC - 1] = v4.w;
                 } else {
                     vv[NC - 4] = vv[NC - 3] = vv[NC - 2] = vv[NC - 1] = 0.0f;
@@ -343,7 +390,7 @@ __global__ void __launch_bounds__(256, HI ? 2 : 4) k_metric_partial(const kvc_un
 #pragma unroll
                 for (int c = 0; c < NC; c++) acc[i][c] = fmaf(wv[i], vv[c], acc[i][c]);
         }
-        __syncthreads();
+        __syncthreads();                            // buffer b is restaged two tiles later
     }
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -529,8 +576,13 @@ int kvc_launch_metric_partial(const kvc_unit * d_units, int n_units, const kvc_p
                               const kvc_layer_out * d_outs, cudaStream_t st) {
     const int mh = P.H < 4 ? P.H : 4;
     if (n_units <= 0 || mh <= 0) return KVC_OK;
-    if (P.dv > 128) k_metric_partial<true><<<dim3(n_units, mh), 256, 0, st>>>(d_units, P, fs, d_outs);
-    else k_metric_partial<false><<<dim3(n_units, mh), 256, 0, st>>>(d_units, P, fs, d_outs);
+    if (P.dv > 128) {
+        KVC_CUDA(cudaFuncSetAttribute(k_metric_partial<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)metric_partial_smem(true)));
+        k_metric_partial<true><<<dim3(n_units, mh), 256, metric_partial_smem(true), st>>>(d_units, P, fs, d_outs);
+    } else {
+        k_metric_partial<false><<<dim3(n_units, mh), 256, metric_partial_smem(false), st>>>(d_units, P, fs, d_outs);
+    }
     KVC_CUDA(cudaGetLastError());
     return KVC_OK;
 }
