@@ -309,8 +309,9 @@ def stage_rooflines(stage_times, cfg, n_steps, clocks, peaks, slices, fp64_tflop
         "softmax_importance": ("k_row_importance", "hbm", "GB/s", 4.0 * nq * tokens * H, hbm, hbm_src),
         "decode": ("k_decode_span", "hbm", "GB/s",
                    tokens * H * d * (kb + 4.0) + (0.0 if v_blocks else tokens * H * d * (vb + 4.0)), hbm, hbm_src),
-        "requant": ("k_encode_gather + k_encode_heads", "hbm", "GB/s",
-                    8.0 * t * H * d + t * H * d * (kb + vb), hbm, hbm_src),
+        # K_out: kept K rows read and written in their stored format; V_out: C_v read (fp32), rows written
+        "requant": ("k_transcode_rows_batch + k_encode_heads_batch", "hbm", "GB/s",
+                    t * H * d * (2.0 * kb + 4.0 + vb), hbm, hbm_src),
         "ls_gram": ("k_dgemm (Gram)", "tensor", "TFLOP/s", 2.0 * per_h(gram), fp64, fp64_src),
         "ls_factor": ("k_lsq_factor", "tensor", "TFLOP/s", 2.0 * per_h(fac), fp64, fp64_src),
         "ls_out": ("k_dgemm (C_v = X^T Z)", "tensor", "TFLOP/s", 2.0 * per_h(outp), fp64, fp64_src),

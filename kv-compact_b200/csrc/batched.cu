@@ -191,11 +191,43 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
     std::vector<const float *> m_parts;
     std::vector<int> m_chunks;
     std::vector<float *> m_res;
+    // requantisation of every layer in one launch per codec where the
+    // layers allow it (else per layer below)
+    bool rq_done = false;
+    {
+        std::vector<const uint8_t *> ks(n);
+        std::vector<const int *> sl(n);
+        std::vector<int> ts(n);
+        std::vector<uint8_t *> kd(n), vd(n);
+        std::vector<const float *> cvs(n);
+        bool all_k = true, all_v = true, any_k = false, any_v = false;
+        for (int i = 0; i < n; i++) {
+            const int l = on[i];
+            ks[i] = (const uint8_t *)L[l].K;
+            sl[i] = R[l].selected_indices;
+            ts[i] = plans[i].t_total;
+            kd[i] = R[l].K_out;
+            vd[i] = R[l].V_out;
+            cvs[i] = R[l].C_v;
+            all_k = all_k && kd[i];
+            all_v = all_v && vd[i];
+            any_k = any_k || kd[i];
+            any_v = any_v || vd[i];
+        }
+        if (k_blocks && all_k == any_k && all_v == any_v && (any_k || any_v)) {
+            kvc_stage_timer tm(ctx, KVC_ST_REQUANT, (any_k ? 1 : 0) + (any_v ? 1 : 0));
+            rc = kvc_launch_requant_batch(n, ks.data(), sl.data(), ts.data(), any_k ? kd.data() : nullptr,
+                                          m->k_row_bytes, ek, m->k_type, cvs.data(), any_v ? vd.data() : nullptr,
+                                          m->v_row_bytes, H, dv, m->v_type, st);
+            if (rc == KVC_OK) rq_done = true;
+            else if (rc != KVC_ERR_SHAPE) return rc;
+        }
+    }
     for (int i = 0; i < n; i++) {
         const int l = on[i];
         const int t = plans[i].t_total;
         R[l].t = t;
-        if (R[l].K_out) {
+        if (R[l].K_out && !rq_done) {
             kvc_stage_timer tm(ctx, KVC_ST_REQUANT, 1);
             rc = k_blocks ? kvc_launch_transcode_gather((const uint8_t *)L[l].K, m->k_row_bytes,
                                                         R[l].selected_indices, t, ek, m->k_type, R[l].K_out,
@@ -204,7 +236,7 @@ KVC_EXPORT int kvc_compact_layers_dev(const kvc_model_desc * m, const kvc_layer_
                                                      m->k_type, R[l].K_out, m->k_row_bytes, st);
             if (rc) return rc;
         }
-        if (R[l].V_out) {
+        if (R[l].V_out && !rq_done) {
             kvc_stage_timer tm(ctx, KVC_ST_REQUANT, 1);
             if ((rc = kvc_launch_encode_heads(R[l].C_v, H, t, t, dv, m->v_type, R[l].V_out, m->v_row_bytes, st)))
                 return rc;

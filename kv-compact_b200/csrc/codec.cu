@@ -712,6 +712,145 @@ __global__ void __launch_bounds__(TR_WARPS * 32) k_transcode_rows(const uint8_t 
     }
 }
 
+// Every layer of a call in one launch (the per-layer launches of a whole
+// model are 10-30 us each and spend part of that in their tail): a table of
+// up to KVC_RQ_MAX_LAYERS layers, passed by value, with the first work item
+// of each layer (rows for the transcode, 64-block spans for the encode);
+// each work item is done exactly as by the per-layer kernels.
+struct kvc_rq_batch {
+    int n;
+    long long start[KVC_RQ_MAX_LAYERS + 1];
+    const void * src[KVC_RQ_MAX_LAYERS];
+    const int * idx[KVC_RQ_MAX_LAYERS];
+    uint8_t * dst[KVC_RQ_MAX_LAYERS];
+    int t[KVC_RQ_MAX_LAYERS];
+};
+
+template <int TYPE>
+__global__ void __launch_bounds__(TR_WARPS * 32) k_transcode_rows_batch(const __grid_constant__ kvc_rq_batch B,
+                                                                        size_t rb, int nb) {
+    constexpr int BB = TYPE == 8 ? 34 : (TYPE == 2 ? 18 : 20);
+    __shared__ __align__(16) uint8_t sin[TR_WARPS][TR_MAX_RB], sout[TR_WARPS][TR_MAX_RB];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nv = (int)(rb / 16);
+    int l = 0;
+    for (long long g = (long long)blockIdx.x * TR_WARPS + warp; g < B.start[B.n]; g += (long long)gridDim.x * TR_WARPS) {
+        while (g >= B.start[l + 1]) l++;           // rows only increase along the loop
+        const long long r = g - B.start[l];
+        const uint4 * s = reinterpret_cast<const uint4 *>((const uint8_t *)B.src[l] + (size_t)B.idx[l][r] * rb);
+        for (int i = lane; i < nv; i += 32) reinterpret_cast<uint4 *>(sin[warp])[i] = s[i];
+        __syncwarp();
+        for (int b = lane; b < nb; b += 32) {
+            float x[QK];
+            decode_block(sin[warp] + b * BB, TYPE, x);
+            encode_block(x, TYPE, sout[warp] + b * BB);
+        }
+        __syncwarp();
+        uint4 * o = reinterpret_cast<uint4 *>(B.dst[l] + (size_t)r * rb);
+        for (int i = lane; i < nv; i += 32) o[i] = reinterpret_cast<const uint4 *>(sout[warp])[i];
+        __syncwarp();
+    }
+}
+
+// k_encode_span<TYPE, 1> over every layer: span sp of layer l covers blocks
+// 64 (sp - start[l]) .. of that layer's t rows x nb blocks.
+template <int TYPE>
+__global__ void __launch_bounds__(256) k_encode_heads_batch(const __grid_constant__ kvc_rq_batch B, int dv, int nb) {
+    constexpr int BB = TYPE == 8 ? 34 : (TYPE == 2 ? 18 : 20);
+    constexpr int SPB = 64, SB = SPB * BB, NV = SB / 16;
+    __shared__ __align__(16) uint8_t sb[SB + BB + 14];
+    const int blk = threadIdx.x >> 2, part = threadIdx.x & 3;
+    int l = 0;
+    for (long long sp = blockIdx.x; sp < B.start[B.n]; sp += gridDim.x) {
+        while (sp >= B.start[l + 1]) l++;
+        const int t = B.t[l];
+        const long long nblocks = (long long)t * nb;
+        const long long b0 = (sp - B.start[l]) * SPB;
+        const int nbk = (int)min((long long)SPB, nblocks - b0);
+        const bool live = blk < nbk;
+        float x[8];
+        if (live) {
+            const long long gb = b0 + blk, r = gb / nb;
+            const int b = (int)(gb - r * nb);
+            const int e0 = b * QK, h = e0 / dv;
+            const float * p = (const float *)B.src[l] + ((long long)h * t + r) * dv + (e0 - h * dv) + 8 * part;
+            const float4 u0 = *reinterpret_cast<const float4 *>(p), u1 = *reinterpret_cast<const float4 *>(p + 4);
+            x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
+            x[4] = u1.x; x[5] = u1.y; x[6] = u1.z; x[7] = u1.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) x[i] = 0.0f;
+        }
+        const float x0 = __shfl_sync(0xffffffffu, x[0], threadIdx.x & 28);
+        encode_oct<TYPE>(x, x0, part, sb + (live ? blk * BB : SB));
+        __syncthreads();
+        const int nbytes = nbk * BB;
+        uint8_t * d = B.dst[l] + b0 * BB;
+        if (threadIdx.x < NV) {
+            const int o = threadIdx.x * 16;
+            if (o + 16 <= nbytes) *reinterpret_cast<uint4 *>(d + o) = *reinterpret_cast<const uint4 *>(sb + o);
+            else
+                for (int i = o; i < nbytes && i < o + 16; i++) d[i] = sb[i];
+        }
+        __syncthreads();
+    }
+}
+
+int kvc_launch_requant_batch(int n, const uint8_t * const * k_src, const int * const * sel, const int * t,
+                             uint8_t * const * k_dst, size_t k_rb, int ek, int k_type, const float * const * cv,
+                             uint8_t * const * v_dst, size_t v_rb, int H, int dv, int v_type, cudaStream_t st) {
+    if (n <= 0) return KVC_OK;
+    if (n > KVC_RQ_MAX_LAYERS) return KVC_ERR_SHAPE;
+    const bool k_on = k_dst != nullptr, v_on = v_dst != nullptr;
+    if (k_on && !(is_block(k_type) && k_rb % 16 == 0 && k_rb <= (size_t)TR_MAX_RB &&
+                  k_rb == (size_t)(ek / QK) * (size_t)kvc_block_bytes(k_type)))
+        return KVC_ERR_SHAPE;
+    if (v_on && !(is_block(v_type) && dv % QK == 0 && v_rb == (size_t)((H * dv) / QK) * (size_t)kvc_block_bytes(v_type)))
+        return KVC_ERR_SHAPE;
+    for (int i = 0; i < n; i++) {
+        if (k_on && ((((uintptr_t)k_src[i]) | ((uintptr_t)k_dst[i])) & 15)) return KVC_ERR_SHAPE;
+        if (v_on && ((((uintptr_t)cv[i]) | ((uintptr_t)v_dst[i])) & 15)) return KVC_ERR_SHAPE;
+    }
+    if (k_on) {
+        kvc_rq_batch B{};
+        B.n = n;
+        for (int i = 0; i < n; i++) {
+            B.start[i + 1] = B.start[i] + t[i];
+            B.src[i] = k_src[i];
+            B.idx[i] = sel[i];
+            B.dst[i] = k_dst[i];
+            B.t[i] = t[i];
+        }
+        const int grid = (int)std::min<long long>((B.start[n] + TR_WARPS - 1) / TR_WARPS, 148LL * 8);
+        if (grid > 0) {
+            if (k_type == 8) k_transcode_rows_batch<8><<<grid, TR_WARPS * 32, 0, st>>>(B, k_rb, ek / QK);
+            else if (k_type == 2) k_transcode_rows_batch<2><<<grid, TR_WARPS * 32, 0, st>>>(B, k_rb, ek / QK);
+            else k_transcode_rows_batch<3><<<grid, TR_WARPS * 32, 0, st>>>(B, k_rb, ek / QK);
+            KVC_CUDA(cudaGetLastError());
+        }
+    }
+    if (v_on) {
+        const int nb = (H * dv) / QK;
+        kvc_rq_batch B{};
+        B.n = n;
+        for (int i = 0; i < n; i++) {
+            B.start[i + 1] = B.start[i] + ((long long)t[i] * nb + 63) / 64;
+            B.src[i] = cv[i];
+            B.idx[i] = nullptr;
+            B.dst[i] = v_dst[i];
+            B.t[i] = t[i];
+        }
+        const int grid = (int)std::min<long long>(B.start[n], 148LL * 32);
+        if (grid > 0) {
+            if (v_type == 8) k_encode_heads_batch<8><<<grid, 256, 0, st>>>(B, dv, nb);
+            else if (v_type == 2) k_encode_heads_batch<2><<<grid, 256, 0, st>>>(B, dv, nb);
+            else k_encode_heads_batch<3><<<grid, 256, 0, st>>>(B, dv, nb);
+            KVC_CUDA(cudaGetLastError());
+        }
+    }
+    return KVC_OK;
+}
+
 int kvc_launch_transcode_gather(const uint8_t * src, size_t src_rb, const int * idx, int rows, int n, int type,
                                 uint8_t * dst, size_t dst_rb, cudaStream_t st) {
     if (rows <= 0) return KVC_OK;

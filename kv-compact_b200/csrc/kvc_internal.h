@@ -55,6 +55,8 @@ enum {
 // The beta fit and OMP selection keep their own bound (KVC_NNLS_MAX_N).
 #define KVC_LSQ_MAX_N 24576
 #define KVC_NNLS_MAX_N 3072
+// Most layers of one batched requantisation launch (kvc_launch_requant_batch).
+#define KVC_RQ_MAX_LAYERS 64
 
 struct kvc_unit {
     const float * K;      // first row of the chunk, row stride ek = H*d_k
@@ -173,3 +175,11 @@ int kvc_launch_transcode_gather(const uint8_t * src, size_t src_rb, const int * 
 // V_out rows 0..rows-1 from cv[h][j][:] (heads t rows apart).
 int kvc_launch_encode_heads(const float * cv, int H, int t, int rows, int dv, int type, uint8_t * dst,
                             size_t dst_row_bytes, cudaStream_t st);
+// The K_out transcode (k_dst != nullptr) and the V_out encode (v_dst !=
+// nullptr) of n layers in one launch each, the same bytes as the per-layer
+// kvc_launch_transcode_gather / kvc_launch_encode_heads. Returns
+// KVC_ERR_SHAPE, launching nothing, where a layer needs the general kernels
+// (types, row sizes, alignment; more than KVC_RQ_MAX_LAYERS layers).
+int kvc_launch_requant_batch(int n, const uint8_t * const * k_src, const int * const * sel, const int * t,
+                             uint8_t * const * k_dst, size_t k_rb, int ek, int k_type, const float * const * cv,
+                             uint8_t * const * v_dst, size_t v_rb, int H, int dv, int v_type, cudaStream_t st);
