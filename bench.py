@@ -307,6 +307,10 @@ def stage_rooflines(stage_times, cfg, n_steps, clocks, peaks, slices, fp64_tflop
                          (4.0 * nq + v_read * d) * tokens * H + 4.0 * nq * d * H * len(units), hbm, hbm_src),
         # the scores are read (once, at least) and nothing of their size is written
         "softmax_importance": ("k_row_importance", "hbm", "GB/s", 4.0 * nq * tokens * H, hbm, hbm_src),
+        # X = softmax(S[:, sel]): with a fifth of the keys kept, nearly every 32-byte
+        # sector of S holds a kept score, so the bytes that must move are all of S
+        # (read) and X (written)
+        "x_build": ("k_gather_softmax_x_reg", "hbm", "GB/s", 4.0 * nq * (tokens + t) * H, hbm, hbm_src),
         "decode": ("k_decode_span", "hbm", "GB/s",
                    tokens * H * d * (kb + 4.0) + (0.0 if v_blocks else tokens * H * d * (vb + 4.0)), hbm, hbm_src),
         # K_out: kept K rows read and written in their stored format; V_out: C_v read (fp32), rows written
