@@ -41,24 +41,34 @@ template <int DV>
 constexpr uint32_t pv_tmem_cols() { return DV <= 32 ? 32 : (DV <= 64 ? 64 : (DV <= 128 ? 128 : 256)); }
 }  // namespace
 
-// Value n of row `row` of a V matrix kept in its block format (VT: 8 Q8_0,
-// 2 Q4_0, 3 Q4_1; head h's values start at block h * DV / 32), with the
-// arithmetic of the codec's decode (separately rounded multiply and add):
-// the same fp32 value a decoded V row holds.
+// Raw bytes of value n of head h in a V row kept in its block format (VT: 8
+// Q8_0, 2 Q4_0, 3 Q4_1; head h's values start at block h * DV / 32), packed
+// for key slot e of a four-key unit: the code byte into byte e of w[0], the
+// block's fp16 scale into half e & 1 of w[1 + e / 2], the Q4_1 minimum into
+// half e & 1 of w[3 + e / 2].
 template <int VT, int DV>
-__device__ __forceinline__ float vq_value(const uint8_t * __restrict__ row, int h, int n) {
+__device__ __forceinline__ void vq_raw(const uint8_t * __restrict__ row, int h, int n, int e, uint32_t * w) {
     constexpr int BB = VT == 8 ? 34 : (VT == 2 ? 18 : 20);
     const uint8_t * blk = row + (h * (DV / 32) + (n >> 5)) * BB;
     const int i = n & 31;
-    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(blk)));
-    if (VT == 8) return __fmul_rn(d, (float)(int8_t)blk[2 + i]);
-    if (VT == 2) {
-        const uint8_t q = blk[2 + (i >> 1)];
-        return __fmul_rn(d, __fsub_rn((float)((i & 1) ? q >> 4 : q & 0xF), 8.0f));
-    }
-    const float m = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(blk + 2)));
-    const uint8_t q = blk[4 + (i >> 1)];
-    return __fadd_rn(__fmul_rn(d, (float)((i & 1) ? q >> 4 : q & 0xF)), m);
+    const uint32_t code = VT == 8 ? blk[2 + i] : blk[(VT == 2 ? 2 : 4) + (i >> 1)];
+    w[0] |= code << (8 * e);
+    w[1 + (e >> 1)] |= (uint32_t)(*reinterpret_cast<const unsigned short *>(blk)) << (16 * (e & 1));
+    if (VT == 3) w[3 + (e >> 1)] |= (uint32_t)(*reinterpret_cast<const unsigned short *>(blk + 2)) << (16 * (e & 1));
+}
+
+// The value of key slot e from vq_raw's packing, with the arithmetic of the
+// codec's decode (separately rounded multiply and add): the same fp32 value a
+// decoded V row holds. An empty slot (zero scale and minimum) gives 0.
+template <int VT>
+__device__ __forceinline__ float vq_cook(const uint32_t * w, int n, int e) {
+    const float d = __half2float(__ushort_as_half((unsigned short)(w[1 + (e >> 1)] >> (16 * (e & 1)))));
+    const uint32_t q = (w[0] >> (8 * e)) & 0xFFu;
+    if (VT == 8) return __fmul_rn(d, (float)(int8_t)q);
+    const uint32_t nib = (n & 1) ? q >> 4 : q & 0xFu;
+    if (VT == 2) return __fmul_rn(d, __fsub_rn((float)nib, 8.0f));
+    const float m = __half2float(__ushort_as_half((unsigned short)(w[3 + (e >> 1)] >> (16 * (e & 1)))));
+    return __fadd_rn(__fmul_rn(d, (float)nib), m);
 }
 
 // One (unit, head) tile. FULL: every query row exists (n_q = 128), every
@@ -123,7 +133,13 @@ __device__ __forceinline__ void pv_tile(const kvc_unit & u, const int h, const k
     // is converted into shared memory (one stage of loads per thread alone
     // leaves too few bytes in flight to keep HBM busy)
     float4 ra[2][4];
-    float rb[2][NPB][4];
+    float rb[2][NPB][4];                               // fp32 V (VT 0)
+    // block-format V (VT != 0): the raw bytes, turned into values only when
+    // the stage is stored (two stages after the loads were issued), so no
+    // warp waits on its V loads: [0] = the four codes (key e in byte e),
+    // [1], [2] = the fp16 scales of keys 0-1 and 2-3, [3], [4] = their Q4_1
+    // minima
+    uint32_t rv[2][NPB][VT == 3 ? 5 : 3];
     auto load = [&](int s, int p) {
         const int k0 = s * PV_KS;
 #pragma unroll
@@ -153,10 +169,17 @@ __device__ __forceinline__ void pv_tile(const kvc_unit & u, const int h, const k
             const int n = idx % DV, kq = idx / DV;
             const int k = k0 + 4 * kq;
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                if (!FULL && k + e >= C) rb[p][pb][e] = 0.0f;
-                else if (VT) rb[p][pb][e] = vq_value<VT, DV>(u.Vq + (long long)(k + e) * P.v_rb, h, n);
-                else rb[p][pb][e] = V[(long long)(k + e) * ev + n];
+            if (VT) {
+                uint32_t w[VT == 3 ? 5 : 3] = {};
+                for (int e = 0; e < 4; e++) {
+                    if (!FULL && k + e >= C) continue;          // zero scale (and minimum): value 0
+                    vq_raw<VT, DV>(u.Vq + (long long)(k + e) * P.v_rb, h, n, e, w);
+                }
+#pragma unroll
+                for (int i = 0; i < (VT == 3 ? 5 : 3); i++) rv[p][pb][i] = w[i];
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++) rb[p][pb][e] = (!FULL && k + e >= C) ? 0.0f : V[(long long)(k + e) * ev + n];
             }
         }
     };
@@ -184,11 +207,19 @@ __device__ __forceinline__ void pv_tile(const kvc_unit & u, const int h, const k
             const int idx = pb * 128 + tid;
             const int n = idx % DV, kq = idx / DV;
             const uint32_t off = (n >> 3) * PV_SBO + kq * PV_LBO + (n & 7) * 16;
+            float v[4];
+            if (VT) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) v[e] = vq_cook<VT>(rv[p][pb], n, e);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++) v[e] = rb[p][pb][e];
+            }
             float4 hi, lo;
-            tf32_split(rb[p][pb][0], hi.x, lo.x);
-            tf32_split(rb[p][pb][1], hi.y, lo.y);
-            tf32_split(rb[p][pb][2], hi.z, lo.z);
-            tf32_split(rb[p][pb][3], hi.w, lo.w);
+            tf32_split(v[0], hi.x, lo.x);
+            tf32_split(v[1], hi.y, lo.y);
+            tf32_split(v[2], hi.z, lo.z);
+            tf32_split(v[3], hi.w, lo.w);
             *reinterpret_cast<float4 *>(base + 2 * A_BYTES + off) = hi;
             *reinterpret_cast<float4 *>(base + 2 * A_BYTES + B_BYTES + off) = lo;
         }
