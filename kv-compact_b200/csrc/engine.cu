@@ -717,6 +717,8 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         int max_nq = 1, max_C = 1, max_t = 1, max_n = 1;
         bool any_primal = false, any_dual = false, lsq_aligned = true;
         size_t lsq_smem = 0;
+        size_t p0 = 0;                           // its primal units' copies in the device unit table
+        int n_primal = 0;
         int row0 = 0, row1 = 0;                  // token rows (streamed job)
         int out0 = 0, out1 = 0;                  // kept-key rows (streamed job)
     };
@@ -785,7 +787,7 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             bt.max_t = std::max(bt.max_t, pu.t);
             bt.max_n = std::max(bt.max_n, n);
             if (pu.nq < pu.t) bt.any_dual = true;
-            else bt.any_primal = true;
+            else { bt.any_primal = true; bt.n_primal++; }
             if (pu.t % 4) bt.lsq_aligned = false;
             bt.lsq_smem = std::max(bt.lsq_smem, kvc_lsq_smem_bytes(n));
             if (bt.U.empty()) { bt.row0 = pu.start; bt.out0 = off; }
@@ -829,7 +831,12 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
     float * F = (float *)a0;
     int * I = (int *)a1;
     double * G = (double *)a2;
-    const size_t n_table = all.size() + (shared ? 1 : 0);
+    // the unit table: every batch's units, the shared-selection unit, then a
+    // copy of each batch's primal units (the primal right-hand side product
+    // launches over those alone)
+    size_t n_primal_all = 0;
+    for (const batch & bt : B) n_primal_all += bt.n_primal;
+    const size_t n_table = all.size() + (shared ? 1 : 0) + n_primal_all;
     if (ctx->units_cap < n_table) {
         if (ctx->d_units) { KVC_CUDA(cudaStreamSynchronize(st)); cudaFree(ctx->d_units); }
         ctx->units_cap = n_table * 2;
@@ -840,6 +847,11 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
         table.reserve(n_table);
         for (const batch & bt : B) table.insert(table.end(), bt.U.begin(), bt.U.end());
         if (shared) table.push_back(sh_unit);
+        for (batch & bt : B) {
+            bt.p0 = table.size();
+            for (const kvc_unit & u : bt.U)
+                if (u.nq >= u.t) table.push_back(u);
+        }
         KVC_CUDA(cudaMemcpyAsync(ctx->d_units, table.data(), table.size() * sizeof(kvc_unit),
                                  cudaMemcpyHostToDevice, st));
     }
@@ -951,7 +963,8 @@ int kvc_engine_run(kvc_ctx * ctx, const kv_compact_params & p, int H, int dk, in
             }
             {
                 kvc_stage_timer tm(ctx, KVC_ST_LSQ, bt.any_primal ? 2 : 1, s);
-                if ((e = kvc_launch_lsq_gram(du, nu, max_n, max_t, P, F, G, ctx->d_outs, bt.any_primal,
+                if ((e = kvc_launch_lsq_gram(du, nu, max_n, max_t, P, F, G, ctx->d_outs, ctx->d_units + bt.p0,
+                                             bt.n_primal,
                                              bt.lsq_aligned, s)))
                     return e;
             }

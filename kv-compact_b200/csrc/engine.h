@@ -314,9 +314,11 @@ size_t kvc_lsq_smem_bytes(int n);
 // `any_primal` / `any_dual`: whether some unit solves the primal (t <= n_q) /
 // dual form; launches only one form needs are skipped otherwise.
 // `aligned`: every unit's t and d_v are multiples of 4 (asynchronous-copy variant).
+// Gram matrices of every unit; the primal right-hand side X^T Y of the units
+// in d_primal[0 .. n_primal) (copies of the primal ones among d_units).
 int kvc_launch_lsq_gram(const kvc_unit * d_units, int n_units, int max_n, int max_t, const kvc_params_dev & P,
-                        const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_primal,
-                        bool aligned, cudaStream_t st);
+                        const float * fs, double * gs, const kvc_layer_out * d_outs, const kvc_unit * d_primal,
+                        int n_primal, bool aligned, cudaStream_t st);
 int kvc_launch_lsq_factor(const kvc_unit * d_units, int n_units, int max_n, size_t smem_bytes,
                           const kvc_params_dev & P, const float * fs, double * gs,
                           const kvc_layer_out * d_outs, cudaStream_t st);

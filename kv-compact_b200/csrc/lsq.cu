@@ -779,15 +779,15 @@ static int launch_dgemm(dim3 grid, const kvc_unit * d_units, const kvc_params_de
 }
 
 int kvc_launch_lsq_gram(const kvc_unit * d_units, int n_units, int max_n, int max_t, const kvc_params_dev & P,
-                        const float * fs, double * gs, const kvc_layer_out * d_outs, bool any_primal,
-                        bool aligned, cudaStream_t st) {
+                        const float * fs, double * gs, const kvc_layer_out * d_outs, const kvc_unit * d_primal,
+                        int n_primal, bool aligned, cudaStream_t st) {
     if (n_units <= 0) return KVC_OK;
     const int tg = (max_n + DT - 1) / DT;
     int rc;
     if ((rc = launch_dgemm(dim3(tg * tg, P.H, n_units), d_units, P, fs, gs, d_outs, DG_GRAM, aligned, st))) return rc;
-    if (any_primal) {
+    if (n_primal > 0) {
         const int to = ((max_t + DT - 1) / DT) * ((P.dv + DT - 1) / DT);
-        if ((rc = launch_dgemm(dim3(to, P.H, n_units), d_units, P, fs, gs, d_outs, DG_RHS, aligned, st))) return rc;
+        if ((rc = launch_dgemm(dim3(to, P.H, n_primal), d_primal, P, fs, gs, d_outs, DG_RHS, aligned, st))) return rc;
     }
     return KVC_OK;
 }

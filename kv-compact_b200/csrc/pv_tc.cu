@@ -168,9 +168,9 @@ __device__ __forceinline__ void pv_tile(const kvc_unit & u, const int h, const k
             const int idx = pb * 128 + tid;
             const int n = idx % DV, kq = idx / DV;
             const int k = k0 + 4 * kq;
-#pragma unroll
             if (VT) {
                 uint32_t w[VT == 3 ? 5 : 3] = {};
+#pragma unroll
                 for (int e = 0; e < 4; e++) {
                     if (!FULL && k + e >= C) continue;          // zero scale (and minimum): value 0
                     vq_raw<VT, DV>(u.Vq + (long long)(k + e) * P.v_rb, h, n, e, w);
