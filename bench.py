@@ -376,7 +376,7 @@ def run_kvc(args, cfg, name):
     cs = shard.auto_chunk(T, cfg["ratio"])
     params = abi.make_params(fns, target_ratio=cfg["ratio"], chunk_size=cs)
     gather = not replicas and world > 1
-    peer = gather and args.gather == "peer"
+    peer = gather and args.gather in ("peer", "peer-copy")
     if replicas:
         plan = [shard.partition(L, T, cfg["ratio"], 1)[0] for _ in range(world)]
     else:
@@ -386,7 +386,8 @@ def run_kvc(args, cfg, name):
     krb, vrb = Kq[0].shape[1], Vq[0].shape[1]
     finals, g = None, None
     if peer:
-        g = shard.PeerGather(dist, fns, rank, world, plan, L, T, cfg["ratio"], H, krb, vrb, device)
+        g = shard.PeerGather(dist, fns, rank, world, plan, L, T, cfg["ratio"], H, krb, vrb, device,
+                             copy_rows=args.gather == "peer-copy")
         finals = g.finals
     job = shard.SliceJob(fns, plan[rank], Kq, Vq, Q, T, H, d, cfg["ktype"], cfg["vtype"], params,
                          out_ptrs=g.out_ptrs() if peer else None)
@@ -524,9 +525,11 @@ def run_kvc(args, cfg, name):
         elif world == 1:
             par = "one GPU"
         else:
-            how = ("writes into rank 0's result buffer over NVLink (CUDA IPC: requantisation kernels store K_out/V_out "
-                   "rows in place, one kernel places indices and beta), rank 0 weighted "
-                   f"{shard.root_weights(world, args.root_extra)[0]:.2f}x" if peer else "NCCL send/recv to rank 0")
+            rows = ("one copy-engine copy per slice and row array" if args.gather == "peer-copy"
+                    else "requantisation kernels store K_out/V_out rows in place")
+            how = (f"writes into rank 0's result buffer over NVLink (CUDA IPC: {rows}, one kernel places indices "
+                   f"and beta), rank 0 weighted {shard.root_weights(world, args.root_extra)[0]:.2f}x"
+                   if peer else "NCCL send/recv to rank 0")
             par = (f"(layer, chunk) partition x{world}: {units_r} units per rank; merge of the kept indices, "
                    f"beta and requantised K/V rows into rank 0's whole-model arrays inside the timed region by "
                    f"{how}, each batched call's slices sent as it returns (C_v stays on the rank that computed it)")
@@ -565,8 +568,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--replicas", action="store_true",
                     help="N>1: every rank compacts its own model (weak scaling) instead of a share of one model")
-    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
-                    help="N>1 partition: merge by copy-engine puts into rank 0's buffer, or NCCL send/recv")
+    ap.add_argument("--gather", default="peer", choices=["peer", "peer-copy", "nccl"],
+                    help="N>1 partition: merge into rank 0's buffer by the requantisation kernels' stores "
+                         "(peer) or by one copy-engine copy per slice and row array (peer-copy), or NCCL send/recv")
     ap.add_argument("--root-extra", type=float, default=0.03,
                     help="peer merge: rank 0's share is 1 + extra*(N-1) times another rank's")
     ap.add_argument("--no-check", action="store_true",

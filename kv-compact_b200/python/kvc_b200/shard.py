@@ -358,10 +358,16 @@ class PeerGather:
     it returns. No receive is posted and nothing is copied twice. Construct
     and close() on every rank together (collective)."""
 
-    def __init__(self, dist, fns, rank, world, plan, n_layers, T, ratio, H, k_row_bytes, v_row_bytes, device):
+    def __init__(self, dist, fns, rank, world, plan, n_layers, T, ratio, H, k_row_bytes, v_row_bytes, device,
+                 copy_rows=False):
         import ctypes
         import torch
         self.dist, self.lib, self.rank, self.world, self.plan = dist, fns["_lib"], rank, world, plan
+        # copy_rows: K_out / V_out are requantised into the rank's own buffers
+        # and each slice's two row arrays go to rank 0 as one copy-engine copy
+        # each (out_ptrs() then gives None), instead of the requantisation
+        # kernels storing them over NVLink
+        self.copy_rows = copy_rows
         self.T, self.ratio, self.H, self.krb, self.vrb = T, ratio, H, k_row_bytes, v_row_bytes
         self.device = device
         self.layout, self.nbytes = result_layout(n_layers, T, ratio, H, k_row_bytes, v_row_bytes)
@@ -408,6 +414,8 @@ class PeerGather:
     def out_ptrs(self):
         """Per slice of this rank, the addresses of its K_out / V_out rows in
         rank 0's result buffer (put_ops' destinations)."""
+        if self.copy_rows:
+            return None
         return [(d[4], d[5]) for d in self.dst]
 
     def send(self, idx, outs):
@@ -421,6 +429,12 @@ class PeerGather:
                                           sel_dst, beta_dst, self.t, st)
             if rc != 0:
                 raise RuntimeError(f"kvc_place_slice failed: {rc}")
+            if self.copy_rows:
+                for dst, src, nb in ((self.dst[i][4], outs[i]["kout"], kept * self.krb),
+                                     (self.dst[i][5], outs[i]["vout"], kept * self.vrb)):
+                    rc = self.lib.kvc_copy_async(dst, src.data_ptr(), nb, st)
+                    if rc != 0:
+                        raise RuntimeError(f"peer copy failed: {rc}")
 
     def finish(self, outs):
         self.dist.all_reduce(self.flag)          # after this rank's copies, on every rank
